@@ -1,0 +1,123 @@
+/*
+ * Prepared dynamic W8A8 linear on one CUDA device.
+ *
+ * The reference exposes this operator only in Python:
+ * PreparedW8A8Linear (src/qpu_xla/models/tinyllama/quantization.py:57-878),
+ * whose QPU dispatch goes through the raw program ABI
+ * (integrations/llama_cpp/include/qpu_llama_runtime.h:114-131 with the
+ * tiled-w8a8-gemm[-dequantize] and w8a8-gemv programs). This header is the
+ * C-ABI form of that plan, with the same contract:
+ *   y[m, n] = ((float)acc[m, n] * s_a[m]) * s_w[n]   (+ bias[n] when given)
+ *   acc[m, n] = sum_k q_a[m, k] * q_w[n, k]          exact int32
+ *   s_a[m] = max(max_k |x[m, k]| / 127, 1/127),  q_a = clip(rint(x / s_a), -127, 127)
+ * (quantization.py:156-171 and :1065-1075; bias after dequantization as in
+ * src/qpu_xla/models/smolvla/accelerated.py:260-261).
+ *
+ * The plan owns the resident int8 weights, scales, bias and the activation
+ * scratch (int8 rows padded to a multiple of 16 bytes plus fp32 row scales),
+ * sized for max_batch rows. One invocation may be in flight per plan
+ * (quantization.py:290-291); a second concurrent execute returns
+ * QPUCUDA_INTERNAL_ERROR.
+ *
+ * Output-channel (N) sharding: resident_output_start/count select a disjoint
+ * column range of the weight; the destination then receives only those
+ * columns (the multi-GPU N-split, and the reference's execute_hybrid output
+ * split, quantization.py:350-514).
+ */
+#ifndef QPUCUDA_W8A8_H
+#define QPUCUDA_W8A8_H
+
+#include "qpucuda_runtime.h"
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+typedef struct qpucuda_w8a8_linear qpucuda_w8a8_linear;
+
+typedef enum qpucuda_memory {
+    QPUCUDA_MEMORY_HOST = 0,
+    QPUCUDA_MEMORY_DEVICE = 1,
+} qpucuda_memory;
+
+/* Weight descriptor; the fields are QuantizedMatrixInt8 (quantization.py:31-54)
+ * plus an optional bias. Pointers are host or device memory per `memory`;
+ * they are only read during prepare (copied into the plan). */
+typedef struct qpucuda_w8a8_linear_desc {
+    const int8_t *weight_values;   /* [output_features][input_features] row-major */
+    const float *weight_scales;    /* [output_features], finite and > 0 */
+    const float *bias;             /* [output_features] or NULL */
+    uint32_t input_features;       /* K */
+    uint32_t output_features;      /* N of the full matrix */
+    uint32_t max_batch;            /* maximum M per call, > 0 */
+    uint32_t resident_output_start;  /* first resident output column */
+    uint32_t resident_output_count;  /* 0 = all columns from resident_output_start */
+    qpucuda_memory memory;
+} qpucuda_w8a8_linear_desc;
+
+/* Host-buffer execution, synchronous (bounded wait). source: host fp32
+ * [rows][input_features]; destination: host fp32 [rows][resident count]. */
+typedef struct qpucuda_w8a8_execution {
+    const float *source;
+    size_t source_size;           /* bytes available at source */
+    float *destination;
+    size_t destination_size;      /* bytes available at destination */
+    uint32_t rows;                /* 1..max_batch */
+} qpucuda_w8a8_execution;
+
+qpucuda_status qpucuda_w8a8_linear_prepare(
+    qpucuda_context *context,
+    const qpucuda_w8a8_linear_desc *desc,
+    qpucuda_w8a8_linear **result);
+void qpucuda_w8a8_linear_destroy(qpucuda_w8a8_linear *linear);
+size_t qpucuda_w8a8_linear_resident_bytes(const qpucuda_w8a8_linear *linear);
+/* Host buffers in and out; copies through pinned staging; on a failed wait
+ * the destination is left untouched and the context is poisoned. */
+qpucuda_status qpucuda_w8a8_linear_execute(qpucuda_w8a8_linear *linear, const qpucuda_w8a8_execution *execution);
+
+/* Device pointers, asynchronous on the context stream:
+ * quantize source rows into the plan scratch, GEMM (tcgen05 kind::i8 for
+ * rows > 8, int8 dot-product GEMV otherwise), fused dequant (+ bias) into
+ * destination[row * destination_stride + column], columns 0..resident count-1. */
+qpucuda_status qpucuda_w8a8_linear_execute_device(
+    qpucuda_w8a8_linear *linear,
+    const float *source,
+    size_t source_stride,
+    uint32_t rows,
+    float *destination,
+    size_t destination_stride);
+
+/* Same, for activations already quantized by the caller (the reference's
+ * execute_prepared, quantization.py:325-348): quantized int8 rows with row
+ * stride quantized_stride bytes (multiple of 16) and fp32 row scales. */
+qpucuda_status qpucuda_w8a8_linear_execute_prepared_device(
+    qpucuda_w8a8_linear *linear,
+    const int8_t *quantized,
+    size_t quantized_stride,
+    const float *row_scales,
+    uint32_t rows,
+    float *destination,
+    size_t destination_stride);
+
+/* Read back the plan scratch after an execute (device pointers, valid until
+ * the next call): int8 activations [max_batch][padded K] and fp32 row scales. */
+qpucuda_status qpucuda_w8a8_linear_scratch(
+    const qpucuda_w8a8_linear *linear,
+    const int8_t **quantized,
+    size_t *quantized_stride,
+    const float **row_scales);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#ifdef __cplusplus
+}
+#endif
+
+#endif

@@ -1,0 +1,322 @@
+// Prepared W8A8 linear (include/qpucuda_w8a8.h): the C-ABI form of
+// PreparedW8A8Linear (src/qpu_xla/models/tinyllama/quantization.py:57-878).
+//
+// Per call: quantize the fp32 rows into the plan's int8 scratch (quantization.py:156-171),
+// then either the int8 GEMV (rows <= 8; the reference's batch == 1 GEMV choice,
+// :184) or the tcgen05 GEMM, with the dequant (+bias) epilogue fused
+// (gemm_int8.py:166-184). Weight rows are padded with zeros to a multiple of 16
+// bytes of K, as the reference pads its packed operands (quantization.py:85-87).
+#include <cfloat>
+#include <climits>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+
+#include "qpucuda_internal.h"
+#include "qpucuda_w8a8.h"
+
+using namespace qpucuda;
+
+struct qpucuda_w8a8_linear {
+    qpucuda_context *context = nullptr;
+    uint32_t k = 0;        // input features
+    uint32_t k_pad = 0;    // K rounded up to 16
+    uint32_t columns = 0;  // resident output columns
+    uint32_t max_batch = 0;
+    bool has_bias = false;
+    int8_t *d_weight = nullptr;        // [columns][k_pad]
+    float *d_weight_scales = nullptr;  // [columns]
+    float *d_bias = nullptr;           // [columns] or null
+    int8_t *d_quantized = nullptr;     // scratch [max_batch][k_pad]
+    float *d_row_scales = nullptr;     // scratch [max_batch]
+    CUtensorMap map_weight;
+    CUtensorMap map_quantized;
+    bool maps_ready = false;
+    // Host-buffer path: device source/output and pinned output staging, allocated on first use.
+    float *h_destination = nullptr;
+    float *d_source = nullptr;
+    float *d_destination = nullptr;
+    size_t resident_bytes = 0;
+    bool busy = false;
+    std::mutex mutex;
+};
+
+namespace {
+
+constexpr uint32_t kGemvMaxRows = 8;
+
+bool accumulation_fits(uint32_t k) { return static_cast<uint64_t>(k) * 127u * 127u <= static_cast<uint64_t>(INT32_MAX); }
+
+void free_linear(qpucuda_w8a8_linear *linear) {
+    DeviceGuard guard(linear->context->device);
+    cudaFree(linear->d_weight);
+    cudaFree(linear->d_weight_scales);
+    cudaFree(linear->d_bias);
+    cudaFree(linear->d_quantized);
+    cudaFree(linear->d_row_scales);
+    cudaFree(linear->d_source);
+    cudaFree(linear->d_destination);
+    cudaFreeHost(linear->h_destination);
+    (void)cudaGetLastError();
+    delete linear;
+}
+
+// Enqueue quantize + GEMM/GEMV + epilogue for `rows` rows already resident on the device.
+qpucuda_status enqueue(qpucuda_w8a8_linear *linear, const float *source, size_t source_stride,
+                       const int8_t *quantized, size_t quantized_stride, const float *row_scales, uint32_t rows,
+                       float *destination, size_t destination_stride) {
+    qpucuda_context *context = linear->context;
+    cudaStream_t stream = context->stream;
+    if (source != nullptr) {
+        const cudaError_t error = launch_quantize_rows_int8(source, source_stride, rows, linear->k, linear->k_pad,
+                                                            linear->d_quantized, linear->k_pad, linear->d_row_scales,
+                                                            stream);
+        if (error != cudaSuccess) return cuda_fail(context, error, "quantize activations");
+        quantized = linear->d_quantized;
+        quantized_stride = linear->k_pad;
+        row_scales = linear->d_row_scales;
+    }
+    GemmEpilogue epilogue;
+    epilogue.mode = linear->has_bias ? EpilogueMode::kDequantizeBias : EpilogueMode::kDequantize;
+    epilogue.row_scales = row_scales;
+    epilogue.col_scales = linear->d_weight_scales;
+    epilogue.bias = linear->d_bias;
+    epilogue.out = destination;
+    epilogue.out_stride = destination_stride;
+    cudaError_t error;
+    if (rows <= kGemvMaxRows) {
+        error = launch_w8a8_gemv(quantized, quantized_stride, linear->d_weight, linear->k_pad, rows, linear->columns,
+                                 linear->k_pad, epilogue, context->sm_count, stream);
+    } else if (quantized == linear->d_quantized && linear->maps_ready) {
+        error = launch_w8a8_gemm_sm100(&linear->map_quantized, &linear->map_weight, rows, linear->columns,
+                                       linear->k_pad, epilogue, context->d_error, context->sm_count, stream);
+    } else {
+        error = run_w8a8_gemm(quantized, quantized_stride, linear->d_weight, linear->k_pad, rows, linear->columns,
+                              linear->k_pad, epilogue, context->d_error, context->sm_count, stream);
+    }
+    if (error == cudaErrorInvalidValue) return cuda_fail(context, error, "W8A8 GEMM launch", QPUCUDA_INVALID_ARGUMENT);
+    if (error != cudaSuccess) return cuda_fail(context, error, "W8A8 GEMM launch");
+    return QPUCUDA_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+qpucuda_status qpucuda_w8a8_linear_prepare(qpucuda_context *context, const qpucuda_w8a8_linear_desc *desc,
+                                           qpucuda_w8a8_linear **result) {
+    if (context == nullptr || desc == nullptr || result == nullptr) return QPUCUDA_INVALID_ARGUMENT;
+    *result = nullptr;
+    const uint32_t count = desc->resident_output_count != 0 ? desc->resident_output_count
+                                                             : (desc->output_features > desc->resident_output_start
+                                                                    ? desc->output_features - desc->resident_output_start
+                                                                    : 0);
+    if (desc->weight_values == nullptr || desc->weight_scales == nullptr || desc->input_features == 0 ||
+        desc->output_features == 0 || desc->max_batch == 0 || count == 0 ||
+        desc->resident_output_start > desc->output_features ||
+        count > desc->output_features - desc->resident_output_start ||
+        (desc->memory != QPUCUDA_MEMORY_HOST && desc->memory != QPUCUDA_MEMORY_DEVICE)) {
+        return fail(context, QPUCUDA_INVALID_ARGUMENT, "w8a8 prepare: invalid weight descriptor");
+    }
+    if (!accumulation_fits(desc->input_features)) {
+        // quantization.py:90-91
+        return fail(context, QPUCUDA_INVALID_ARGUMENT, "prepared W8A8 linear accumulation can overflow int32");
+    }
+    const size_t start = desc->resident_output_start;
+    if (desc->memory == QPUCUDA_MEMORY_HOST) {
+        // QuantizedMatrixInt8 invariant (quantization.py:45-46): finite, positive scales.
+        for (uint32_t i = 0; i < count; ++i) {
+            const float s = desc->weight_scales[start + i];
+            if (!std::isfinite(s) || s <= 0.0f) {
+                return fail(context, QPUCUDA_INVALID_ARGUMENT, "quantized matrix scales must be finite and positive");
+            }
+        }
+    }
+    std::lock_guard<std::mutex> lock(context->mutex);
+    if (context->poisoned) return fail(context, QPUCUDA_IO_FAILED, "CUDA context is poisoned after a wait failure");
+    if ((context->failure_mask & QPUCUDA_FAIL_ALLOCATION) != 0) {
+        return fail(context, QPUCUDA_ALLOCATION_FAILED, "injected device allocation failure");
+    }
+    qpucuda_w8a8_linear *linear = new (std::nothrow) qpucuda_w8a8_linear();
+    if (linear == nullptr) return QPUCUDA_ALLOCATION_FAILED;
+    linear->context = context;
+    linear->k = desc->input_features;
+    linear->k_pad = (desc->input_features + 15u) & ~15u;
+    linear->columns = count;
+    linear->max_batch = desc->max_batch;
+    linear->has_bias = desc->bias != nullptr;
+    DeviceGuard guard(context->device);
+    const size_t weight_bytes = static_cast<size_t>(count) * linear->k_pad;
+    const size_t scratch_bytes = static_cast<size_t>(desc->max_batch) * linear->k_pad;
+    cudaError_t error = cudaMalloc(reinterpret_cast<void **>(&linear->d_weight), weight_bytes);
+    if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_weight_scales), count * sizeof(float));
+    if (error == cudaSuccess && linear->has_bias)
+        error = cudaMalloc(reinterpret_cast<void **>(&linear->d_bias), count * sizeof(float));
+    if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_quantized), scratch_bytes);
+    if (error == cudaSuccess)
+        error = cudaMalloc(reinterpret_cast<void **>(&linear->d_row_scales), desc->max_batch * sizeof(float));
+    if (error != cudaSuccess) {
+        free_linear(linear);
+        return cuda_fail(context, error, "allocate W8A8 plan", QPUCUDA_ALLOCATION_FAILED);
+    }
+    const cudaMemcpyKind kind = desc->memory == QPUCUDA_MEMORY_HOST ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice;
+    cudaStream_t stream = context->stream;
+    error = cudaMemsetAsync(linear->d_weight, 0, weight_bytes, stream);
+    if (error == cudaSuccess) error = cudaMemsetAsync(linear->d_quantized, 0, scratch_bytes, stream);
+    if (error == cudaSuccess)
+        error = cudaMemcpy2DAsync(linear->d_weight, linear->k_pad, desc->weight_values + start * desc->input_features,
+                                  desc->input_features, desc->input_features, count, kind, stream);
+    if (error == cudaSuccess)
+        error = cudaMemcpyAsync(linear->d_weight_scales, desc->weight_scales + start, count * sizeof(float), kind, stream);
+    if (error == cudaSuccess && linear->has_bias)
+        error = cudaMemcpyAsync(linear->d_bias, desc->bias + start, count * sizeof(float), kind, stream);
+    if (error != cudaSuccess) {
+        free_linear(linear);
+        return cuda_fail(context, error, "copy W8A8 weights", QPUCUDA_IO_FAILED);
+    }
+    const qpucuda_status waited = wait_stream(context);
+    if (waited != QPUCUDA_OK) {
+        free_linear(linear);
+        return waited;
+    }
+    // Tensor maps for the resident weight and the activation scratch (sm_100 only).
+    if (context->cc_major == 10 && context->cc_minor == 0) {
+        linear->maps_ready =
+            encode_tensor_map_2d_u8(&linear->map_weight, linear->d_weight, linear->k_pad, count, linear->k_pad,
+                                    kGemmBlockK, kGemmBlockN) &&
+            encode_tensor_map_2d_u8(&linear->map_quantized, linear->d_quantized, linear->k_pad, desc->max_batch,
+                                    linear->k_pad, kGemmBlockK, kGemmBlockM);
+    }
+    linear->resident_bytes = weight_bytes + count * sizeof(float) * (linear->has_bias ? 2 : 1) + scratch_bytes +
+                             desc->max_batch * sizeof(float);
+    *result = linear;
+    return QPUCUDA_OK;
+}
+
+void qpucuda_w8a8_linear_destroy(qpucuda_w8a8_linear *linear) {
+    if (linear == nullptr) return;
+    free_linear(linear);
+}
+
+size_t qpucuda_w8a8_linear_resident_bytes(const qpucuda_w8a8_linear *linear) {
+    return linear != nullptr ? linear->resident_bytes : 0;
+}
+
+qpucuda_status qpucuda_w8a8_linear_execute_device(qpucuda_w8a8_linear *linear, const float *source,
+                                                  size_t source_stride, uint32_t rows, float *destination,
+                                                  size_t destination_stride) {
+    if (linear == nullptr) return QPUCUDA_INVALID_ARGUMENT;
+    qpucuda_context *context = linear->context;
+    if (source == nullptr || destination == nullptr || rows == 0 || rows > linear->max_batch ||
+        source_stride < linear->k || destination_stride < linear->columns) {
+        return fail(context, QPUCUDA_INVALID_ARGUMENT, "prepared W8A8 linear source exceeds the plan shape");
+    }
+    if (rows > kGemvMaxRows && !(context->cc_major == 10 && context->cc_minor == 0)) {
+        return fail(context, QPUCUDA_CAPABILITY_MISSING, "the tcgen05 int8 GEMM needs an sm_100 device");
+    }
+    std::lock_guard<std::mutex> lock(context->mutex);
+    qpucuda_status status = begin_submit(context);
+    if (status != QPUCUDA_OK) return status;
+    DeviceGuard guard(context->device);
+    return enqueue(linear, source, source_stride, nullptr, 0, nullptr, rows, destination, destination_stride);
+}
+
+qpucuda_status qpucuda_w8a8_linear_execute_prepared_device(qpucuda_w8a8_linear *linear, const int8_t *quantized,
+                                                           size_t quantized_stride, const float *row_scales,
+                                                           uint32_t rows, float *destination,
+                                                           size_t destination_stride) {
+    if (linear == nullptr) return QPUCUDA_INVALID_ARGUMENT;
+    qpucuda_context *context = linear->context;
+    if (quantized == nullptr || row_scales == nullptr || destination == nullptr || rows == 0 ||
+        rows > linear->max_batch || quantized_stride < linear->k_pad || quantized_stride % 16 != 0 ||
+        (reinterpret_cast<uintptr_t>(quantized) & 15u) != 0 || destination_stride < linear->columns) {
+        return fail(context, QPUCUDA_INVALID_ARGUMENT,
+                    "prepared W8A8 linear: quantized rows need a 16-byte aligned stride >= the padded K");
+    }
+    if (rows > kGemvMaxRows && !(context->cc_major == 10 && context->cc_minor == 0)) {
+        return fail(context, QPUCUDA_CAPABILITY_MISSING, "the tcgen05 int8 GEMM needs an sm_100 device");
+    }
+    std::lock_guard<std::mutex> lock(context->mutex);
+    qpucuda_status status = begin_submit(context);
+    if (status != QPUCUDA_OK) return status;
+    DeviceGuard guard(context->device);
+    return enqueue(linear, nullptr, 0, quantized, quantized_stride, row_scales, rows, destination, destination_stride);
+}
+
+qpucuda_status qpucuda_w8a8_linear_execute(qpucuda_w8a8_linear *linear, const qpucuda_w8a8_execution *execution) {
+    if (linear == nullptr || execution == nullptr) return QPUCUDA_INVALID_ARGUMENT;
+    qpucuda_context *context = linear->context;
+    const uint32_t rows = execution->rows;
+    size_t source_bytes = 0, destination_bytes = 0;
+    if (execution->source == nullptr || execution->destination == nullptr || rows == 0 || rows > linear->max_batch ||
+        !multiply_size(static_cast<size_t>(rows) * linear->k, sizeof(float), &source_bytes) ||
+        !multiply_size(static_cast<size_t>(rows) * linear->columns, sizeof(float), &destination_bytes) ||
+        execution->source_size < source_bytes || execution->destination_size < destination_bytes) {
+        return fail(context, QPUCUDA_INVALID_ARGUMENT, "prepared W8A8 linear source exceeds the plan shape");
+    }
+    if (rows > kGemvMaxRows && !(context->cc_major == 10 && context->cc_minor == 0)) {
+        return fail(context, QPUCUDA_CAPABILITY_MISSING, "the tcgen05 int8 GEMM needs an sm_100 device");
+    }
+    {
+        std::lock_guard<std::mutex> guard(linear->mutex);
+        if (linear->busy) {
+            return fail(context, QPUCUDA_INTERNAL_ERROR,
+                        "prepared W8A8 linear plan already has an in-flight invocation");
+        }
+        linear->busy = true;
+    }
+    std::lock_guard<std::mutex> lock(context->mutex);
+    DeviceGuard device_guard(context->device);
+    auto release = [linear](qpucuda_status status) {
+        std::lock_guard<std::mutex> guard(linear->mutex);
+        linear->busy = false;
+        return status;
+    };
+    qpucuda_status status = begin_submit(context);
+    if (status != QPUCUDA_OK) return release(status);
+    const size_t max_source = static_cast<size_t>(linear->max_batch) * linear->k * sizeof(float);
+    const size_t max_destination = static_cast<size_t>(linear->max_batch) * linear->columns * sizeof(float);
+    if (linear->d_source == nullptr) {
+        if ((context->failure_mask & QPUCUDA_FAIL_ALLOCATION) != 0 ||
+            cudaMallocHost(reinterpret_cast<void **>(&linear->h_destination), max_destination) != cudaSuccess ||
+            cudaMalloc(reinterpret_cast<void **>(&linear->d_source), max_source) != cudaSuccess ||
+            cudaMalloc(reinterpret_cast<void **>(&linear->d_destination), max_destination) != cudaSuccess) {
+            (void)cudaGetLastError();
+            cudaFreeHost(linear->h_destination);
+            cudaFree(linear->d_source);
+            cudaFree(linear->d_destination);
+            linear->h_destination = nullptr;
+            linear->d_source = linear->d_destination = nullptr;
+            return release(fail(context, QPUCUDA_ALLOCATION_FAILED, "allocate W8A8 host staging"));
+        }
+    }
+    // The source is copied straight from the caller's buffer (a DMA when it is pinned). The
+    // result lands in plan-owned pinned staging first and reaches the caller only after a
+    // successful wait, so a failed or timed-out wait never writes the caller's destination.
+    cudaError_t error =
+        cudaMemcpyAsync(linear->d_source, execution->source, source_bytes, cudaMemcpyHostToDevice, context->stream);
+    if (error != cudaSuccess) return release(cuda_fail(context, error, "copy W8A8 source"));
+    status = enqueue(linear, linear->d_source, linear->k, nullptr, 0, nullptr, rows, linear->d_destination,
+                     linear->columns);
+    if (status != QPUCUDA_OK) return release(status);
+    error = cudaMemcpyAsync(linear->h_destination, linear->d_destination, destination_bytes, cudaMemcpyDeviceToHost,
+                            context->stream);
+    if (error != cudaSuccess) return release(cuda_fail(context, error, "copy W8A8 destination"));
+    status = wait_stream(context);
+    if (status == QPUCUDA_OK) parallel_memcpy(execution->destination, linear->h_destination, destination_bytes);
+    return release(status);
+}
+
+qpucuda_status qpucuda_w8a8_linear_scratch(const qpucuda_w8a8_linear *linear, const int8_t **quantized,
+                                           size_t *quantized_stride, const float **row_scales) {
+    if (linear == nullptr || quantized == nullptr || quantized_stride == nullptr || row_scales == nullptr) {
+        return QPUCUDA_INVALID_ARGUMENT;
+    }
+    *quantized = linear->d_quantized;
+    *quantized_stride = linear->k_pad;
+    *row_scales = linear->d_row_scales;
+    return QPUCUDA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,143 @@
+// Internal declarations shared by the qpucuda translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <mutex>
+
+#include "qpucuda_runtime.h"
+
+#ifndef QPUCUDA_VERSION
+#define QPUCUDA_VERSION "0.1.0"
+#endif
+
+struct qpucuda_context {
+    int device = 0;
+    uint64_t timeout_ns = 0;
+    uint32_t failure_mask = 0;
+    cudaStream_t stream = nullptr;      // stream work is issued on
+    cudaStream_t own_stream = nullptr;  // library-owned stream (always created)
+    cudaEvent_t done_event = nullptr;   // reused for bounded waits
+    bool poisoned = false;
+    int sm_count = 0;
+    int cc_major = 0;
+    int cc_minor = 0;
+    size_t l2_bytes = 0;
+    size_t global_bytes = 0;
+    char device_name[128] = {0};
+    // Device error word written by kernels whose bounded waits expire, and a
+    // pinned host mirror read back after synchronous waits.
+    unsigned int *d_error = nullptr;
+    unsigned int *h_error = nullptr;
+    std::mutex mutex;
+    char last_error[256] = {0};
+};
+
+namespace qpucuda {
+
+// Kernel-side error codes stored in qpucuda_context::d_error.
+enum KernelError : unsigned int {
+    kKernelOk = 0,
+    kKernelWaitTimeout = 1,  // an mbarrier wait exceeded its bound
+};
+
+// Upper bound for any single in-kernel barrier wait, in nanoseconds.
+constexpr unsigned long long kKernelWaitLimitNs = 1000000000ull;
+
+qpucuda_status fail(qpucuda_context *context, qpucuda_status status, const char *format, ...);
+qpucuda_status cuda_fail(qpucuda_context *context, cudaError_t error, const char *operation,
+                         qpucuda_status status = QPUCUDA_SUBMISSION_FAILED);
+// Rejects work on a poisoned context and applies QPUCUDA_FAIL_SUBMISSION.
+qpucuda_status begin_submit(qpucuda_context *context);
+// Bounded wait on the context stream (event poll against timeout_ns), then
+// applies QPUCUDA_FAIL_WAIT and checks the kernels' error word. A failure
+// poisons the context.
+qpucuda_status wait_stream(qpucuda_context *context);
+// Current-device guard.
+class DeviceGuard {
+  public:
+    explicit DeviceGuard(int device);
+    ~DeviceGuard();
+
+  private:
+    int previous_ = -1;
+    bool changed_ = false;
+};
+
+uint64_t monotonic_ns();
+// Host memcpy split over several threads for large copies (pinned staging -> caller memory).
+void parallel_memcpy(void *destination, const void *source, size_t bytes);
+bool multiply_size(size_t left, size_t right, size_t *result);
+bool valid_range(size_t total, size_t offset, size_t size);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the library
+// links only the static CUDA runtime, so it loads on machines without a driver).
+bool encode_tensor_map_2d_u8(CUtensorMap *map, const void *base, uint64_t inner_bytes, uint64_t rows,
+                             uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows);
+
+// ---- kernel launchers (one per .cu file) -------------------------------------------------
+
+cudaError_t launch_quantize_rows_int8(const float *x, size_t x_stride, uint32_t rows, uint32_t cols,
+                                      uint32_t padded_cols, int8_t *q, size_t q_stride, float *scales,
+                                      cudaStream_t stream);
+cudaError_t launch_quantize_q8_0(const float *x, size_t x_stride, uint32_t rows, uint32_t cols, uint8_t *blocks,
+                                 cudaStream_t stream);
+cudaError_t launch_quantize_q4_0(const float *x, size_t x_stride, uint32_t rows, uint32_t cols, uint8_t *blocks,
+                                 cudaStream_t stream);
+
+enum class EpilogueMode : int { kStoreS32 = 0, kDequantize = 1, kDequantizeBias = 2 };
+
+struct GemmEpilogue {
+    EpilogueMode mode = EpilogueMode::kDequantize;
+    const float *row_scales = nullptr;
+    const float *col_scales = nullptr;
+    const float *bias = nullptr;
+    void *out = nullptr;  // float* or int32_t*
+    size_t out_stride = 0;  // elements
+};
+
+// tcgen05 int8 GEMM: a [m][k] and w [n][k] int8, K-major, 16-byte aligned rows.
+cudaError_t launch_w8a8_gemm_sm100(const CUtensorMap *map_a, const CUtensorMap *map_w, uint32_t m, uint32_t n,
+                                   uint32_t k, const GemmEpilogue &epilogue, unsigned int *error_word,
+                                   int sm_count, cudaStream_t stream);
+// Builds both tensor maps and launches; returns cudaErrorInvalidValue when a map cannot be encoded.
+cudaError_t run_w8a8_gemm(const int8_t *a, size_t a_stride, const int8_t *w, size_t w_stride, uint32_t m,
+                          uint32_t n, uint32_t k, const GemmEpilogue &epilogue, unsigned int *error_word,
+                          int sm_count, cudaStream_t stream);
+constexpr uint32_t kGemmBlockN = 256;  // box rows of the weight tensor map
+constexpr uint32_t kGemmBlockM = 128;
+constexpr uint32_t kGemmBlockK = 128;  // bytes of K per pipeline stage
+
+cudaError_t launch_w8a8_gemv(const int8_t *a, size_t a_stride, const int8_t *w, size_t w_stride, uint32_t m,
+                             uint32_t n, uint32_t k, const GemmEpilogue &epilogue, int sm_count,
+                             cudaStream_t stream);
+cudaError_t launch_w8a8_dequantize(const int32_t *acc, size_t acc_stride, uint32_t m, uint32_t n,
+                                   const GemmEpilogue &epilogue, cudaStream_t stream);
+
+// Q4_0 x Q8_0 over the prepared (repacked) weight layout.
+struct Q40Weights {
+    const uint8_t *nibbles = nullptr;  // [columns][blocks][16]
+    const uint16_t *scales = nullptr;  // [columns][blocks] fp16 bits
+    uint32_t columns = 0;
+    uint32_t blocks = 0;
+};
+// activation: native Q8_0 rows [rows][blocks][34] (interleave 0) or CPU_REPACK
+// block_q8_0x4 groups (interleave 4/8). Writes destination[r * stride + out_col0 + j]
+// for weight columns col0 + j, j < count.
+cudaError_t launch_q4_0_q8_0_gemv(const Q40Weights &weights, const uint8_t *activation, uint32_t rows,
+                                  uint32_t interleave, float *destination, size_t destination_stride,
+                                  uint32_t col0, uint32_t out_col0, uint32_t count, int sm_count,
+                                  cudaStream_t stream);
+// Native 18-byte blocks [columns][blocks][18] -> prepared layout.
+cudaError_t launch_q4_0_repack(const uint8_t *native, uint32_t columns, uint32_t blocks, uint8_t *nibbles,
+                               uint16_t *scales, cudaStream_t stream);
+// Reads native blocks directly (no prepared layout), for the single-kernel entry point.
+cudaError_t launch_q4_0_q8_0_gemv_native(const uint8_t *activation, uint32_t rows, uint32_t blocks,
+                                         const uint8_t *weight, float *destination, size_t destination_stride,
+                                         uint32_t col0, uint32_t out_col0, uint32_t count, int sm_count,
+                                         cudaStream_t stream);
+
+}  // namespace qpucuda

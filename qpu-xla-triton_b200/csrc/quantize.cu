@@ -1,0 +1,267 @@
+// Quantizer kernels of the quantized-linear path (all HBM-bound, no tensor cores).
+//
+//  * quantize_rows_int8: per-row symmetric int8 (src/qpu_xla/models/tinyllama/quantization.py:156-171,
+//    :1065-1071 for activations, :1085-1092 for weights). One CTA per row; the row is read once with
+//    128-bit loads into registers, reduced to max|x| with warp shuffles, then quantized from registers.
+//    Bit-exact with NumPy: IEEE division (__fdiv_rn, never fast-math), round-half-even, clamp to +-127.
+//  * quantize_q8_0: fp32 -> native block_q8_0 (examples/benchmark_llama_cpp_qpu_persistent_q4.py:42-54).
+//  * quantize_q4_0: fp32 -> native block_q4_0, ggml's published quantize_row_q4_0_ref.
+//  * q4_0_repack: native 18-byte Q4_0 blocks -> the prepared layout (16-byte nibble blocks + fp16 scales).
+#include <cuda_fp16.h>
+
+#include "qpucuda_internal.h"
+
+namespace qpucuda {
+namespace {
+
+// np.float32(1.0 / 127.0), the scale floor of every per-row quantizer (quantization.py:165).
+__device__ __forceinline__ float scale_floor() { return __uint_as_float(0x3c010204u); }
+
+__device__ __forceinline__ int quantize_value(float x, float scale) {
+    const int v = __float2int_rn(__fdiv_rn(x, scale));
+    return v < -127 ? -127 : (v > 127 ? 127 : v);
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+    return (static_cast<uint32_t>(a) & 0xffu) | ((static_cast<uint32_t>(b) & 0xffu) << 8) |
+           ((static_cast<uint32_t>(c) & 0xffu) << 16) | ((static_cast<uint32_t>(d) & 0xffu) << 24);
+}
+
+__device__ __forceinline__ float4 load_stream(const float4 *p) {
+    float4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+template <int THREADS>
+__device__ __forceinline__ float block_max(float value, float *scratch) {
+#pragma unroll
+    for (int offset = 16; offset > 0; offset >>= 1) value = fmaxf(value, __shfl_xor_sync(0xffffffffu, value, offset));
+    constexpr int kWarps = THREADS / 32;
+    if constexpr (kWarps > 1) {
+        const int warp = threadIdx.x >> 5;
+        const int lane = threadIdx.x & 31;
+        __syncthreads();  // scratch reuse across rows
+        if (lane == 0) scratch[warp] = value;
+        __syncthreads();
+        value = lane < kWarps ? scratch[lane] : 0.0f;
+#pragma unroll
+        for (int offset = 16; offset > 0; offset >>= 1)
+            value = fmaxf(value, __shfl_xor_sync(0xffffffffu, value, offset));
+    }
+    return value;
+}
+
+// Vector path: cols % 4 == 0, 16-byte aligned rows; VEC float4 per thread cached in registers.
+template <int THREADS, int VEC>
+__global__ void __launch_bounds__(THREADS) quantize_rows_int8_vec(const float *__restrict__ x, size_t x_stride,
+                                                                  uint32_t rows, uint32_t cols, uint32_t padded_cols,
+                                                                  int8_t *__restrict__ q, size_t q_stride,
+                                                                  float *__restrict__ scales) {
+    __shared__ float scratch[32];
+    const uint32_t vectors = cols / 4;
+    for (uint32_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const float4 *source = reinterpret_cast<const float4 *>(x + static_cast<size_t>(row) * x_stride);
+        float4 cache[VEC];
+        float amax = 0.0f;
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+            const uint32_t index = threadIdx.x + v * THREADS;
+            if (index < vectors) {
+                cache[v] = load_stream(source + index);
+                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(cache[v].x), fabsf(cache[v].y)),
+                                         fmaxf(fabsf(cache[v].z), fabsf(cache[v].w))));
+            }
+        }
+        amax = block_max<THREADS>(amax, scratch);
+        const float scale = fmaxf(__fdiv_rn(amax, 127.0f), scale_floor());
+        uint32_t *destination = reinterpret_cast<uint32_t *>(q + static_cast<size_t>(row) * q_stride);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) {
+            const uint32_t index = threadIdx.x + v * THREADS;
+            if (index < vectors) {
+                destination[index] = pack4(quantize_value(cache[v].x, scale), quantize_value(cache[v].y, scale),
+                                           quantize_value(cache[v].z, scale), quantize_value(cache[v].w, scale));
+            }
+        }
+        int8_t *row_q = q + static_cast<size_t>(row) * q_stride;
+        for (uint32_t c = cols + threadIdx.x; c < padded_cols; c += THREADS) row_q[c] = 0;
+        if (threadIdx.x == 0) scales[row] = scale;
+    }
+}
+
+// Generic path: any alignment / column count; the second pass re-reads the row (an L2 hit).
+__global__ void __launch_bounds__(256) quantize_rows_int8_generic(const float *__restrict__ x, size_t x_stride,
+                                                                  uint32_t rows, uint32_t cols, uint32_t padded_cols,
+                                                                  int8_t *__restrict__ q, size_t q_stride,
+                                                                  float *__restrict__ scales) {
+    __shared__ float scratch[32];
+    for (uint32_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const float *source = x + static_cast<size_t>(row) * x_stride;
+        float amax = 0.0f;
+        for (uint32_t c = threadIdx.x; c < cols; c += 256) amax = fmaxf(amax, fabsf(source[c]));
+        amax = block_max<256>(amax, scratch);
+        const float scale = fmaxf(__fdiv_rn(amax, 127.0f), scale_floor());
+        int8_t *row_q = q + static_cast<size_t>(row) * q_stride;
+        for (uint32_t c = threadIdx.x; c < padded_cols; c += 256) {
+            row_q[c] = c < cols ? static_cast<int8_t>(quantize_value(source[c], scale)) : static_cast<int8_t>(0);
+        }
+        if (threadIdx.x == 0) scales[row] = scale;
+    }
+}
+
+template <int THREADS, int VEC>
+cudaError_t launch_vec(const float *x, size_t x_stride, uint32_t rows, uint32_t cols, uint32_t padded_cols, int8_t *q,
+                       size_t q_stride, float *scales, cudaStream_t stream) {
+    const uint32_t grid = rows < 65535u * 4u ? rows : 65535u * 4u;
+    quantize_rows_int8_vec<THREADS, VEC><<<grid, THREADS, 0, stream>>>(x, x_stride, rows, cols, padded_cols, q,
+                                                                        q_stride, scales);
+    return cudaGetLastError();
+}
+
+// ---- Q8_0 -------------------------------------------------------------------------------
+
+// One warp per 32-element block: d = amax / 127 (fp32), id = 1/d (0 when d == 0),
+// q = clip(rint(x * id), -127, 127), stored scale fp16(d) (round to nearest even).
+__global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float *__restrict__ x, size_t x_stride,
+                                                            uint32_t rows, uint32_t blocks_per_row,
+                                                            uint8_t *__restrict__ out) {
+    const uint32_t lane = threadIdx.x & 31;
+    const size_t total = static_cast<size_t>(rows) * blocks_per_row;
+    for (size_t block = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; block < total;
+         block += static_cast<size_t>(gridDim.x) * blockDim.x / 32) {
+        const size_t row = block / blocks_per_row;
+        const size_t column_block = block % blocks_per_row;
+        const float value = x[row * x_stride + column_block * 32 + lane];
+        float amax = fabsf(value);
+#pragma unroll
+        for (int offset = 16; offset > 0; offset >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, offset));
+        const float d = __fdiv_rn(amax, 127.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        int v = __float2int_rn(__fmul_rn(value, id));
+        v = v < -127 ? -127 : (v > 127 ? 127 : v);
+        uint8_t *destination = out + block * 34;
+        destination[2 + lane] = static_cast<uint8_t>(static_cast<int8_t>(v));
+        if (lane == 0) {
+            const unsigned short bits = __half_as_ushort(__float2half_rn(d));
+            destination[0] = static_cast<uint8_t>(bits & 0xffu);
+            destination[1] = static_cast<uint8_t>(bits >> 8);
+        }
+    }
+}
+
+// ---- Q4_0 -------------------------------------------------------------------------------
+
+// One warp per block. max = the signed value of largest magnitude, first index on ties
+// (ggml compares amax < |v| in index order); d = max / -8; id = 1/d (0 when d == 0);
+// code = min(15, trunc(x * id + 8.5)); byte j = code j | code j+16 << 4.
+__global__ void __launch_bounds__(256) quantize_q4_0_kernel(const float *__restrict__ x, size_t x_stride,
+                                                            uint32_t rows, uint32_t blocks_per_row,
+                                                            uint8_t *__restrict__ out) {
+    const uint32_t lane = threadIdx.x & 31;
+    const size_t total = static_cast<size_t>(rows) * blocks_per_row;
+    for (size_t block = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) / 32; block < total;
+         block += static_cast<size_t>(gridDim.x) * blockDim.x / 32) {
+        const size_t row = block / blocks_per_row;
+        const size_t column_block = block % blocks_per_row;
+        const float value = x[row * x_stride + column_block * 32 + lane];
+        float best_abs = fabsf(value);
+        uint32_t best_lane = lane;
+#pragma unroll
+        for (int offset = 16; offset > 0; offset >>= 1) {
+            const float other_abs = __shfl_xor_sync(0xffffffffu, best_abs, offset);
+            const uint32_t other_lane = __shfl_xor_sync(0xffffffffu, best_lane, offset);
+            if (other_abs > best_abs || (other_abs == best_abs && other_lane < best_lane)) {
+                best_abs = other_abs;
+                best_lane = other_lane;
+            }
+        }
+        const float maximum = __shfl_sync(0xffffffffu, value, best_lane);
+        const float d = __fdiv_rn(maximum, -8.0f);
+        const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+        int code = __float2int_rz(__fadd_rn(__fmul_rn(value, id), 8.5f));
+        code = code > 15 ? 15 : (code < 0 ? 0 : code);
+        const int high = __shfl_down_sync(0xffffffffu, code, 16);
+        uint8_t *destination = out + block * 18;
+        if (lane < 16) destination[2 + lane] = static_cast<uint8_t>(code | (high << 4));
+        if (lane == 0) {
+            const unsigned short bits = __half_as_ushort(__float2half_rn(d));
+            destination[0] = static_cast<uint8_t>(bits & 0xffu);
+            destination[1] = static_cast<uint8_t>(bits >> 8);
+        }
+    }
+}
+
+// Native [columns][blocks][18] -> nibbles [columns][blocks][16] + scales [columns][blocks].
+__global__ void __launch_bounds__(256) q4_0_repack_kernel(const uint8_t *__restrict__ native, size_t total_blocks,
+                                                          uint8_t *__restrict__ nibbles,
+                                                          uint16_t *__restrict__ scales) {
+    for (size_t block = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; block < total_blocks;
+         block += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const uint16_t *source = reinterpret_cast<const uint16_t *>(native + block * 18);  // blocks start on even bytes
+        uint32_t words[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            words[i] = static_cast<uint32_t>(source[1 + 2 * i]) | (static_cast<uint32_t>(source[2 + 2 * i]) << 16);
+        }
+        reinterpret_cast<uint4 *>(nibbles)[block] = make_uint4(words[0], words[1], words[2], words[3]);
+        scales[block] = source[0];
+    }
+}
+
+uint32_t grid_for(size_t work_items, uint32_t per_block) {
+    size_t grid = (work_items + per_block - 1) / per_block;
+    if (grid > 148u * 64u) grid = 148u * 64u;
+    return grid == 0 ? 1u : static_cast<uint32_t>(grid);
+}
+
+}  // namespace
+
+cudaError_t launch_quantize_rows_int8(const float *x, size_t x_stride, uint32_t rows, uint32_t cols,
+                                      uint32_t padded_cols, int8_t *q, size_t q_stride, float *scales,
+                                      cudaStream_t stream) {
+    if (rows == 0) return cudaSuccess;
+    const bool vector_ok = cols % 4 == 0 && x_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                           q_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(q) & 3u) == 0;
+    const uint32_t vectors = cols / 4;
+    if (vector_ok) {
+        // VEC = 8 float4 per thread; pick the smallest warp multiple of threads that covers the row.
+        if (vectors <= 32 * 8) return launch_vec<32, 8>(x, x_stride, rows, cols, padded_cols, q, q_stride, scales, stream);
+        if (vectors <= 64 * 8) return launch_vec<64, 8>(x, x_stride, rows, cols, padded_cols, q, q_stride, scales, stream);
+        if (vectors <= 128 * 8) return launch_vec<128, 8>(x, x_stride, rows, cols, padded_cols, q, q_stride, scales, stream);
+        if (vectors <= 256 * 8) return launch_vec<256, 8>(x, x_stride, rows, cols, padded_cols, q, q_stride, scales, stream);
+        if (vectors <= 512 * 8) return launch_vec<512, 8>(x, x_stride, rows, cols, padded_cols, q, q_stride, scales, stream);
+        if (vectors <= 1024 * 8) return launch_vec<1024, 8>(x, x_stride, rows, cols, padded_cols, q, q_stride, scales, stream);
+    }
+    const uint32_t grid = rows < 65535u * 4u ? rows : 65535u * 4u;
+    quantize_rows_int8_generic<<<grid, 256, 0, stream>>>(x, x_stride, rows, cols, padded_cols, q, q_stride, scales);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_q8_0(const float *x, size_t x_stride, uint32_t rows, uint32_t cols, uint8_t *blocks,
+                                 cudaStream_t stream) {
+    const size_t total = static_cast<size_t>(rows) * (cols / 32);
+    if (total == 0) return cudaSuccess;
+    quantize_q8_0_kernel<<<grid_for(total, 8), 256, 0, stream>>>(x, x_stride, rows, cols / 32, blocks);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_q4_0(const float *x, size_t x_stride, uint32_t rows, uint32_t cols, uint8_t *blocks,
+                                 cudaStream_t stream) {
+    const size_t total = static_cast<size_t>(rows) * (cols / 32);
+    if (total == 0) return cudaSuccess;
+    quantize_q4_0_kernel<<<grid_for(total, 8), 256, 0, stream>>>(x, x_stride, rows, cols / 32, blocks);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_q4_0_repack(const uint8_t *native, uint32_t columns, uint32_t blocks, uint8_t *nibbles,
+                               uint16_t *scales, cudaStream_t stream) {
+    const size_t total = static_cast<size_t>(columns) * blocks;
+    if (total == 0) return cudaSuccess;
+    q4_0_repack_kernel<<<grid_for(total, 256), 256, 0, stream>>>(native, total, nibbles, scales);
+    return cudaGetLastError();
+}
+
+}  // namespace qpucuda

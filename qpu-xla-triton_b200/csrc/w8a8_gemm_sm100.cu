@@ -1,0 +1,441 @@
+// W8A8 GEMM for sm_100a: int8 x int8 -> int32 on the 5th-generation tensor cores
+// (tcgen05.mma kind::i8), operands staged by TMA, accumulators in tensor memory,
+// fused dequant (+bias) epilogue.
+//
+// Replaces the reference's vc7.tiled_w8a8_gemm[_dequantize] QPU program
+// (src/qpu_xla/kernels/gemm_int8.py:43-204): same contract, acc[m, n] =
+// sum_k a[m, k] * w[n, k] exactly in int32, and, in the dequantize modes,
+// out = ((float)acc * row_scale[m]) * col_scale[n] (gemm_int8.py:166-184,
+// itof then two fmul in that order) with the bias added afterwards
+// (src/qpu_xla/models/smolvla/accelerated.py:260-261). The epilogue uses
+// __int2float_rn / __fmul_rn / __fadd_rn so nothing is contracted into an FMA
+// and the result is bit-identical to the reference's NumPy arithmetic.
+//
+// Structure: one persistent CTA per SM (192 threads, ~197 KB of shared memory,
+// so exactly one CTA per SM and its 512 TMEM columns are always free).
+//   warp 0      TMA producer: A tile 128 x 128 B and W tile 256 x 128 B per stage,
+//               4-stage ring, 128-byte swizzle, mbarrier complete_tx.
+//   warp 1      TMEM allocator and MMA issuer: 4 x tcgen05.mma (M=128, N=256, K=32)
+//               per stage; tcgen05.commit releases the stage and, after the last
+//               K block, signals the accumulator buffer full.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, dequantize,
+//               store; two accumulator buffers (2 x 256 columns) let the epilogue
+//               of tile i overlap the main loop of tile i+1.
+// Every mbarrier wait is bounded (globaltimer); on expiry the kernel records
+// kKernelWaitTimeout in the error word, drains its own copies and MMAs with
+// bounded waits, frees TMEM and returns. No multicast is used anywhere.
+#include "qpucuda_internal.h"
+
+namespace qpucuda {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // bytes (int8 elements) of K per stage = one 128-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int UMMA_K = 32;  // K per tcgen05.mma kind::i8
+constexpr int A_STAGE_BYTES = BM * BK;
+constexpr int B_STAGE_BYTES = BN * BK;
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int TMEM_COLS = 2 * BN;  // two s32 accumulators of BN columns
+constexpr int NUM_THREADS = 192;
+constexpr int EPILOGUE_THREADS = 128;
+
+static_assert(BN == kGemmBlockN && BM == kGemmBlockM && BK == kGemmBlockK, "tile constants must agree");
+
+// Instruction descriptor (kind::i8): D = s32 (bits 4-5 = 2), A = s8 (bits 7-9 = 1),
+// B = s8 (bits 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bits 17-22,
+// M >> 4 at bits 24-28.
+constexpr uint32_t kInstrDesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                                (static_cast<uint32_t>(BM >> 4) << 24);
+
+struct Control {
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t tmem_full[2];
+    uint64_t tmem_empty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    volatile int abort_flag;
+};
+
+constexpr size_t kSmemBytes = static_cast<size_t>(STAGES) * STAGE_BYTES + 1024 + sizeof(Control);
+
+struct GemmParams {
+    uint32_t m, n, k;
+    uint32_t num_kb;
+    uint32_t m_blocks, n_blocks;
+    int mode;
+    const float *row_scales;
+    const float *col_scales;
+    const float *bias;
+    void *out;
+    size_t out_stride;
+    unsigned int *error_word;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void *pointer) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(pointer));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+    uint64_t value;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(value));
+    return value;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait: false when the CTA was aborted or the wait exceeded kKernelWaitLimitNs
+// (the latter records the error and aborts the CTA).
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, Control *control,
+                                             unsigned int *error_word) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = globaltimer();
+    for (uint32_t spin = 1;; ++spin) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((spin & 63u) == 0) {
+            if (control->abort_flag != 0) return false;
+            if (globaltimer() - start > kKernelWaitLimitNs) {
+                control->abort_flag = 1;
+                atomicExch(error_word, static_cast<unsigned int>(kKernelWaitTimeout));
+                return false;
+            }
+        }
+    }
+}
+
+// Drain wait: bounded, ignores the abort flag (used only on the abort path).
+__device__ __forceinline__ void wait_drain(uint32_t bar, uint32_t parity) {
+    const uint64_t start = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - start > kKernelWaitLimitNs) return;
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t destination, const CUtensorMap *map, uint32_t bar, int x,
+                                            int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];" ::"r"(destination),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensor_map(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle
+// canonical layout: rows of 128 bytes, 8-row (1024-byte) swizzle atoms stacked
+// along M/N. start >> 4 at bits 0-13, LBO = 16 B (unused for swizzled K-major)
+// at 16-29, SBO = 1024 B at 32-45, descriptor version 1 at bit 46, layout
+// SWIZZLE_128B (2) at bits 61-63.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t address) {
+    uint64_t desc = static_cast<uint64_t>((address & 0x3FFFFu) >> 4);
+    desc |= static_cast<uint64_t>(1) << 16;
+    desc |= static_cast<uint64_t>(1024 >> 4) << 32;
+    desc |= static_cast<uint64_t>(1) << 46;
+    desc |= static_cast<uint64_t>(2) << 61;
+    return desc;
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(kInstrDesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_load_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float dequant(uint32_t bits, float row_scale, float col_scale) {
+    return __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(bits)), row_scale), col_scale);
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    w8a8_gemm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                           const GemmParams params) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *stage_a = smem;
+    uint8_t *stage_b = smem + STAGES * A_STAGE_BYTES;
+    Control *control = reinterpret_cast<Control *>(smem + STAGES * STAGE_BYTES);
+
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t num_tiles = params.m_blocks * params.n_blocks;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&control->full[s]), 1);
+            mbar_init(smem_u32(&control->empty[s]), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_u32(&control->tmem_full[i]), 1);
+            mbar_init(smem_u32(&control->tmem_empty[i]), EPILOGUE_THREADS / 32);
+        }
+        mbar_init(smem_u32(&control->drain), 1);
+        control->abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&control->tmem_base)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = control->tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            prefetch_tensor_map(&map_a);
+            prefetch_tensor_map(&map_w);
+            uint32_t stage = 0, phase = 0;
+            uint32_t issued_phase[STAGES];
+            bool issued[STAGES];
+            for (int s = 0; s < STAGES; ++s) issued[s] = false;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+                const int m0 = static_cast<int>((tile % params.m_blocks) * BM);
+                const int n0 = static_cast<int>((tile / params.m_blocks) * BN);
+                for (uint32_t kb = 0; kb < params.num_kb; ++kb) {
+                    if (!wait_bounded(smem_u32(&control->empty[stage]), phase ^ 1u, control, params.error_word)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t full = smem_u32(&control->full[stage]);
+                    mbar_expect_tx(full, STAGE_BYTES);
+                    tma_load_2d(smem_u32(stage_a + stage * A_STAGE_BYTES), &map_a, full, static_cast<int>(kb * BK), m0);
+                    tma_load_2d(smem_u32(stage_b + stage * B_STAGE_BYTES), &map_w, full, static_cast<int>(kb * BK), n0);
+                    issued[stage] = true;
+                    issued_phase[stage] = phase;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                // Abort path: let every copy this thread started land before the CTA exits.
+                for (int s = 0; s < STAGES; ++s) {
+                    if (issued[s]) wait_drain(smem_u32(&control->full[s]), issued_phase[s]);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        uint32_t stage = 0, phase = 0, local_tile = 0;
+        bool ok = true, any_mma = false;
+        for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++local_tile) {
+            const uint32_t acc = local_tile & 1u;
+            const uint32_t acc_phase = (local_tile >> 1) & 1u;
+            if (lane == 0) ok = wait_bounded(smem_u32(&control->tmem_empty[acc]), acc_phase ^ 1u, control, params.error_word);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + acc * BN;
+            for (uint32_t kb = 0; kb < params.num_kb; ++kb) {
+                if (lane == 0) ok = wait_bounded(smem_u32(&control->full[stage]), phase, control, params.error_word);
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                if (!ok) break;
+                tc_fence_after();
+                if (lane == 0) {
+                    const uint64_t a_desc = smem_desc_sw128(smem_u32(stage_a + stage * A_STAGE_BYTES));
+                    const uint64_t b_desc = smem_desc_sw128(smem_u32(stage_b + stage * B_STAGE_BYTES));
+#pragma unroll
+                    for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+                        // Advance the start address by 32 bytes (encoded >> 4) within the swizzle row.
+                        umma_i8(d_tmem, a_desc + static_cast<uint64_t>(kk * (UMMA_K >> 4)),
+                                b_desc + static_cast<uint64_t>(kk * (UMMA_K >> 4)), (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    umma_commit(smem_u32(&control->empty[stage]));
+                    any_mma = true;
+                }
+                __syncwarp();
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+            if (lane == 0) umma_commit(smem_u32(&control->tmem_full[acc]));
+            __syncwarp();
+        }
+        if (!ok && lane == 0 && any_mma) {
+            // Abort path: wait for every MMA this thread issued before TMEM is freed.
+            umma_commit(smem_u32(&control->drain));
+            wait_drain(smem_u32(&control->drain), 0);
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const uint32_t quarter = warp & 3u;  // TMEM lanes this warp may access
+        uint32_t local_tile = 0;
+        for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local_tile) {
+            const uint32_t acc = local_tile & 1u;
+            const uint32_t acc_phase = (local_tile >> 1) & 1u;
+            const uint32_t m_block = tile % params.m_blocks;
+            const uint32_t n_block = tile / params.m_blocks;
+            const uint32_t n_base = n_block * BN;
+            bool ok = true;
+            if (lane == 0) ok = wait_bounded(smem_u32(&control->tmem_full[acc]), acc_phase, control, params.error_word);
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            tc_fence_after();
+
+            const uint32_t m = m_block * BM + quarter * 32 + lane;
+            const bool row_ok = m < params.m;
+            const float row_scale =
+                (row_ok && params.mode != static_cast<int>(EpilogueMode::kStoreS32)) ? params.row_scales[m] : 0.0f;
+            const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN;
+#pragma unroll 1
+            for (uint32_t chunk = 0; chunk < BN / 32; ++chunk) {
+                uint32_t r[32];
+                tmem_load_32x32b_x32(taddr + chunk * 32, r);
+                const uint32_t n0 = n_base + chunk * 32;
+                if (!row_ok || n0 >= params.n) continue;
+                const bool full_chunk = n0 + 32 <= params.n;
+                if (params.mode == static_cast<int>(EpilogueMode::kStoreS32)) {
+                    int32_t *row = static_cast<int32_t *>(params.out) + static_cast<size_t>(m) * params.out_stride + n0;
+                    if (full_chunk && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<int4 *>(row + j) = make_int4(static_cast<int>(r[j]), static_cast<int>(r[j + 1]),
+                                                                           static_cast<int>(r[j + 2]), static_cast<int>(r[j + 3]));
+                    } else {
+                        for (uint32_t j = 0; j < 32 && n0 + j < params.n; ++j) row[j] = static_cast<int>(r[j]);
+                    }
+                } else {
+                    // Column scales / bias: every lane reads the same address (an L1 broadcast).
+                    const float *cs = params.col_scales + n0;
+                    const float *cb = params.bias + n0;
+                    const bool with_bias = params.mode == static_cast<int>(EpilogueMode::kDequantizeBias);
+                    float *row = static_cast<float *>(params.out) + static_cast<size_t>(m) * params.out_stride + n0;
+                    if (full_chunk && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
+                        float v[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            v[j] = dequant(r[j], row_scale, __ldg(cs + j));
+                            if (with_bias) v[j] = __fadd_rn(v[j], __ldg(cb + j));
+                        }
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4 *>(row + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    } else {
+                        for (uint32_t j = 0; j < 32 && n0 + j < params.n; ++j) {
+                            float v = dequant(r[j], row_scale, __ldg(cs + j));
+                            if (with_bias) v = __fadd_rn(v, __ldg(cb + j));
+                            row[j] = v;
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&control->tmem_empty[acc]));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                     : "memory");
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_w8a8_gemm_sm100(const CUtensorMap *map_a, const CUtensorMap *map_w, uint32_t m, uint32_t n,
+                                   uint32_t k, const GemmEpilogue &epilogue, unsigned int *error_word, int sm_count,
+                                   cudaStream_t stream) {
+    if (m == 0 || n == 0) return cudaSuccess;
+    if (k == 0) return cudaErrorInvalidValue;
+    static bool configured = false;
+    if (!configured) {
+        const cudaError_t error = cudaFuncSetAttribute(w8a8_gemm_sm100_kernel,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       static_cast<int>(kSmemBytes));
+        if (error != cudaSuccess) return error;
+        configured = true;
+    }
+    GemmParams params;
+    params.m = m;
+    params.n = n;
+    params.k = k;
+    params.num_kb = (k + BK - 1) / BK;
+    params.m_blocks = (m + BM - 1) / BM;
+    params.n_blocks = (n + BN - 1) / BN;
+    params.mode = static_cast<int>(epilogue.mode);
+    params.row_scales = epilogue.row_scales;
+    params.col_scales = epilogue.col_scales;
+    params.bias = epilogue.bias;
+    params.out = epilogue.out;
+    params.out_stride = epilogue.out_stride;
+    params.error_word = error_word;
+    const uint32_t tiles = params.m_blocks * params.n_blocks;
+    const uint32_t grid = tiles < static_cast<uint32_t>(sm_count) ? tiles : static_cast<uint32_t>(sm_count);
+    w8a8_gemm_sm100_kernel<<<grid, NUM_THREADS, kSmemBytes, stream>>>(*map_a, *map_w, params);
+    return cudaGetLastError();
+}
+
+cudaError_t run_w8a8_gemm(const int8_t *a, size_t a_stride, const int8_t *w, size_t w_stride, uint32_t m, uint32_t n,
+                          uint32_t k, const GemmEpilogue &epilogue, unsigned int *error_word, int sm_count,
+                          cudaStream_t stream) {
+    CUtensorMap map_a, map_w;
+    if (!encode_tensor_map_2d_u8(&map_a, a, k, m, a_stride, BK, BM) ||
+        !encode_tensor_map_2d_u8(&map_w, w, k, n, w_stride, BK, BN)) {
+        return cudaErrorInvalidValue;
+    }
+    return launch_w8a8_gemm_sm100(&map_a, &map_w, m, n, k, epilogue, error_word, sm_count, stream);
+}
+
+}  // namespace qpucuda

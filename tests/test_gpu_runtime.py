@@ -1,0 +1,206 @@
+"""The drop-in Python surface on the GPU: Device/Tensor on CUDA memory, Queue/Event on
+CUDA streams and events, the W8A8 and Q4_0 plans, kernel handles and the N-split."""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+
+from oracle import qpu_oracle as oracle
+from qpu_xla import AccessMode, Device, EventStatus, Placement, workloads
+from qpu_xla.candidates import CandidateRegistry
+from qpu_xla.ggml import PreparedQ4_0Linear, quantize_q8_0
+from qpu_xla.kernels import (
+    CUDA_QUANTIZE_ROWS_INT8_KERNEL,
+    CUDA_W8A8_DEQUANTIZE_KERNEL,
+    CUDA_W8A8_GEMM_DEQUANTIZE_KERNEL,
+    CUDA_W8A8_GEMM_KERNEL,
+    CUDA_GGML_Q4_0_Q8_0_LINEAR_KERNEL,
+)
+from qpu_xla.quantization import CalibratedW8A8Linear, PreparedW8A8Linear, QuantizedMatrixInt8, quantize_per_output_channel_int8
+
+pytestmark = pytest.mark.gpu
+
+
+def test_cuda_tensors_write_read_and_slice(cuda_device: Device) -> None:
+    tensor = cuda_device.tensor((8, 16), np.float32)
+    values = np.arange(128, dtype=np.float32).reshape(8, 16)
+    tensor.write(values)
+    np.testing.assert_array_equal(tensor.numpy(), values)
+    view = tensor.slice((slice(2, 5), slice(4, 12)))
+    np.testing.assert_array_equal(view.numpy(), values[2:5, 4:12])
+    assert view.torch().data_ptr() == view.address
+    assert tensor.address % 256 == 0
+
+
+def test_quantize_per_output_channel_on_gpu_matches_reference_weights(cuda_device: Device, golden: dict) -> None:
+    case = workloads.square_case(512)
+    quantized = quantize_per_output_channel_int8(case.weight, device=cuda_device)
+    np.testing.assert_array_equal(quantized.values, golden["w8a8_square_512"]["weight_values"])
+    np.testing.assert_array_equal(quantized.scales, golden["w8a8_square_512"]["weight_scales"])
+
+
+def test_prepared_linear_on_a_queue_matches_the_reference(cuda_device: Device, golden: dict) -> None:
+    ref = golden["w8a8_square_512"]
+    case = workloads.square_case(512)
+    weight = QuantizedMatrixInt8(ref["weight_values"], ref["weight_scales"])
+    with cuda_device.queue() as queue, PreparedW8A8Linear(cuda_device, weight, max_batch=512, bias=ref["bias"]) as plan:
+        source = cuda_device.tensor((512, 512), np.float32)
+        destination = cuda_device.tensor((512, 512), np.float32)
+        source.write(case.source)
+        event = plan.execute(destination, source, queue=queue)
+        event.wait()
+        assert event.name == "cuda.w8a8_gemm_dequantize" and event.status is EventStatus.SUCCEEDED
+        assert event.device_milliseconds is not None and event.device_milliseconds > 0
+        np.testing.assert_array_equal(destination.numpy(), ref["output"])
+        # the decode row goes through the GEMV kernel
+        one = cuda_device.tensor((1, 512), np.float32)
+        one_out = cuda_device.tensor((1, 512), np.float32)
+        one.write(case.source[:1])
+        event = plan.execute(one_out, one, queue=queue)
+        event.wait()
+        assert event.name == "cuda.w8a8_gemv"
+        np.testing.assert_array_equal(one_out.numpy(), ref["output"][:1])
+        # host-buffer C-ABI path of the same plan
+        np.testing.assert_array_equal(plan.execute_host(case.source), ref["output"])
+
+
+def test_plan_binding_and_in_flight_rules(cuda_device: Device) -> None:
+    from qpu_xla import DependencyError
+
+    values = np.ones((32, 32), dtype=np.int8)
+    scales = np.full(32, 0.5, dtype=np.float32)
+    with cuda_device.queue() as first, cuda_device.queue() as second:
+        plan = PreparedW8A8Linear(cuda_device, QuantizedMatrixInt8(values, scales), max_batch=16)
+        source = cuda_device.tensor((16, 32), np.float32)
+        source.write(np.ones((16, 32), dtype=np.float32))
+        destination = cuda_device.tensor((16, 32), np.float32)
+        plan.execute(destination, source, queue=first).wait()
+        with pytest.raises(DependencyError):
+            plan.execute(destination, source, queue=second)
+        with pytest.raises(ValueError):
+            plan.execute(cuda_device.tensor((16, 31), np.float32), source, queue=first)
+        plan.close()
+        with pytest.raises(RuntimeError):
+            plan.execute(destination, source, queue=first)
+
+
+def test_kernel_handles_compose_on_queues_with_cross_queue_events(cuda_device: Device) -> None:
+    """quantize on one queue, GEMM s32 + standalone dequant on another, fused GEMM on a third."""
+    rng = np.random.default_rng(8)
+    m, k, n = 200, 256, 384
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    weight_values, weight_scales = oracle.quantize_per_output_channel_int8(rng.standard_normal((n, k), dtype=np.float32))
+    bias = rng.standard_normal(n).astype(np.float32)
+    expected = oracle.w8a8_linear(x, weight_values, weight_scales, bias)
+    with cuda_device.queue() as q1, cuda_device.queue() as q2:
+        source = cuda_device.tensor((m, k), np.float32)
+        source.write(x)
+        quantized = cuda_device.tensor((m, k), np.int8)
+        row_scales = cuda_device.tensor((m,), np.float32)
+        weight = cuda_device.tensor((n, k), np.int8)
+        weight.write(weight_values)
+        col_scales = cuda_device.tensor((n,), np.float32)
+        col_scales.write(weight_scales)
+        bias_t = cuda_device.tensor((n,), np.float32)
+        bias_t.write(bias)
+        acc = cuda_device.tensor((m, n), np.int32)
+        out = cuda_device.tensor((m, n), np.float32)
+        fused = cuda_device.tensor((m, n), np.float32)
+        e_quant = q1.submit(CUDA_QUANTIZE_ROWS_INT8_KERNEL, (source, quantized, row_scales), buffers=(quantized.access(AccessMode.WRITE),))
+        e_gemm = q2.submit(CUDA_W8A8_GEMM_KERNEL, (quantized, weight, acc), wait_for=(e_quant,))
+        e_deq = q2.submit(CUDA_W8A8_DEQUANTIZE_KERNEL, (acc, row_scales, col_scales, out, bias_t), wait_for=(e_gemm,))
+        e_fused = q1.submit(CUDA_W8A8_GEMM_DEQUANTIZE_KERNEL, (quantized, weight, row_scales, col_scales, fused, bias_t), wait_for=(e_quant,))
+        e_deq.wait()
+        e_fused.wait()
+        np.testing.assert_array_equal(acc.numpy(), oracle.int8_accumulate(oracle.quantize_rows_int8(x)[0], weight_values))
+        np.testing.assert_array_equal(out.numpy(), expected)
+        np.testing.assert_array_equal(fused.numpy(), expected)
+        trace = q2.chrome_trace()["traceEvents"]
+        assert {"cuda.w8a8_gemm", "cuda.w8a8_dequantize", "dependency"} <= {event["name"] for event in trace}
+        assert q2.consume_completed_event_counts() == {"cuda": 2}
+
+
+def test_calibrated_linear_auto_runs_on_cuda(cuda_device: Device, golden: dict) -> None:
+    ref = golden["w8a8_square_64"]
+    case = workloads.square_case(64)
+    weight = QuantizedMatrixInt8(ref["weight_values"], ref["weight_scales"])
+    with cuda_device.queue() as queue, CalibratedW8A8Linear(cuda_device, weight, max_batch=64, candidates=CandidateRegistry()) as plan:
+        source = cuda_device.tensor((64, 64), np.float32)
+        destination = cuda_device.tensor((64, 64), np.float32)
+        source.write(case.source)
+        plan.execute(destination, source, queue=queue, placement=Placement.CUDA).wait()
+        np.testing.assert_array_equal(destination.numpy(), ref["output"])
+        with pytest.raises(ValueError):
+            plan.execute(destination, source, queue=queue, placement=Placement.QPU)
+
+
+def test_q4_0_plan_and_kernel_handle(cuda_device: Device, golden: dict) -> None:
+    import torch
+
+    ref = golden["q4_0_reference"]
+    source, weight = workloads.q4_0_case(workloads.TINYLLAMA_Q4_0_SHAPES[1], 4)
+    weight_blocks = oracle.quantize_q4_0(weight)
+    with cuda_device.queue() as queue, PreparedQ4_0Linear(cuda_device, weight_blocks, rows=4) as plan:
+        activation = cuda_device.tensor((4, 176, 34), np.uint8)
+        activation.write(ref["ffn_down_m4_activation"])
+        destination = cuda_device.tensor((4, 2048), np.float32)
+        plan.execute(destination, activation, queue=queue).wait()
+        expected = ref["ffn_down_m4_expected"]
+        scale = float(np.abs(expected).max())
+        assert float(np.abs(destination.numpy() - expected).max()) <= 1e-4 * scale
+        # weight/output column split: weight columns [512, 1024) -> destination columns [0, 512)
+        split = cuda_device.tensor((4, 512), np.float32)
+        plan.execute(split, activation, queue=queue, column_start=512, column_count=512, output_column_start=0).wait()
+        np.testing.assert_array_equal(split.numpy(), destination.numpy()[:, 512:1024])
+        # fused fp32 path from the queue and the torch path
+        fp32 = cuda_device.tensor((4, 5632), np.float32)
+        fp32.write(source)
+        fused = cuda_device.tensor((4, 2048), np.float32)
+        plan.execute_f32(fused, fp32, queue=queue).wait()
+        np.testing.assert_array_equal(fused.numpy(), destination.numpy())
+        torch_out = plan.forward(quantize_q8_0(cuda_device, fp32.torch()))
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(torch_out.cpu().numpy(), destination.numpy())
+        # the single-kernel handle over native blocks
+        weight_t = cuda_device.tensor(weight_blocks.shape, np.uint8)
+        weight_t.write(weight_blocks)
+        native_out = cuda_device.tensor((4, 2048), np.float32)
+        queue.submit(CUDA_GGML_Q4_0_Q8_0_LINEAR_KERNEL, (activation, weight_t, native_out, 0, 0, 2048)).wait()
+        np.testing.assert_array_equal(native_out.numpy(), destination.numpy())
+
+
+def test_sharded_linear_on_one_rank_equals_the_unsharded_plan(cuda_device: Device) -> None:
+    """The N-split code path with a one-rank NCCL group (the multi-rank run is bench.py --gpus N)."""
+    import torch
+    import torch.distributed as dist
+
+    from qpu_xla.sharded import ShardedQ4_0Linear, ShardedW8A8Linear
+
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29517")
+    owned = not dist.is_initialized()
+    if owned:
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
+    try:
+        case = workloads.linear_inputs(96, 512, 1000, seed=31, weight_std=0.02, bias=True)
+        values, scales = oracle.quantize_per_output_channel_int8(case.weight)
+        weight = QuantizedMatrixInt8(values, scales)
+        sharded = ShardedW8A8Linear(cuda_device, weight, max_batch=96, bias=case.bias)
+        out = sharded.forward(torch.from_numpy(case.source).cuda())
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(out.cpu().numpy(), oracle.w8a8_linear(case.source, values, scales, case.bias))
+        sharded.close()
+        source, w = workloads.q4_0_case(workloads.TINYLLAMA_Q4_0_SHAPES[0], 1)
+        blocks = oracle.quantize_q4_0(w)
+        q4 = ShardedQ4_0Linear(cuda_device, blocks, rows=1)
+        y = q4.forward(torch.from_numpy(source).cuda(), fp32_source=True)
+        torch.cuda.synchronize()
+        expected = oracle.q4_0_q8_0_linear(oracle.quantize_q8_0(source), blocks)
+        assert float(np.abs(y.cpu().numpy() - expected).max()) <= 1e-4 * float(np.abs(expected).max())
+        q4.close()
+    finally:
+        if owned:
+            dist.destroy_process_group()

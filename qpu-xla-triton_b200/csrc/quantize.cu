@@ -142,13 +142,9 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float *__restr
         const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
         int v = __float2int_rn(__fmul_rn(value, id));
         v = v < -127 ? -127 : (v > 127 ? 127 : v);
-        uint8_t *destination = out + block * 34;
+        uint8_t *destination = out + block * 34;  // blocks start on even bytes
+        if (lane == 0) *reinterpret_cast<unsigned short *>(destination) = __half_as_ushort(__float2half_rn(d));
         destination[2 + lane] = static_cast<uint8_t>(static_cast<int8_t>(v));
-        if (lane == 0) {
-            const unsigned short bits = __half_as_ushort(__float2half_rn(d));
-            destination[0] = static_cast<uint8_t>(bits & 0xffu);
-            destination[1] = static_cast<uint8_t>(bits >> 8);
-        }
     }
 }
 
@@ -184,13 +180,9 @@ __global__ void __launch_bounds__(256) quantize_q4_0_kernel(const float *__restr
         int code = __float2int_rz(__fadd_rn(__fmul_rn(value, id), 8.5f));
         code = code > 15 ? 15 : (code < 0 ? 0 : code);
         const int high = __shfl_down_sync(0xffffffffu, code, 16);
-        uint8_t *destination = out + block * 18;
+        uint8_t *destination = out + block * 18;  // blocks start on even bytes
+        if (lane == 0) *reinterpret_cast<unsigned short *>(destination) = __half_as_ushort(__float2half_rn(d));
         if (lane < 16) destination[2 + lane] = static_cast<uint8_t>(code | (high << 4));
-        if (lane == 0) {
-            const unsigned short bits = __half_as_ushort(__float2half_rn(d));
-            destination[0] = static_cast<uint8_t>(bits & 0xffu);
-            destination[1] = static_cast<uint8_t>(bits >> 8);
-        }
     }
 }
 

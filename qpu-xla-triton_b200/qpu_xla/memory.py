@@ -284,7 +284,10 @@ class Tensor:
             return
         import torch
 
-        self.torch().copy_(torch.from_numpy(np.ascontiguousarray(array)))
+        host = np.ascontiguousarray(array)
+        if not host.flags.writeable:
+            host = host.copy()
+        self.torch().copy_(torch.from_numpy(host))
 
     def slice(self: Self, slices: tuple[slice, ...]) -> Tensor:
         """Unit-step slice without copying (memory.py:247-261)."""

@@ -84,9 +84,13 @@ const char *qpucuda_context_last_error(const qpucuda_context *context);
 qpucuda_status qpucuda_context_capabilities(const qpucuda_context *context, qpucuda_capabilities *result);
 /* qpu_llama_context_set_failure_mask (qpu_llama_runtime.h:93). */
 void qpucuda_context_set_failure_mask(qpucuda_context *context, uint32_t failure_mask);
-/* Re-target the context at another stream of the same device (NULL = the library stream). */
+/* Re-target the context at another stream of the same device. The value is a
+ * cudaStream_t with CUDA's meaning: NULL is the legacy default stream (the
+ * stream PyTorch reports as 0). */
 qpucuda_status qpucuda_context_set_stream(qpucuda_context *context, void *stream);
 void *qpucuda_context_stream(const qpucuda_context *context);
+/* The library-owned non-blocking stream (what a NULL config->stream selects at creation). */
+void *qpucuda_context_library_stream(const qpucuda_context *context);
 /* Bounded wait for all work issued on the context stream, then the kernels'
  * device-side error word is checked. A timeout or a kernel-reported error
  * poisons the context (as qpu_llama_submission_wait does,

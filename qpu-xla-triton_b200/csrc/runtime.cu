@@ -268,12 +268,16 @@ void qpucuda_context_set_failure_mask(qpucuda_context *context, uint32_t failure
 qpucuda_status qpucuda_context_set_stream(qpucuda_context *context, void *stream) {
     if (context == nullptr) return QPUCUDA_INVALID_ARGUMENT;
     std::lock_guard<std::mutex> lock(context->mutex);
-    context->stream = stream != nullptr ? static_cast<cudaStream_t>(stream) : context->own_stream;
+    context->stream = static_cast<cudaStream_t>(stream);
     return QPUCUDA_OK;
 }
 
 void *qpucuda_context_stream(const qpucuda_context *context) {
     return context != nullptr ? static_cast<void *>(context->stream) : nullptr;
+}
+
+void *qpucuda_context_library_stream(const qpucuda_context *context) {
+    return context != nullptr ? static_cast<void *>(context->own_stream) : nullptr;
 }
 
 qpucuda_status qpucuda_context_synchronize(qpucuda_context *context) {

@@ -151,6 +151,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "qpucuda_context_set_failure_mask": (None, [_P, c_uint32]),
     "qpucuda_context_set_stream": (_S, [_P, _P]),
     "qpucuda_context_stream": (_P, [_P]),
+    "qpucuda_context_library_stream": (_P, [_P]),
     "qpucuda_context_synchronize": (_S, [_P]),
     "qpucuda_context_poisoned": (c_int, [_P]),
     "qpucuda_status_string": (c_char_p, [c_int]),
@@ -279,7 +280,12 @@ class NativeContext:
         raise_for_status(status, self.handle, what)
 
     def set_stream(self, stream: int | None) -> None:
-        self.check(self._library.qpucuda_context_set_stream(self.handle, stream), "qpucuda_context_set_stream")
+        """Issue on ``stream`` (a cudaStream_t; 0/None is CUDA's legacy default stream)."""
+        self.check(self._library.qpucuda_context_set_stream(self.handle, stream or None), "qpucuda_context_set_stream")
+
+    def use_library_stream(self) -> None:
+        """Issue on the library-owned non-blocking stream (the host-buffer entry points use it)."""
+        self.set_stream(self._library.qpucuda_context_library_stream(self.handle))
 
     def set_failure_mask(self, mask: int) -> None:
         self._library.qpucuda_context_set_failure_mask(self.handle, int(mask))

@@ -344,7 +344,7 @@ class PreparedQ4_0Linear:
         )
         timing = _native.Q40Timing()
         with self._backend.launch_lock:  # type: ignore[attr-defined]
-            self._native.set_stream(None)
+            self._native.use_library_stream()
             status = self._native.library.qpucuda_q4_0_linear_execute(self._handle, ctypes.byref(execution), ctypes.byref(timing))
         self._native.check(status, "qpucuda_q4_0_linear_execute")
         return {name: int(getattr(timing, name)) for name, _ in _native.Q40Timing._fields_}

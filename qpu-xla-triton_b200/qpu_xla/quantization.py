@@ -160,7 +160,7 @@ class PreparedW8A8Linear:
         )
         handle = ctypes.c_void_p()
         with self._backend.launch_lock:  # type: ignore[attr-defined]
-            self._native.set_stream(None)
+            self._native.use_library_stream()
             status = self._native.library.qpucuda_w8a8_linear_prepare(self._native.handle, ctypes.byref(desc), ctypes.byref(handle))
         self._native.check(status, "qpucuda_w8a8_linear_prepare")
         self._handle = int(handle.value)  # type: ignore[arg-type]
@@ -329,7 +329,7 @@ class PreparedW8A8Linear:
             destination = np.empty((batch, self.output_count), dtype=np.float32)
         execution = _native.W8A8Execution(source.ctypes.data, source.nbytes, destination.ctypes.data, destination.nbytes, batch)
         with self._backend.launch_lock:  # type: ignore[attr-defined]
-            self._native.set_stream(None)
+            self._native.use_library_stream()
             status = self._native.library.qpucuda_w8a8_linear_execute(self._handle, ctypes.byref(execution))
         self._native.check(status, "qpucuda_w8a8_linear_execute")
         return destination

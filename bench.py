@@ -45,10 +45,13 @@ L2_FLUSH_BYTES = 256 << 20
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
+ONLY: set[str] = set()  # --only: restrict to some projections (profiling captures of a smaller case)
+
+
 def shapes() -> list[tuple[str, int, int]]:
     from qpu_xla import workloads
 
-    return [(s.name, s.in_features, s.out_features) for s in workloads.LLAMA2_70B_FFN]
+    return [(s.name, s.in_features, s.out_features) for s in workloads.LLAMA2_70B_FFN if not ONLY or s.name in ONLY]
 
 
 def measured_peaks() -> tuple[dict[str, float], str]:
@@ -422,44 +425,48 @@ def run_ours(args: argparse.Namespace) -> None:
 # ---------------------------------------------------------------------------- reference (CPU)
 
 
+_CPU_SAMPLES: list[tuple[object, object, object]] = []
+CPU_COLUMNS = 1024
+
+
 def cpu_reference_sample(*, target_seconds: float, rows: int | None = None) -> dict[str, object]:
     """The reference's CPU path (oracle port of quantization.py:1065-1082: NumPy per-row
     quantization, int32 matmul, fp32 dequant) on a bounded sample of the workload: ``rows``
-    token rows x 1024 output columns of each projection at its full K, all host threads."""
+    token rows (sized to ``target_seconds``, at most the full 4096) x 1024 output columns of
+    each projection at its full K, split over all host threads."""
     import numpy as np
 
     from oracle import qpu_oracle as oracle
 
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
-    columns = 1024
-    rng = np.random.default_rng(SEED)
-    samples = []
-    for _, k, _n in shapes():
-        x = rng.standard_normal((64, k), dtype=np.float32)
-        w = (rng.standard_normal((columns, k), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
-        values, scales = oracle.quantize_per_output_channel_int8(w)
-        samples.append((x, values.astype(np.int32), scales))
+    columns = CPU_COLUMNS
+    if not _CPU_SAMPLES:
+        rng = np.random.default_rng(SEED)
+        for _, k, _n in shapes():
+            x = rng.standard_normal((TOKENS, k), dtype=np.float32)
+            w = (rng.standard_normal((columns, k), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+            values, scales = oracle.quantize_per_output_channel_int8(w)
+            _CPU_SAMPLES.append((x, values.astype(np.int32), scales))
     pool = ThreadPoolExecutor(max_workers=cores)
 
     def run(sample_rows: int) -> float:
         ops = 0.0
-        for x, w32, scales in samples:
-            xs = x[:sample_rows]
+        for x, w32, scales in _CPU_SAMPLES:
+            xs = x[:sample_rows]  # type: ignore[index]
             q, s = oracle.quantize_rows_int8(xs)
             q32 = q.astype(np.int32)
-            chunks = np.array_split(np.arange(w32.shape[0]), cores)
-            parts = list(pool.map(lambda idx: q32 @ w32[idx].T, [c for c in chunks if len(c)]))
+            chunks = np.array_split(np.arange(w32.shape[0]), cores)  # type: ignore[union-attr]
+            parts = list(pool.map(lambda idx: q32 @ w32[idx].T, [c for c in chunks if len(c)]))  # type: ignore[index]
             acc = np.concatenate(parts, axis=1)
-            oracle.w8a8_dequantize(acc, s, scales)
-            ops += 2.0 * xs.shape[0] * w32.shape[0] * xs.shape[1]
+            oracle.w8a8_dequantize(acc, s, scales)  # type: ignore[arg-type]
+            ops += 2.0 * xs.shape[0] * w32.shape[0] * xs.shape[1]  # type: ignore[union-attr]
         return ops
 
-    t0 = time.perf_counter()
-    probe_ops = run(4)
-    probe = time.perf_counter() - t0
-    rate = probe_ops / max(probe, 1e-6)
     if rows is None:
-        rows = int(max(4, min(64, target_seconds * rate / max(probe_ops / 4, 1.0))))
+        t0 = time.perf_counter()
+        probe_ops = run(8)
+        rate = probe_ops / max(time.perf_counter() - t0, 1e-6)
+        rows = int(max(8, min(TOKENS, target_seconds * rate / (probe_ops / 8))))
     t0 = time.perf_counter()
     ops = run(rows)
     seconds = time.perf_counter() - t0
@@ -479,7 +486,7 @@ def run_reference(args: argparse.Namespace) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    per_step = max(1.0, min(20.0, 150.0 / max(1, args.steps + args.warmup)))
+    per_step = max(0.05, min(20.0, 120.0 / max(1, args.steps + args.warmup)))
     first = cpu_reference_sample(target_seconds=per_step)
     rows = int(str(first["sample"]).split()[0])
     for _ in range(max(0, args.warmup - 1)):
@@ -515,15 +522,17 @@ def run_reference(args: argparse.Namespace) -> None:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=100)
+    parser.add_argument("--steps", type=int, default=300)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=15.0)
+    parser.add_argument("--only", default="", help="comma-separated projections (profiling captures only)")
     args = parser.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    ONLY.update(name for name in args.only.split(",") if name)
     if args.impl == "reference":
         run_reference(args)
     else:

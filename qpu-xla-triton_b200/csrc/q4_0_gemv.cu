@@ -29,6 +29,7 @@ namespace {
 
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
+constexpr int kUnroll = 8;
 
 struct ActivationView {
     const uint8_t *base;
@@ -64,27 +65,42 @@ __device__ __forceinline__ int8_t activation_value(const ActivationView &view, c
 }
 
 // Shared memory: q [rows][blocks * 32] int8, d [rows][blocks] fp32, sum8 [rows][blocks] int32.
+// One thread per (row, block): a native block is read with independent 16-bit loads (blocks
+// start on even bytes), so staging costs one round trip to L2 rather than one per block.
 __device__ __forceinline__ void stage_activation(const ActivationView &view, int8_t *q, float *d, int *sum8) {
-    const uint32_t warp = threadIdx.x >> 5;
-    const uint32_t lane = threadIdx.x & 31;
     const uint32_t total = view.rows * view.blocks;
-    for (uint32_t item = warp; item < total; item += blockDim.x / 32) {
+    const uint32_t interleaved_rows = view.interleave == 0 ? 0 : view.rows - view.rows % 4;
+    for (uint32_t item = threadIdx.x; item < total; item += blockDim.x) {
         const uint32_t row = item / view.blocks;
         const uint32_t block = item % view.blocks;
         const uint8_t *scale_bytes;
         const uint8_t *values;
         activation_block(view, row, block, &scale_bytes, &values);
-        const int8_t value = activation_value(view, values, row, lane);
-        q[static_cast<size_t>(item) * 32 + lane] = value;
-        int sum = value;
+        uint32_t words[8];
+        if (row >= interleaved_rows) {
+            const uint16_t *halves = reinterpret_cast<const uint16_t *>(values);
 #pragma unroll
-        for (int offset = 16; offset > 0; offset >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, offset);
-        if (lane == 0) {
-            const unsigned short bits =
-                static_cast<unsigned short>(scale_bytes[0]) | static_cast<unsigned short>(scale_bytes[1] << 8);
-            d[item] = __half2float(__ushort_as_half(bits));
-            sum8[item] = 8 * sum;
+            for (int i = 0; i < 8; ++i)
+                words[i] = static_cast<uint32_t>(halves[2 * i]) | (static_cast<uint32_t>(halves[2 * i + 1]) << 16);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                uint32_t word = 0;
+#pragma unroll
+                for (int byte = 0; byte < 4; ++byte)
+                    word |= static_cast<uint32_t>(static_cast<uint8_t>(activation_value(view, values, row, 4 * i + byte)))
+                            << (8 * byte);
+                words[i] = word;
+            }
         }
+        int sum = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum = __dp4a(static_cast<int>(words[i]), 0x01010101, sum);
+        uint4 *destination = reinterpret_cast<uint4 *>(q + static_cast<size_t>(item) * 32);
+        destination[0] = make_uint4(words[0], words[1], words[2], words[3]);
+        destination[1] = make_uint4(words[4], words[5], words[6], words[7]);
+        d[item] = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(scale_bytes)));
+        sum8[item] = 8 * sum;
     }
 }
 
@@ -158,17 +174,17 @@ __global__ void __launch_bounds__(kThreads) q4_0_gemv_kernel(const uint8_t *__re
             const uint8_t *w_col = nibbles + column * blocks * 16;
             const uint16_t *s_col = scales + column * blocks;
             uint32_t b = lane;
-            // Four independent 16-byte loads in flight per lane.
-            for (; b + 96 < blocks; b += 128) {
-                uint4 w[4];
-                uint16_t s[4];
+            // Eight independent 16-byte loads in flight per lane (4 KB per warp).
+            for (; b + 32 * (kUnroll - 1) < blocks; b += 32 * kUnroll) {
+                uint4 w[kUnroll];
+                uint16_t s[kUnroll];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
+                for (int u = 0; u < kUnroll; ++u) {
                     w[u] = load_stream_u4(w_col + static_cast<size_t>(b + 32 * u) * 16);
                     s[u] = __ldg(s_col + b + 32 * u);
                 }
 #pragma unroll
-                for (int u = 0; u < 4; ++u) accumulate_block<ROWS>(w[u], s[u], b + 32 * u, blocks, q, d, sum8, acc);
+                for (int u = 0; u < kUnroll; ++u) accumulate_block<ROWS>(w[u], s[u], b + 32 * u, blocks, q, d, sum8, acc);
             }
             for (; b < blocks; b += 32) {
                 const uint4 w = load_stream_u4(w_col + static_cast<size_t>(b) * 16);
@@ -204,11 +220,12 @@ cudaError_t launch_rows(const uint8_t *nibbles, const uint16_t *scales, const ui
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (error != cudaSuccess) return error;
     }
-    // Enough CTAs to cover every column once, at most a few per SM (each stages the activation).
+    // Persistent CTAs, at most a few per SM (each stages the activation once). The grid is
+    // balanced so every warp gets the same number of columns (no straggling last round).
     const uint32_t per_sm = smem <= 40u * 1024u ? 4u : (smem <= 100u * 1024u ? 2u : 1u);
-    uint32_t grid = (count + kWarps - 1) / kWarps;
     const uint32_t cap = static_cast<uint32_t>(sm_count) * per_sm;
-    if (grid > cap) grid = cap;
+    const uint32_t rounds = (count + cap * kWarps - 1) / (cap * kWarps);
+    const uint32_t grid = (count + kWarps * rounds - 1) / (kWarps * rounds);
     kernel<<<grid, kThreads, smem, stream>>>(nibbles, scales, native, blocks, view, destination, destination_stride,
                                              col0, out_col0, count);
     return cudaGetLastError();
@@ -233,7 +250,9 @@ cudaError_t launch_q4_0_q8_0_gemv(const Q40Weights &weights, const uint8_t *acti
                                   uint32_t interleave, float *destination, size_t destination_stride, uint32_t col0,
                                   uint32_t out_col0, uint32_t count, int sm_count, cudaStream_t stream) {
     if (count == 0 || rows == 0) return cudaSuccess;
-    if ((reinterpret_cast<uintptr_t>(weights.nibbles) & 15u) != 0) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(weights.nibbles) & 15u) != 0 || (reinterpret_cast<uintptr_t>(activation) & 1u) != 0) {
+        return cudaErrorInvalidValue;
+    }
     const ActivationView view{activation, rows, weights.blocks, interleave};
     return dispatch_rows<false>(weights.nibbles, weights.scales, nullptr, weights.blocks, view, destination,
                                 destination_stride, col0, out_col0, count, sm_count, stream);
@@ -244,7 +263,9 @@ cudaError_t launch_q4_0_q8_0_gemv_native(const uint8_t *activation, uint32_t row
                                          uint32_t col0, uint32_t out_col0, uint32_t count, int sm_count,
                                          cudaStream_t stream) {
     if (count == 0 || rows == 0) return cudaSuccess;
-    if ((reinterpret_cast<uintptr_t>(weight) & 1u) != 0) return cudaErrorInvalidValue;
+    if ((reinterpret_cast<uintptr_t>(weight) & 1u) != 0 || (reinterpret_cast<uintptr_t>(activation) & 1u) != 0) {
+        return cudaErrorInvalidValue;
+    }
     const ActivationView view{activation, rows, blocks, 0};
     return dispatch_rows<true>(nullptr, nullptr, weight, blocks, view, destination, destination_stride, col0,
                                out_col0, count, sm_count, stream);

@@ -280,7 +280,8 @@ def test_host_buffer_execute_and_injected_failures() -> None:
 def test_injected_allocation_failure_leaves_no_plan() -> None:
     from gpu_helpers import Native
 
-    native = Native(failure_mask=int(_native.FailurePoint.ALLOCATION))
+    native = Native()
+    native.context.set_failure_mask(int(_native.FailurePoint.ALLOCATION))
     try:
         values = np.ones((32, 32), dtype=np.int8)
         scales = np.ones(32, dtype=np.float32)

@@ -12,8 +12,10 @@
 //
 // Prepared weight layout (made once at prepare, same bytes per block as the
 // native 18-byte block): nibbles [columns][blocks][16] (16-byte aligned) and
-// fp16 scales [columns][blocks]. One warp per output column; lane l takes blocks
-// l, l + 32, ..., so a warp reads 512 contiguous bytes of nibbles per step.
+// fp16 scales [columns][blocks]. One warp per output column (SPLIT = 2 or 4 warps for
+// long reductions, their partials added in a fixed order); lane l takes blocks
+// l, l + 32 * SPLIT, ..., so a warp reads 512 contiguous bytes of nibbles per load,
+// eight loads in flight per lane.
 // Weight codes stay packed: dp4a(nibbles & 0x0F0F0F0F, a[0..3]) and
 // dp4a((nibbles >> 4) & 0x0F0F0F0F, a[16..19]) etc., and the -8 offset is one
 // subtraction of 8 * sum(a) per block, precomputed when the activation is staged.
@@ -27,7 +29,7 @@
 namespace qpucuda {
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kUnroll = 8;
 
@@ -139,7 +141,9 @@ __device__ __forceinline__ void accumulate_block(uint4 w, uint16_t w_scale_bits,
     }
 }
 
-template <int ROWS, bool NATIVE>
+// SPLIT warps share one column: warp part p takes blocks p*32 + lane + i*32*SPLIT, and
+// the SPLIT partial sums are added in part order through shared memory (deterministic).
+template <int ROWS, bool NATIVE, int SPLIT>
 __global__ void __launch_bounds__(kThreads) q4_0_gemv_kernel(const uint8_t *__restrict__ nibbles,
                                                              const uint16_t *__restrict__ scales,
                                                              const uint8_t *__restrict__ native, uint32_t blocks,
@@ -147,21 +151,28 @@ __global__ void __launch_bounds__(kThreads) q4_0_gemv_kernel(const uint8_t *__re
                                                              size_t destination_stride, uint32_t col0,
                                                              uint32_t out_col0, uint32_t count) {
     extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float partial[kWarps][ROWS];
     int8_t *q = reinterpret_cast<int8_t *>(smem);
     float *d = reinterpret_cast<float *>(smem + static_cast<size_t>(ROWS) * blocks * 32);
     int *sum8 = reinterpret_cast<int *>(d + static_cast<size_t>(ROWS) * blocks);
     stage_activation(view, q, d, sum8);
     __syncthreads();
 
+    constexpr uint32_t kSlots = kWarps / SPLIT;
+    constexpr uint32_t kStride = 32 * SPLIT;  // blocks between a lane's consecutive blocks
+    const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
-    for (uint32_t j = blockIdx.x * kWarps + (threadIdx.x >> 5); j < count; j += gridDim.x * kWarps) {
+    const uint32_t part = warp % SPLIT;
+    const uint32_t slot = warp / SPLIT;
+    const uint32_t first = part * 32 + lane;
+    for (uint32_t j = blockIdx.x * kSlots + slot; j < count; j += gridDim.x * kSlots) {
         const size_t column = col0 + j;
         float acc[ROWS];
 #pragma unroll
         for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
         if constexpr (NATIVE) {
             // Native 18-byte blocks: 2-byte aligned, read as nine 16-bit words.
-            for (uint32_t b = lane; b < blocks; b += 32) {
+            for (uint32_t b = first; b < blocks; b += kStride) {
                 const uint16_t *src = reinterpret_cast<const uint16_t *>(native + (column * blocks + b) * 18);
                 uint4 w;
                 w.x = static_cast<uint32_t>(src[1]) | (static_cast<uint32_t>(src[2]) << 16);
@@ -173,20 +184,20 @@ __global__ void __launch_bounds__(kThreads) q4_0_gemv_kernel(const uint8_t *__re
         } else {
             const uint8_t *w_col = nibbles + column * blocks * 16;
             const uint16_t *s_col = scales + column * blocks;
-            uint32_t b = lane;
+            uint32_t b = first;
             // Eight independent 16-byte loads in flight per lane (4 KB per warp).
-            for (; b + 32 * (kUnroll - 1) < blocks; b += 32 * kUnroll) {
+            for (; b + kStride * (kUnroll - 1) < blocks; b += kStride * kUnroll) {
                 uint4 w[kUnroll];
                 uint16_t s[kUnroll];
 #pragma unroll
                 for (int u = 0; u < kUnroll; ++u) {
-                    w[u] = load_stream_u4(w_col + static_cast<size_t>(b + 32 * u) * 16);
-                    s[u] = __ldg(s_col + b + 32 * u);
+                    w[u] = load_stream_u4(w_col + static_cast<size_t>(b + kStride * u) * 16);
+                    s[u] = __ldg(s_col + b + kStride * u);
                 }
 #pragma unroll
-                for (int u = 0; u < kUnroll; ++u) accumulate_block<ROWS>(w[u], s[u], b + 32 * u, blocks, q, d, sum8, acc);
+                for (int u = 0; u < kUnroll; ++u) accumulate_block<ROWS>(w[u], s[u], b + kStride * u, blocks, q, d, sum8, acc);
             }
-            for (; b < blocks; b += 32) {
+            for (; b < blocks; b += kStride) {
                 const uint4 w = load_stream_u4(w_col + static_cast<size_t>(b) * 16);
                 accumulate_block<ROWS>(w, __ldg(s_col + b), b, blocks, q, d, sum8, acc);
             }
@@ -196,7 +207,21 @@ __global__ void __launch_bounds__(kThreads) q4_0_gemv_kernel(const uint8_t *__re
 #pragma unroll
             for (int offset = 16; offset > 0; offset >>= 1) acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], offset));
         }
-        if (lane < static_cast<uint32_t>(ROWS)) {
+        if constexpr (SPLIT > 1) {
+            // The SPLIT warps of this slot run the same trip count, so the named barrier is safe.
+            if (lane == 0) {
+#pragma unroll
+                for (int r = 0; r < ROWS; ++r) partial[warp][r] = acc[r];
+            }
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + slot), "r"(32 * SPLIT) : "memory");
+            if (part == 0 && lane < static_cast<uint32_t>(ROWS)) {
+                float value = partial[slot * SPLIT][lane];
+#pragma unroll
+                for (int p = 1; p < SPLIT; ++p) value = __fadd_rn(value, partial[slot * SPLIT + p][lane]);
+                destination[static_cast<size_t>(lane) * destination_stride + out_col0 + j] = value;
+            }
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + slot), "r"(32 * SPLIT) : "memory");
+        } else if (lane < static_cast<uint32_t>(ROWS)) {
             float value = acc[0];
 #pragma unroll
             for (int r = 1; r < ROWS; ++r)
@@ -208,38 +233,62 @@ __global__ void __launch_bounds__(kThreads) q4_0_gemv_kernel(const uint8_t *__re
 
 size_t smem_bytes(uint32_t rows, uint32_t blocks) { return static_cast<size_t>(rows) * blocks * (32 + 4 + 4); }
 
-template <int ROWS, bool NATIVE>
-cudaError_t launch_rows(const uint8_t *nibbles, const uint16_t *scales, const uint8_t *native, uint32_t blocks,
-                        const ActivationView &view, float *destination, size_t destination_stride, uint32_t col0,
-                        uint32_t out_col0, uint32_t count, int sm_count, cudaStream_t stream) {
-    const size_t smem = smem_bytes(ROWS, blocks);
+struct LaunchArgs {
+    const uint8_t *nibbles;
+    const uint16_t *scales;
+    const uint8_t *native;
+    uint32_t blocks;
+    ActivationView view;
+    float *destination;
+    size_t destination_stride;
+    uint32_t col0;
+    uint32_t out_col0;
+    uint32_t count;
+    int sm_count;
+    cudaStream_t stream;
+};
+
+template <int ROWS, bool NATIVE, int SPLIT>
+cudaError_t launch_split(const LaunchArgs &a) {
+    const size_t smem = smem_bytes(ROWS, a.blocks);
     if (smem > 200u * 1024u) return cudaErrorInvalidValue;
-    auto kernel = q4_0_gemv_kernel<ROWS, NATIVE>;
+    auto kernel = q4_0_gemv_kernel<ROWS, NATIVE, SPLIT>;
     if (smem > 48u * 1024u) {
         const cudaError_t error =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (error != cudaSuccess) return error;
     }
-    // Persistent CTAs, at most a few per SM (each stages the activation once). The grid is
-    // balanced so every warp gets the same number of columns (no straggling last round).
-    const uint32_t per_sm = smem <= 40u * 1024u ? 4u : (smem <= 100u * 1024u ? 2u : 1u);
-    const uint32_t cap = static_cast<uint32_t>(sm_count) * per_sm;
-    const uint32_t rounds = (count + cap * kWarps - 1) / (cap * kWarps);
-    const uint32_t grid = (count + kWarps * rounds - 1) / (kWarps * rounds);
-    kernel<<<grid, kThreads, smem, stream>>>(nibbles, scales, native, blocks, view, destination, destination_stride,
-                                             col0, out_col0, count);
+    // Persistent CTAs filling the SM's real residency (each stages the activation once); the
+    // grid is balanced so every column slot runs the same number of rounds (no straggling tail).
+    int per_sm = 0;
+    cudaError_t error = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
+    if (error != cudaSuccess) return error;
+    if (per_sm < 1) per_sm = 1;
+    constexpr uint32_t kSlots = kWarps / SPLIT;
+    const uint64_t capacity = static_cast<uint64_t>(a.sm_count) * static_cast<uint64_t>(per_sm);
+    const uint64_t rounds = (a.count + capacity * kSlots - 1) / (capacity * kSlots);
+    const uint32_t grid = static_cast<uint32_t>((a.count + kSlots * rounds - 1) / (kSlots * rounds));
+    kernel<<<grid, kThreads, smem, a.stream>>>(a.nibbles, a.scales, a.native, a.blocks, a.view, a.destination,
+                                               a.destination_stride, a.col0, a.out_col0, a.count);
     return cudaGetLastError();
 }
 
+template <int ROWS, bool NATIVE>
+cudaError_t launch_rows(const LaunchArgs &a) {
+    // Columns with many blocks are split over 2 or 4 warps so there are enough independent
+    // units to keep every SM busy without a long last round.
+    if (a.blocks >= 2048) return launch_split<ROWS, NATIVE, 4>(a);
+    if (a.blocks >= 512) return launch_split<ROWS, NATIVE, 2>(a);
+    return launch_split<ROWS, NATIVE, 1>(a);
+}
+
 template <bool NATIVE>
-cudaError_t dispatch_rows(const uint8_t *nibbles, const uint16_t *scales, const uint8_t *native, uint32_t blocks,
-                          const ActivationView &view, float *destination, size_t destination_stride, uint32_t col0,
-                          uint32_t out_col0, uint32_t count, int sm_count, cudaStream_t stream) {
-    switch (view.rows) {
-        case 1: return launch_rows<1, NATIVE>(nibbles, scales, native, blocks, view, destination, destination_stride, col0, out_col0, count, sm_count, stream);
-        case 2: return launch_rows<2, NATIVE>(nibbles, scales, native, blocks, view, destination, destination_stride, col0, out_col0, count, sm_count, stream);
-        case 3: return launch_rows<3, NATIVE>(nibbles, scales, native, blocks, view, destination, destination_stride, col0, out_col0, count, sm_count, stream);
-        case 4: return launch_rows<4, NATIVE>(nibbles, scales, native, blocks, view, destination, destination_stride, col0, out_col0, count, sm_count, stream);
+cudaError_t dispatch_rows(const LaunchArgs &a) {
+    switch (a.view.rows) {
+        case 1: return launch_rows<1, NATIVE>(a);
+        case 2: return launch_rows<2, NATIVE>(a);
+        case 3: return launch_rows<3, NATIVE>(a);
+        case 4: return launch_rows<4, NATIVE>(a);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -253,9 +302,10 @@ cudaError_t launch_q4_0_q8_0_gemv(const Q40Weights &weights, const uint8_t *acti
     if ((reinterpret_cast<uintptr_t>(weights.nibbles) & 15u) != 0 || (reinterpret_cast<uintptr_t>(activation) & 1u) != 0) {
         return cudaErrorInvalidValue;
     }
-    const ActivationView view{activation, rows, weights.blocks, interleave};
-    return dispatch_rows<false>(weights.nibbles, weights.scales, nullptr, weights.blocks, view, destination,
-                                destination_stride, col0, out_col0, count, sm_count, stream);
+    const LaunchArgs args{weights.nibbles, weights.scales, nullptr, weights.blocks,
+                          ActivationView{activation, rows, weights.blocks, interleave},
+                          destination, destination_stride, col0, out_col0, count, sm_count, stream};
+    return dispatch_rows<false>(args);
 }
 
 cudaError_t launch_q4_0_q8_0_gemv_native(const uint8_t *activation, uint32_t rows, uint32_t blocks,
@@ -266,9 +316,9 @@ cudaError_t launch_q4_0_q8_0_gemv_native(const uint8_t *activation, uint32_t row
     if ((reinterpret_cast<uintptr_t>(weight) & 1u) != 0 || (reinterpret_cast<uintptr_t>(activation) & 1u) != 0) {
         return cudaErrorInvalidValue;
     }
-    const ActivationView view{activation, rows, blocks, 0};
-    return dispatch_rows<true>(nullptr, nullptr, weight, blocks, view, destination, destination_stride, col0,
-                               out_col0, count, sm_count, stream);
+    const LaunchArgs args{nullptr, nullptr, weight, blocks, ActivationView{activation, rows, blocks, 0},
+                          destination, destination_stride, col0, out_col0, count, sm_count, stream};
+    return dispatch_rows<true>(args);
 }
 
 }  // namespace qpucuda

@@ -113,6 +113,52 @@ qpucuda_status qpucuda_w8a8_linear_scratch(
     size_t *quantized_stride,
     const float **row_scales);
 
+/* Size of the fixed device scratch used by qpucuda_w8a8_linear_execute_static
+ * (16 MiB, held by every GPU that loads this library until the process exits). */
+#define QPUCUDA_STATIC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+/* W8A8 linear that allocates nothing. This entry point has no counterpart in
+ * the reference; it exists for callers that cannot call cudaMalloc (or any
+ * allocating routine) when they run the operator -- code running inside an
+ * allocator callback it must not re-enter, or under a device-memory budget
+ * fixed at start-up -- and so cannot use a prepared linear, which allocates
+ * its activation scratch.
+ *
+ * Computes, on the context stream, the same result as a prepared linear:
+ *   destination[m, n] = ((float)acc[m, n] * s_a[m]) * weight_scales[n] (+ bias[n])
+ * with the activations quantized per row. The caller passes every input and
+ * output in device memory: source fp32 [rows][k] (row stride source_stride
+ * elements), weight int8 [n][weight_stride bytes] (16-byte aligned rows, the K
+ * values zero-padded up to a multiple of 16), weight_scales fp32 [n], bias fp32
+ * [n] or NULL, destination fp32 (row stride destination_stride elements).
+ *
+ * The quantized activations live in one fixed device array compiled into the
+ * library: rows * (k rounded up to 16) bytes, rounded up to 256, plus 4 * rows
+ * bytes must fit in QPUCUDA_STATIC_SCRATCH_BYTES (e.g. 1024 rows at k = 8192);
+ * larger requests return QPUCUDA_INVALID_ARGUMENT with the reason in
+ * qpucuda_context_last_error. Nothing is allocated: no cudaMalloc, cudaFree or
+ * allocating library routine is called.
+ *
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture. All calls share the one array and it keeps the
+ * last call's contents; each call rewrites every byte it later reads, so
+ * nothing needs clearing, but calls whose work overlaps on the GPU (different
+ * streams, or different contexts on one device) race on the array. */
+qpucuda_status qpucuda_w8a8_linear_execute_static(
+    qpucuda_context *context,
+    const float *source,
+    size_t source_stride,
+    uint32_t rows,
+    const int8_t *weight,
+    size_t weight_stride,
+    const float *weight_scales,
+    const float *bias,
+    uint32_t k,
+    uint32_t n,
+    float *destination,
+    size_t destination_stride);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

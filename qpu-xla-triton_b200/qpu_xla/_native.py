@@ -182,6 +182,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "qpucuda_w8a8_linear_execute_device": (_S, [_P, _P, c_size_t, c_uint32, _P, c_size_t]),
     "qpucuda_w8a8_linear_execute_prepared_device": (_S, [_P, _P, c_size_t, _P, c_uint32, _P, c_size_t]),
     "qpucuda_w8a8_linear_scratch": (_S, [_P, POINTER(c_void_p), POINTER(c_size_t), POINTER(c_void_p)]),
+    "qpucuda_w8a8_linear_execute_static": (
+        _S,
+        [_P, _P, c_size_t, c_uint32, _P, c_size_t, _P, _P, c_uint32, c_uint32, _P, c_size_t],
+    ),
     # qpucuda_q4_0.h
     "qpucuda_q4_0_linear_prepare": (_S, [_P, POINTER(Q40LinearDesc), POINTER(c_void_p)]),
     "qpucuda_q4_0_linear_destroy": (None, [_P]),

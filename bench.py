@@ -155,7 +155,6 @@ class ClockSampler:
 
 
 def run_ours(args: argparse.Namespace) -> None:
-    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -208,6 +207,12 @@ def run_ours(args: argparse.Namespace) -> None:
     torch.cuda.empty_cache()
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=cuda)
 
+    def prime() -> None:
+        """Flush L2, then hold the stream ~60 us so the host has queued the bracketed launches
+        before the start event executes (no host launch latency inside a timed bracket)."""
+        flush.zero_()
+        torch.cuda._sleep(120_000)
+
     def step() -> None:
         for p in projections:
             g = p["gather"]
@@ -240,14 +245,14 @@ def run_ours(args: argparse.Namespace) -> None:
 
     # ---- headline: K whole steps, per-step CUDA events, L2 flushed in between ----
     for _ in range(args.warmup):
-        flush.zero_()
+        prime()
         step()
     barrier()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     wall0 = time.perf_counter()
     for i in range(args.steps):
-        flush.zero_()
+        prime()
         starts[i].record(stream)
         step()
         ends[i].record(stream)
@@ -275,7 +280,7 @@ def run_ours(args: argparse.Namespace) -> None:
         reps = 10
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
         for s, e in evs:
-            flush.zero_()
+            prime()
             s.record(stream)
             gemm()
             e.record(stream)
@@ -284,7 +289,7 @@ def run_ours(args: argparse.Namespace) -> None:
     rank_gemm_ops = sum(2.0 * TOKENS * p["gather"].count * p["k"] for p in projections)
     gemm_seconds = sum(gemm_ms) * 1e-3
     achieved_tops = rank_gemm_ops / gemm_seconds / 1e12 if gemm_seconds > 0 else 0.0
-    achieved_tops = min_over = max_over_ranks(-achieved_tops) * -1 if world > 1 else achieved_tops  # slowest rank
+    achieved_tops = -max_over_ranks(-achieved_tops)  # the slowest rank's rate
 
     # ---- Q4_0 x Q8_0 decode matvec (M = 1), Q8_0 activations already on the device ----
     q4_ms = []
@@ -300,7 +305,7 @@ def run_ours(args: argparse.Namespace) -> None:
         reps = 20
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
         for s, e in evs:
-            flush.zero_()
+            prime()
             s.record(stream)
             p["q4"].forward(act, out=out[:, : g.count])
             e.record(stream)
@@ -419,7 +424,6 @@ def run_ours(args: argparse.Namespace) -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    _ = (np, min_over)
 
 
 # ---------------------------------------------------------------------------- reference (CPU)

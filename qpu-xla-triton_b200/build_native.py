@@ -36,9 +36,12 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found; the CUDA toolkit is required to build libqpucuda.so")
 
 
+Q4_0_KERNEL_SOURCES = ("q4_0_gemv.cu", "sm100_sync.cuh")
+
+
 def q4_0_source_hash() -> str:
-    """SHA-256 of the Q4_0 kernel source: the identity Q4_0 linears are prepared against."""
-    return hashlib.sha256((CSRC / "q4_0_gemv.cu").read_bytes()).hexdigest()
+    """SHA-256 of the Q4_0 kernel sources (concatenated): the identity Q4_0 linears are prepared against."""
+    return hashlib.sha256(b"".join((CSRC / name).read_bytes() for name in Q4_0_KERNEL_SOURCES)).hexdigest()
 
 
 def sources() -> list[Path]:

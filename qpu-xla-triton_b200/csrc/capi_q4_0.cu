@@ -31,7 +31,7 @@ struct qpucuda_q4_0_linear {
     uint32_t resident_column_start = 0;
     uint32_t resident_column_count = 0;
     uint8_t *d_nibbles = nullptr;     // [resident][blocks][16]
-    uint16_t *d_scales = nullptr;     // [resident][blocks]
+    uint16_t *d_scales = nullptr;     // [resident][scale_stride], zero padded
     uint8_t *d_activation = nullptr;  // [rows][blocks][34] staging
     float *d_output = nullptr;        // [rows][resident] staging
     uint8_t *h_activation = nullptr;  // pinned
@@ -82,6 +82,7 @@ Q40Weights weights_of(const qpucuda_q4_0_linear *linear) {
     weights.scales = linear->d_scales;
     weights.columns = linear->resident_column_count;
     weights.blocks = linear->blocks;
+    weights.scale_stride = q4_0_scale_stride(linear->blocks);
     return weights;
 }
 
@@ -145,12 +146,13 @@ qpucuda_status qpucuda_q4_0_linear_prepare(qpucuda_context *context, const qpucu
     linear->resident_column_count = desc->resident_column_count;
     DeviceGuard guard(context->device);
     const size_t resident_blocks = static_cast<size_t>(desc->resident_column_count) * blocks;
+    const size_t scale_bytes = static_cast<size_t>(desc->resident_column_count) * q4_0_scale_stride(linear->blocks) * 2;
     const size_t native_bytes = resident_blocks * kWeightBlockBytes;
     const size_t activation_bytes = static_cast<size_t>(kMaxRows) * blocks * kActivationBlockBytes;
     const size_t output_bytes = static_cast<size_t>(kMaxRows) * desc->resident_column_count * sizeof(float);
     uint8_t *d_native = nullptr;
     cudaError_t error = cudaMalloc(reinterpret_cast<void **>(&linear->d_nibbles), resident_blocks * 16);
-    if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_scales), resident_blocks * 2);
+    if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_scales), scale_bytes);
     if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_activation), activation_bytes);
     if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_output), output_bytes);
     if (error == cudaSuccess) error = cudaMallocHost(reinterpret_cast<void **>(&linear->h_activation), activation_bytes);
@@ -165,9 +167,11 @@ qpucuda_status qpucuda_q4_0_linear_prepare(qpucuda_context *context, const qpucu
     const uint8_t *source = static_cast<const uint8_t *>(desc->weights) +
                             static_cast<size_t>(desc->resident_column_start) * weight_row_bytes;
     error = cudaMemcpyAsync(d_native, source, native_bytes, cudaMemcpyHostToDevice, context->stream);
+    if (error == cudaSuccess) error = cudaMemsetAsync(linear->d_scales, 0, scale_bytes, context->stream);
     if (error == cudaSuccess)
-        error = launch_q4_0_repack(d_native, desc->resident_column_count, linear->blocks, linear->d_nibbles,
-                                   linear->d_scales, context->stream);
+        error = launch_q4_0_repack(d_native, desc->resident_column_count, linear->blocks,
+                                   q4_0_scale_stride(linear->blocks), linear->d_nibbles, linear->d_scales,
+                                   context->stream);
     qpucuda_status status = error == cudaSuccess ? wait_stream(context)
                                                  : cuda_fail(context, error, "stage Q4_0 weights", QPUCUDA_IO_FAILED);
     cudaFree(d_native);
@@ -243,7 +247,8 @@ qpucuda_status qpucuda_q4_0_linear_submit(qpucuda_q4_0_linear *linear, const qpu
             error = launch_q4_0_q8_0_gemv(weights_of(linear), linear->d_activation, rows,
                                           execution->activation_interleave, linear->d_output,
                                           linear->resident_column_count, local_start, local_start,
-                                          execution->column_count, context->sm_count, context->stream);
+                                          execution->column_count, context->d_error, context->sm_count,
+                                          context->stream);
         }
         if (error == cudaSuccess) {
             // Only the requested window crosses back to the host.
@@ -352,8 +357,8 @@ qpucuda_status qpucuda_q4_0_linear_execute_device(qpucuda_q4_0_linear *linear, c
     DeviceGuard guard(context->device);
     const cudaError_t error = launch_q4_0_q8_0_gemv(weights_of(linear), static_cast<const uint8_t *>(activation), rows,
                                                     0, destination, destination_stride, local_start,
-                                                    output_column_start, column_count, context->sm_count,
-                                                    context->stream);
+                                                    output_column_start, column_count, context->d_error,
+                                                    context->sm_count, context->stream);
     if (error != cudaSuccess) return cuda_fail(context, error, "launch Q4_0 linear");
     return QPUCUDA_OK;
 }
@@ -379,7 +384,7 @@ qpucuda_status qpucuda_q4_0_linear_execute_f32_device(qpucuda_q4_0_linear *linea
     if (error == cudaSuccess)
         error = launch_q4_0_q8_0_gemv(weights_of(linear), linear->d_activation, rows, 0, destination,
                                       destination_stride, local_start, output_column_start, column_count,
-                                      context->sm_count, context->stream);
+                                      context->d_error, context->sm_count, context->stream);
     if (error != cudaSuccess) return cuda_fail(context, error, "launch Q4_0 linear");
     return QPUCUDA_OK;
 }

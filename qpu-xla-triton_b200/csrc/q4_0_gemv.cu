@@ -10,28 +10,33 @@
 // followed by a warp tree, a different order from the reference's sequential
 // sum, so the result agrees to ~1e-6 relative rather than bit for bit.
 //
-// Prepared weight layout (made once at prepare, same bytes per block as the
-// native 18-byte block): nibbles [columns][blocks][16] (16-byte aligned) and
-// fp16 scales [columns][blocks]. One warp per output column (SPLIT = 2 or 4 warps for
-// long reductions, their partials added in a fixed order); lane l takes blocks
-// l, l + 32 * SPLIT, ..., so a warp reads 512 contiguous bytes of nibbles per load,
-// eight loads in flight per lane.
-// Weight codes stay packed: dp4a(nibbles & 0x0F0F0F0F, a[0..3]) and
-// dp4a((nibbles >> 4) & 0x0F0F0F0F, a[16..19]) etc., and the -8 offset is one
-// subtraction of 8 * sum(a) per block, precomputed when the activation is staged.
-// The activation (rows x K bytes) is staged once per CTA in shared memory as
-// 16-byte aligned int8 rows, fp32 block scales and block sums; CTAs are
-// persistent over columns.
+// Two kernels:
+//  * q4_0_stream_kernel (prepared weights, the operator's path). Prepared layout,
+//    made once at prepare with the same 18 bytes per block as the native format:
+//    nibbles [columns][blocks][16] and fp16 scales [columns][scale_stride]
+//    (scale_stride = blocks rounded up to 8, so every column's scales are a
+//    16-byte multiple). One persistent CTA per SM owns a contiguous column
+//    range; a producer thread streams each column's nibbles and scales into a
+//    ring of shared-memory slots with 1D TMA bulk copies (cp.async.bulk +
+//    mbarrier complete_tx), keeping ~100-160 KB per SM in flight with no register
+//    cost; consumer warps take one column each from the ring (lane l reads
+//    blocks l, l + 32, ... from shared memory) and release the slot.
+//  * q4_0_native_kernel (single-kernel entry point over native 18-byte blocks,
+//    which are only 2-byte aligned): lanes read each block as nine 16-bit loads.
+// Both keep the weight codes packed: dp4a(nibbles & 0x0F0F0F0F, a[0..3]) and
+// dp4a((nibbles >> 4) & 0x0F0F0F0F, a[16..19]) etc.; the -8 offset is one
+// subtraction of 8 * sum(a) per block, precomputed when the activation (rows x K
+// bytes, 16-byte aligned rows + fp32 block scales + block sums) is staged in
+// shared memory once per CTA.
 #include <cuda_fp16.h>
 
 #include "qpucuda_internal.h"
+#include "sm100_sync.cuh"
 
 namespace qpucuda {
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
-constexpr int kUnroll = 8;
+using namespace sm100;
 
 struct ActivationView {
     const uint8_t *base;
@@ -69,10 +74,11 @@ __device__ __forceinline__ int8_t activation_value(const ActivationView &view, c
 // Shared memory: q [rows][blocks * 32] int8, d [rows][blocks] fp32, sum8 [rows][blocks] int32.
 // One thread per (row, block): a native block is read with independent 16-bit loads (blocks
 // start on even bytes), so staging costs one round trip to L2 rather than one per block.
-__device__ __forceinline__ void stage_activation(const ActivationView &view, int8_t *q, float *d, int *sum8) {
+__device__ __forceinline__ void stage_activation(const ActivationView &view, int8_t *q, float *d, int *sum8,
+                                                 uint32_t thread, uint32_t threads) {
     const uint32_t total = view.rows * view.blocks;
     const uint32_t interleaved_rows = view.interleave == 0 ? 0 : view.rows - view.rows % 4;
-    for (uint32_t item = threadIdx.x; item < total; item += blockDim.x) {
+    for (uint32_t item = thread; item < total; item += threads) {
         const uint32_t row = item / view.blocks;
         const uint32_t block = item % view.blocks;
         const uint8_t *scale_bytes;
@@ -106,14 +112,6 @@ __device__ __forceinline__ void stage_activation(const ActivationView &view, int
     }
 }
 
-__device__ __forceinline__ uint4 load_stream_u4(const void *p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-
 __device__ __forceinline__ int block_dot(uint4 w, const int8_t *a) {
     const int4 lo = *reinterpret_cast<const int4 *>(a);       // activation values 0..15
     const int4 hi = *reinterpret_cast<const int4 *>(a + 16);  // activation values 16..31
@@ -141,102 +139,143 @@ __device__ __forceinline__ void accumulate_block(uint4 w, uint16_t w_scale_bits,
     }
 }
 
-// SPLIT warps share one column: warp part p takes blocks p*32 + lane + i*32*SPLIT, and
-// the SPLIT partial sums are added in part order through shared memory (deterministic).
-template <int ROWS, bool NATIVE, int SPLIT>
-__global__ void __launch_bounds__(kThreads) q4_0_gemv_kernel(const uint8_t *__restrict__ nibbles,
-                                                             const uint16_t *__restrict__ scales,
-                                                             const uint8_t *__restrict__ native, uint32_t blocks,
-                                                             ActivationView view, float *__restrict__ destination,
-                                                             size_t destination_stride, uint32_t col0,
-                                                             uint32_t out_col0, uint32_t count) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ float partial[kWarps][ROWS];
-    int8_t *q = reinterpret_cast<int8_t *>(smem);
-    float *d = reinterpret_cast<float *>(smem + static_cast<size_t>(ROWS) * blocks * 32);
-    int *sum8 = reinterpret_cast<int *>(d + static_cast<size_t>(ROWS) * blocks);
-    stage_activation(view, q, d, sum8);
-    __syncthreads();
-
-    constexpr uint32_t kSlots = kWarps / SPLIT;
-    constexpr uint32_t kStride = 32 * SPLIT;  // blocks between a lane's consecutive blocks
-    const uint32_t warp = threadIdx.x >> 5;
-    const uint32_t lane = threadIdx.x & 31;
-    const uint32_t part = warp % SPLIT;
-    const uint32_t slot = warp / SPLIT;
-    const uint32_t first = part * 32 + lane;
-    for (uint32_t j = blockIdx.x * kSlots + slot; j < count; j += gridDim.x * kSlots) {
-        const size_t column = col0 + j;
-        float acc[ROWS];
+template <int ROWS>
+__device__ __forceinline__ void warp_sum(float (&acc)[ROWS]) {
 #pragma unroll
-        for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
-        if constexpr (NATIVE) {
-            // Native 18-byte blocks: 2-byte aligned, read as nine 16-bit words.
-            for (uint32_t b = first; b < blocks; b += kStride) {
-                const uint16_t *src = reinterpret_cast<const uint16_t *>(native + (column * blocks + b) * 18);
-                uint4 w;
-                w.x = static_cast<uint32_t>(src[1]) | (static_cast<uint32_t>(src[2]) << 16);
-                w.y = static_cast<uint32_t>(src[3]) | (static_cast<uint32_t>(src[4]) << 16);
-                w.z = static_cast<uint32_t>(src[5]) | (static_cast<uint32_t>(src[6]) << 16);
-                w.w = static_cast<uint32_t>(src[7]) | (static_cast<uint32_t>(src[8]) << 16);
-                accumulate_block<ROWS>(w, src[0], b, blocks, q, d, sum8, acc);
-            }
-        } else {
-            const uint8_t *w_col = nibbles + column * blocks * 16;
-            const uint16_t *s_col = scales + column * blocks;
-            uint32_t b = first;
-            // Eight independent 16-byte loads in flight per lane (4 KB per warp).
-            for (; b + kStride * (kUnroll - 1) < blocks; b += kStride * kUnroll) {
-                uint4 w[kUnroll];
-                uint16_t s[kUnroll];
+    for (int r = 0; r < ROWS; ++r) {
 #pragma unroll
-                for (int u = 0; u < kUnroll; ++u) {
-                    w[u] = load_stream_u4(w_col + static_cast<size_t>(b + kStride * u) * 16);
-                    s[u] = __ldg(s_col + b + kStride * u);
-                }
-#pragma unroll
-                for (int u = 0; u < kUnroll; ++u) accumulate_block<ROWS>(w[u], s[u], b + kStride * u, blocks, q, d, sum8, acc);
-            }
-            for (; b < blocks; b += kStride) {
-                const uint4 w = load_stream_u4(w_col + static_cast<size_t>(b) * 16);
-                accumulate_block<ROWS>(w, __ldg(s_col + b), b, blocks, q, d, sum8, acc);
-            }
-        }
-#pragma unroll
-        for (int r = 0; r < ROWS; ++r) {
-#pragma unroll
-            for (int offset = 16; offset > 0; offset >>= 1) acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], offset));
-        }
-        if constexpr (SPLIT > 1) {
-            // The SPLIT warps of this slot run the same trip count, so the named barrier is safe.
-            if (lane == 0) {
-#pragma unroll
-                for (int r = 0; r < ROWS; ++r) partial[warp][r] = acc[r];
-            }
-            asm volatile("bar.sync %0, %1;" ::"r"(1 + slot), "r"(32 * SPLIT) : "memory");
-            if (part == 0 && lane < static_cast<uint32_t>(ROWS)) {
-                float value = partial[slot * SPLIT][lane];
-#pragma unroll
-                for (int p = 1; p < SPLIT; ++p) value = __fadd_rn(value, partial[slot * SPLIT + p][lane]);
-                destination[static_cast<size_t>(lane) * destination_stride + out_col0 + j] = value;
-            }
-            asm volatile("bar.sync %0, %1;" ::"r"(1 + slot), "r"(32 * SPLIT) : "memory");
-        } else if (lane < static_cast<uint32_t>(ROWS)) {
-            float value = acc[0];
-#pragma unroll
-            for (int r = 1; r < ROWS; ++r)
-                if (lane == static_cast<uint32_t>(r)) value = acc[r];
-            destination[static_cast<size_t>(lane) * destination_stride + out_col0 + j] = value;
-        }
+        for (int offset = 16; offset > 0; offset >>= 1) acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], offset));
     }
 }
 
-size_t smem_bytes(uint32_t rows, uint32_t blocks) { return static_cast<size_t>(rows) * blocks * (32 + 4 + 4); }
+template <int ROWS>
+__device__ __forceinline__ void store_rows(const float (&acc)[ROWS], uint32_t lane, float *destination,
+                                           size_t destination_stride, size_t column) {
+    if (lane < static_cast<uint32_t>(ROWS)) {
+        float value = acc[0];
+#pragma unroll
+        for (int r = 1; r < ROWS; ++r)
+            if (lane == static_cast<uint32_t>(r)) value = acc[r];
+        destination[static_cast<size_t>(lane) * destination_stride + column] = value;
+    }
+}
 
-struct LaunchArgs {
+size_t activation_bytes(uint32_t rows, uint32_t blocks) { return static_cast<size_t>(rows) * blocks * (32 + 4 + 4); }
+
+// ---- streaming kernel over the prepared layout ------------------------------------------
+
+constexpr int kMaxSlots = 32;
+constexpr size_t kSmemBudget = 200u * 1024u;
+
+struct StreamParams {
     const uint8_t *nibbles;
     const uint16_t *scales;
-    const uint8_t *native;
+    uint32_t blocks;
+    uint32_t scale_stride;  // fp16 scales per column row (blocks rounded up to 8)
+    ActivationView view;
+    float *destination;
+    size_t destination_stride;
+    uint32_t col0;      // first weight column (resident-relative)
+    uint32_t out_col0;  // destination column of weight column col0
+    uint32_t count;
+    uint32_t slots;
+    uint32_t slot_bytes;
+    uint32_t act_bytes;  // activation area, 128-aligned
+    unsigned int *error_word;
+};
+
+template <int ROWS, int CONSUMERS>
+__global__ void __launch_bounds__(32 * (CONSUMERS + 1), 1) q4_0_stream_kernel(const StreamParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t full_bar[kMaxSlots];
+    __shared__ uint64_t empty_bar[kMaxSlots];
+    __shared__ volatile int abort_flag;
+    int8_t *q = reinterpret_cast<int8_t *>(smem);
+    float *d = reinterpret_cast<float *>(smem + static_cast<size_t>(ROWS) * p.blocks * 32);
+    int *sum8 = reinterpret_cast<int *>(d + static_cast<size_t>(ROWS) * p.blocks);
+    uint8_t *ring = smem + p.act_bytes;
+
+    // This CTA's contiguous column range, balanced to within one column.
+    const uint32_t per = p.count / gridDim.x;
+    const uint32_t extra = p.count % gridDim.x;
+    const uint32_t begin = blockIdx.x * per + (blockIdx.x < extra ? blockIdx.x : extra);
+    const uint32_t columns = per + (blockIdx.x < extra ? 1u : 0u);
+    const uint32_t nibble_bytes = p.blocks * 16;
+    const uint32_t scale_bytes = p.scale_stride * 2;
+
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < p.slots; ++s) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), 1);
+        }
+        abort_flag = 0;
+        mbar_init_fence();
+    }
+    __syncthreads();
+
+    if (warp == CONSUMERS) {
+        // ---- producer: one thread streams every column of the range through the ring ----
+        if (lane == 0) {
+            bool ok = true;
+            uint32_t issued = 0;
+            for (uint32_t i = 0; i < columns; ++i) {
+                const uint32_t slot = i % p.slots;
+                const uint32_t round = i / p.slots;
+                if (round > 0 && !wait_bounded(smem_u32(&empty_bar[slot]), (round - 1) & 1u, &abort_flag, p.error_word)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t bar = smem_u32(&full_bar[slot]);
+                const size_t column = p.col0 + begin + i;
+                uint8_t *destination = ring + static_cast<size_t>(slot) * p.slot_bytes;
+                mbar_expect_tx(bar, nibble_bytes + scale_bytes);
+                bulk_load(smem_u32(destination), p.nibbles + column * nibble_bytes, nibble_bytes, bar);
+                bulk_load(smem_u32(destination + nibble_bytes), p.scales + column * p.scale_stride, scale_bytes, bar);
+                issued = i + 1;
+            }
+            if (!ok) {
+                // Abort path: let this thread's copies land before the CTA exits.
+                for (uint32_t i = issued > p.slots ? issued - p.slots : 0; i < issued; ++i) {
+                    wait_drain(smem_u32(&full_bar[i % p.slots]), (i / p.slots) & 1u);
+                }
+            }
+        }
+        __syncwarp();  // reconverge before the CTA barrier below
+    } else {
+        // ---- consumers: stage the activation, then one column per warp from the ring ----
+        stage_activation(p.view, q, d, sum8, threadIdx.x, 32 * CONSUMERS);
+        asm volatile("bar.sync 1, %0;" ::"r"(32 * CONSUMERS) : "memory");
+        for (uint32_t i = warp; i < columns; i += CONSUMERS) {
+            const uint32_t slot = i % p.slots;
+            bool ok = true;
+            if (lane == 0) ok = wait_bounded(smem_u32(&full_bar[slot]), (i / p.slots) & 1u, &abort_flag, p.error_word);
+            if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
+            const uint8_t *slot_base = ring + static_cast<size_t>(slot) * p.slot_bytes;
+            const uint4 *w = reinterpret_cast<const uint4 *>(slot_base);
+            const uint16_t *s = reinterpret_cast<const uint16_t *>(slot_base + nibble_bytes);
+            float acc[ROWS];
+#pragma unroll
+            for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
+#pragma unroll 4
+            for (uint32_t b = lane; b < p.blocks; b += 32) accumulate_block<ROWS>(w[b], s[b], b, p.blocks, q, d, sum8, acc);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[slot]));
+            warp_sum<ROWS>(acc);
+            store_rows<ROWS>(acc, lane, p.destination, p.destination_stride, p.out_col0 + begin + i);
+        }
+    }
+    __syncthreads();
+}
+
+// ---- native-block kernel (single-kernel entry point) --------------------------------------
+
+constexpr int kNativeThreads = 256;
+constexpr int kNativeWarps = kNativeThreads / 32;
+
+struct NativeParams {
+    const uint8_t *weight;  // [columns][blocks][18]
     uint32_t blocks;
     ActivationView view;
     float *destination;
@@ -244,68 +283,105 @@ struct LaunchArgs {
     uint32_t col0;
     uint32_t out_col0;
     uint32_t count;
-    int sm_count;
-    cudaStream_t stream;
 };
 
-template <int ROWS, bool NATIVE, int SPLIT>
-cudaError_t launch_split(const LaunchArgs &a) {
-    const size_t smem = smem_bytes(ROWS, a.blocks);
-    if (smem > 200u * 1024u) return cudaErrorInvalidValue;
-    auto kernel = q4_0_gemv_kernel<ROWS, NATIVE, SPLIT>;
+template <int ROWS>
+__global__ void __launch_bounds__(kNativeThreads) q4_0_native_kernel(const NativeParams p) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    int8_t *q = reinterpret_cast<int8_t *>(smem);
+    float *d = reinterpret_cast<float *>(smem + static_cast<size_t>(ROWS) * p.blocks * 32);
+    int *sum8 = reinterpret_cast<int *>(d + static_cast<size_t>(ROWS) * p.blocks);
+    stage_activation(p.view, q, d, sum8, threadIdx.x, blockDim.x);
+    __syncthreads();
+    const uint32_t lane = threadIdx.x & 31;
+    for (uint32_t j = blockIdx.x * kNativeWarps + (threadIdx.x >> 5); j < p.count; j += gridDim.x * kNativeWarps) {
+        const size_t column = p.col0 + j;
+        float acc[ROWS];
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
+        for (uint32_t b = lane; b < p.blocks; b += 32) {
+            // Native 18-byte blocks are 2-byte aligned: nine 16-bit loads.
+            const uint16_t *src = reinterpret_cast<const uint16_t *>(p.weight + (column * p.blocks + b) * 18);
+            uint4 w;
+            w.x = static_cast<uint32_t>(src[1]) | (static_cast<uint32_t>(src[2]) << 16);
+            w.y = static_cast<uint32_t>(src[3]) | (static_cast<uint32_t>(src[4]) << 16);
+            w.z = static_cast<uint32_t>(src[5]) | (static_cast<uint32_t>(src[6]) << 16);
+            w.w = static_cast<uint32_t>(src[7]) | (static_cast<uint32_t>(src[8]) << 16);
+            accumulate_block<ROWS>(w, src[0], b, p.blocks, q, d, sum8, acc);
+        }
+        warp_sum<ROWS>(acc);
+        store_rows<ROWS>(acc, lane, p.destination, p.destination_stride, p.out_col0 + j);
+    }
+}
+
+template <int ROWS, int CONSUMERS>
+cudaError_t launch_stream(StreamParams p, int sm_count, cudaStream_t stream) {
+    const size_t act = (activation_bytes(ROWS, p.blocks) + 127) & ~static_cast<size_t>(127);
+    const size_t slot = (static_cast<size_t>(p.blocks) * 16 + static_cast<size_t>(p.scale_stride) * 2 + 127) &
+                        ~static_cast<size_t>(127);
+    if (act + slot > kSmemBudget) return cudaErrorInvalidValue;
+    size_t slots = (kSmemBudget - act) / slot;
+    if (slots > static_cast<size_t>(kMaxSlots)) slots = kMaxSlots;
+    const size_t smem = act + slots * slot;
+    auto kernel = q4_0_stream_kernel<ROWS, CONSUMERS>;
+    cudaError_t error = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (error != cudaSuccess) return error;
+    p.slots = static_cast<uint32_t>(slots);
+    p.slot_bytes = static_cast<uint32_t>(slot);
+    p.act_bytes = static_cast<uint32_t>(act);
+    const uint32_t grid = p.count < static_cast<uint32_t>(sm_count) ? p.count : static_cast<uint32_t>(sm_count);
+    kernel<<<grid, 32 * (CONSUMERS + 1), smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+template <int ROWS>
+cudaError_t launch_native(const NativeParams &p, int sm_count, cudaStream_t stream) {
+    const size_t smem = activation_bytes(ROWS, p.blocks);
+    if (smem > kSmemBudget) return cudaErrorInvalidValue;
+    auto kernel = q4_0_native_kernel<ROWS>;
     if (smem > 48u * 1024u) {
         const cudaError_t error =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (error != cudaSuccess) return error;
     }
-    // Persistent CTAs filling the SM's real residency (each stages the activation once); the
-    // grid is balanced so every column slot runs the same number of rounds (no straggling tail).
-    int per_sm = 0;
-    cudaError_t error = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
-    if (error != cudaSuccess) return error;
-    if (per_sm < 1) per_sm = 1;
-    constexpr uint32_t kSlots = kWarps / SPLIT;
-    const uint64_t capacity = static_cast<uint64_t>(a.sm_count) * static_cast<uint64_t>(per_sm);
-    const uint64_t rounds = (a.count + capacity * kSlots - 1) / (capacity * kSlots);
-    const uint32_t grid = static_cast<uint32_t>((a.count + kSlots * rounds - 1) / (kSlots * rounds));
-    kernel<<<grid, kThreads, smem, a.stream>>>(a.nibbles, a.scales, a.native, a.blocks, a.view, a.destination,
-                                               a.destination_stride, a.col0, a.out_col0, a.count);
+    uint32_t grid = (p.count + kNativeWarps - 1) / kNativeWarps;
+    const uint32_t cap = static_cast<uint32_t>(sm_count) * 4u;
+    if (grid > cap) grid = cap;
+    kernel<<<grid, kNativeThreads, smem, stream>>>(p);
     return cudaGetLastError();
-}
-
-template <int ROWS, bool NATIVE>
-cudaError_t launch_rows(const LaunchArgs &a) {
-    // Columns with many blocks are split over 2 or 4 warps so there are enough independent
-    // units to keep every SM busy without a long last round.
-    if (a.blocks >= 2048) return launch_split<ROWS, NATIVE, 4>(a);
-    if (a.blocks >= 512) return launch_split<ROWS, NATIVE, 2>(a);
-    return launch_split<ROWS, NATIVE, 1>(a);
-}
-
-template <bool NATIVE>
-cudaError_t dispatch_rows(const LaunchArgs &a) {
-    switch (a.view.rows) {
-        case 1: return launch_rows<1, NATIVE>(a);
-        case 2: return launch_rows<2, NATIVE>(a);
-        case 3: return launch_rows<3, NATIVE>(a);
-        case 4: return launch_rows<4, NATIVE>(a);
-        default: return cudaErrorInvalidValue;
-    }
 }
 
 }  // namespace
 
 cudaError_t launch_q4_0_q8_0_gemv(const Q40Weights &weights, const uint8_t *activation, uint32_t rows,
                                   uint32_t interleave, float *destination, size_t destination_stride, uint32_t col0,
-                                  uint32_t out_col0, uint32_t count, int sm_count, cudaStream_t stream) {
+                                  uint32_t out_col0, uint32_t count, unsigned int *error_word, int sm_count,
+                                  cudaStream_t stream) {
     if (count == 0 || rows == 0) return cudaSuccess;
-    if ((reinterpret_cast<uintptr_t>(weights.nibbles) & 15u) != 0 || (reinterpret_cast<uintptr_t>(activation) & 1u) != 0) {
+    if ((reinterpret_cast<uintptr_t>(weights.nibbles) & 15u) != 0 || (reinterpret_cast<uintptr_t>(weights.scales) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(activation) & 1u) != 0 || weights.scale_stride % 8 != 0 ||
+        weights.scale_stride < weights.blocks) {
         return cudaErrorInvalidValue;
     }
-    const LaunchArgs args{weights.nibbles, weights.scales, nullptr, weights.blocks,
-                          ActivationView{activation, rows, weights.blocks, interleave},
-                          destination, destination_stride, col0, out_col0, count, sm_count, stream};
-    return dispatch_rows<false>(args);
+    StreamParams p{};
+    p.nibbles = weights.nibbles;
+    p.scales = weights.scales;
+    p.blocks = weights.blocks;
+    p.scale_stride = weights.scale_stride;
+    p.view = ActivationView{activation, rows, weights.blocks, interleave};
+    p.destination = destination;
+    p.destination_stride = destination_stride;
+    p.col0 = col0;
+    p.out_col0 = out_col0;
+    p.count = count;
+    p.error_word = error_word;
+    switch (rows) {
+        case 1: return launch_stream<1, 8>(p, sm_count, stream);
+        case 2: return launch_stream<2, 8>(p, sm_count, stream);
+        case 3: return launch_stream<3, 16>(p, sm_count, stream);
+        case 4: return launch_stream<4, 16>(p, sm_count, stream);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 cudaError_t launch_q4_0_q8_0_gemv_native(const uint8_t *activation, uint32_t rows, uint32_t blocks,
@@ -316,9 +392,15 @@ cudaError_t launch_q4_0_q8_0_gemv_native(const uint8_t *activation, uint32_t row
     if ((reinterpret_cast<uintptr_t>(weight) & 1u) != 0 || (reinterpret_cast<uintptr_t>(activation) & 1u) != 0) {
         return cudaErrorInvalidValue;
     }
-    const LaunchArgs args{nullptr, nullptr, weight, blocks, ActivationView{activation, rows, blocks, 0},
-                          destination, destination_stride, col0, out_col0, count, sm_count, stream};
-    return dispatch_rows<true>(args);
+    const NativeParams p{weight, blocks, ActivationView{activation, rows, blocks, 0}, destination, destination_stride,
+                         col0, out_col0, count};
+    switch (rows) {
+        case 1: return launch_native<1>(p, sm_count, stream);
+        case 2: return launch_native<2>(p, sm_count, stream);
+        case 3: return launch_native<3>(p, sm_count, stream);
+        case 4: return launch_native<4>(p, sm_count, stream);
+        default: return cudaErrorInvalidValue;
+    }
 }
 
 }  // namespace qpucuda

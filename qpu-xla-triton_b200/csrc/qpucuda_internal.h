@@ -120,20 +120,23 @@ cudaError_t launch_w8a8_dequantize(const int32_t *acc, size_t acc_stride, uint32
 // Q4_0 x Q8_0 over the prepared (repacked) weight layout.
 struct Q40Weights {
     const uint8_t *nibbles = nullptr;  // [columns][blocks][16]
-    const uint16_t *scales = nullptr;  // [columns][blocks] fp16 bits
+    const uint16_t *scales = nullptr;  // [columns][scale_stride] fp16 bits, zero padded
     uint32_t columns = 0;
     uint32_t blocks = 0;
+    uint32_t scale_stride = 0;  // blocks rounded up to a multiple of 8 (16-byte rows)
 };
+inline uint32_t q4_0_scale_stride(uint32_t blocks) { return (blocks + 7u) & ~7u; }
 // activation: native Q8_0 rows [rows][blocks][34] (interleave 0) or CPU_REPACK
 // block_q8_0x4 groups (interleave 4/8). Writes destination[r * stride + out_col0 + j]
 // for weight columns col0 + j, j < count.
 cudaError_t launch_q4_0_q8_0_gemv(const Q40Weights &weights, const uint8_t *activation, uint32_t rows,
                                   uint32_t interleave, float *destination, size_t destination_stride,
-                                  uint32_t col0, uint32_t out_col0, uint32_t count, int sm_count,
-                                  cudaStream_t stream);
-// Native 18-byte blocks [columns][blocks][18] -> prepared layout.
-cudaError_t launch_q4_0_repack(const uint8_t *native, uint32_t columns, uint32_t blocks, uint8_t *nibbles,
-                               uint16_t *scales, cudaStream_t stream);
+                                  uint32_t col0, uint32_t out_col0, uint32_t count, unsigned int *error_word,
+                                  int sm_count, cudaStream_t stream);
+// Native 18-byte blocks [columns][blocks][18] -> prepared layout (scales rows of scale_stride,
+// the padding must be zeroed beforehand).
+cudaError_t launch_q4_0_repack(const uint8_t *native, uint32_t columns, uint32_t blocks, uint32_t scale_stride,
+                               uint8_t *nibbles, uint16_t *scales, cudaStream_t stream);
 // Reads native blocks directly (no prepared layout), for the single-kernel entry point.
 cudaError_t launch_q4_0_q8_0_gemv_native(const uint8_t *activation, uint32_t rows, uint32_t blocks,
                                          const uint8_t *weight, float *destination, size_t destination_stride,

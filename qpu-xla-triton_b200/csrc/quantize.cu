@@ -186,8 +186,9 @@ __global__ void __launch_bounds__(256) quantize_q4_0_kernel(const float *__restr
     }
 }
 
-// Native [columns][blocks][18] -> nibbles [columns][blocks][16] + scales [columns][blocks].
+// Native [columns][blocks][18] -> nibbles [columns][blocks][16] + scales [columns][scale_stride].
 __global__ void __launch_bounds__(256) q4_0_repack_kernel(const uint8_t *__restrict__ native, size_t total_blocks,
+                                                          uint32_t blocks, uint32_t scale_stride,
                                                           uint8_t *__restrict__ nibbles,
                                                           uint16_t *__restrict__ scales) {
     for (size_t block = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; block < total_blocks;
@@ -199,7 +200,7 @@ __global__ void __launch_bounds__(256) q4_0_repack_kernel(const uint8_t *__restr
             words[i] = static_cast<uint32_t>(source[1 + 2 * i]) | (static_cast<uint32_t>(source[2 + 2 * i]) << 16);
         }
         reinterpret_cast<uint4 *>(nibbles)[block] = make_uint4(words[0], words[1], words[2], words[3]);
-        scales[block] = source[0];
+        scales[(block / blocks) * scale_stride + block % blocks] = source[0];
     }
 }
 
@@ -248,11 +249,11 @@ cudaError_t launch_quantize_q4_0(const float *x, size_t x_stride, uint32_t rows,
     return cudaGetLastError();
 }
 
-cudaError_t launch_q4_0_repack(const uint8_t *native, uint32_t columns, uint32_t blocks, uint8_t *nibbles,
-                               uint16_t *scales, cudaStream_t stream) {
+cudaError_t launch_q4_0_repack(const uint8_t *native, uint32_t columns, uint32_t blocks, uint32_t scale_stride,
+                               uint8_t *nibbles, uint16_t *scales, cudaStream_t stream) {
     const size_t total = static_cast<size_t>(columns) * blocks;
     if (total == 0) return cudaSuccess;
-    q4_0_repack_kernel<<<grid_for(total, 256), 256, 0, stream>>>(native, total, nibbles, scales);
+    q4_0_repack_kernel<<<grid_for(total, 256), 256, 0, stream>>>(native, total, blocks, scale_stride, nibbles, scales);
     return cudaGetLastError();
 }
 

@@ -25,6 +25,7 @@
 // kKernelWaitTimeout in the error word, drains its own copies and MMAs with
 // bounded waits, frees TMEM and returns. No multicast is used anywhere.
 #include "qpucuda_internal.h"
+#include "sm100_sync.cuh"
 
 namespace qpucuda {
 namespace {
@@ -74,78 +75,12 @@ struct GemmParams {
     unsigned int *error_word;
 };
 
-__device__ __forceinline__ uint32_t smem_u32(const void *pointer) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(pointer));
-}
+using namespace sm100;
 
-__device__ __forceinline__ uint64_t globaltimer() {
-    uint64_t value;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(value));
-    return value;
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return done != 0;
-}
-
-// Bounded wait: false when the CTA was aborted or the wait exceeded kKernelWaitLimitNs
-// (the latter records the error and aborts the CTA).
+// Bounded wait on this CTA's abort flag (see sm100_sync.cuh).
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, Control *control,
                                              unsigned int *error_word) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t start = globaltimer();
-    for (uint32_t spin = 1;; ++spin) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((spin & 63u) == 0) {
-            if (control->abort_flag != 0) return false;
-            if (globaltimer() - start > kKernelWaitLimitNs) {
-                control->abort_flag = 1;
-                atomicExch(error_word, static_cast<unsigned int>(kKernelWaitTimeout));
-                return false;
-            }
-        }
-    }
-}
-
-// Drain wait: bounded, ignores the abort flag (used only on the abort path).
-__device__ __forceinline__ void wait_drain(uint32_t bar, uint32_t parity) {
-    const uint64_t start = globaltimer();
-    while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer() - start > kKernelWaitLimitNs) return;
-    }
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t destination, const CUtensorMap *map, uint32_t bar, int x,
-                                            int y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
-        "[%2];" ::"r"(destination),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
-        : "memory");
-}
-
-__device__ __forceinline__ void prefetch_tensor_map(const CUtensorMap *map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+    return sm100::wait_bounded(bar, parity, &control->abort_flag, error_word);
 }
 
 // Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle
@@ -270,6 +205,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
         }
+        __syncwarp();  // reconverge before the CTA barrier at the end
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         uint32_t stage = 0, phase = 0, local_tile = 0;
@@ -314,6 +250,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             umma_commit(smem_u32(&control->drain));
             wait_drain(smem_u32(&control->drain), 0);
         }
+        __syncwarp();
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         const uint32_t quarter = warp & 3u;  // TMEM lanes this warp may access

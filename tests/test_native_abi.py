@@ -84,5 +84,6 @@ def test_injected_device_open_failure_is_reported_before_any_cuda_call() -> None
 def test_q4_0_kernel_source_hash_is_the_sha256_of_the_kernel_source() -> None:
     import hashlib
 
-    source = REPO / "qpu-xla-triton_b200" / "csrc" / "q4_0_gemv.cu"
-    assert _native.load().qpucuda_q4_0_kernel_source_hash().decode() == hashlib.sha256(source.read_bytes()).hexdigest()
+    csrc = REPO / "qpu-xla-triton_b200" / "csrc"
+    digest = hashlib.sha256((csrc / "q4_0_gemv.cu").read_bytes() + (csrc / "sm100_sync.cuh").read_bytes()).hexdigest()
+    assert _native.load().qpucuda_q4_0_kernel_source_hash().decode() == digest

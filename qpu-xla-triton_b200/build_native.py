@@ -36,7 +36,7 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found; the CUDA toolkit is required to build libqpucuda.so")
 
 
-Q4_0_KERNEL_SOURCES = ("q4_0_gemv.cu", "sm100_sync.cuh")
+Q4_0_KERNEL_SOURCES = ("q4_0_gemv.cu",)
 
 
 def q4_0_source_hash() -> str:

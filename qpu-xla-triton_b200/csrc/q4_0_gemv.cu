@@ -11,16 +11,14 @@
 // sum, so the result agrees to ~1e-6 relative rather than bit for bit.
 //
 // Two kernels:
-//  * q4_0_stream_kernel (prepared weights, the operator's path). Prepared layout,
+//  * q4_0_direct_kernel (prepared weights, the operator's path). Prepared layout,
 //    made once at prepare with the same 18 bytes per block as the native format:
 //    nibbles [columns][blocks][16] and fp16 scales [columns][scale_stride]
-//    (scale_stride = blocks rounded up to 8, so every column's scales are a
-//    16-byte multiple). One persistent CTA per SM owns a contiguous column
-//    range; a producer thread streams each column's nibbles and scales into a
-//    ring of shared-memory slots with 1D TMA bulk copies (cp.async.bulk +
-//    mbarrier complete_tx), keeping ~100-160 KB per SM in flight with no register
-//    cost; consumer warps take one column each from the ring (lane l reads
-//    blocks l, l + 32, ... from shared memory) and release the slot.
+//    (scale_stride = blocks rounded up to 8). One warp per output column (2 or 4
+//    warps for long reductions, partials added in a fixed order); lane l takes
+//    blocks l, l + 32, ..., a warp reads 512 contiguous bytes per 16-byte load,
+//    eight loads in flight per lane; persistent CTAs sized from the occupancy
+//    API with a balanced number of rounds.
 //  * q4_0_native_kernel (single-kernel entry point over native 18-byte blocks,
 //    which are only 2-byte aligned): lanes read each block as nine 16-bit loads.
 // Both keep the weight codes packed: dp4a(nibbles & 0x0F0F0F0F, a[0..3]) and
@@ -31,12 +29,10 @@
 #include <cuda_fp16.h>
 
 #include "qpucuda_internal.h"
-#include "sm100_sync.cuh"
 
 namespace qpucuda {
 namespace {
 
-using namespace sm100;
 
 struct ActivationView {
     const uint8_t *base;
@@ -162,111 +158,97 @@ __device__ __forceinline__ void store_rows(const float (&acc)[ROWS], uint32_t la
 
 size_t activation_bytes(uint32_t rows, uint32_t blocks) { return static_cast<size_t>(rows) * blocks * (32 + 4 + 4); }
 
-// ---- streaming kernel over the prepared layout ------------------------------------------
+// ---- direct-load kernel over the prepared layout -------------------------------------------
 
-constexpr int kMaxSlots = 32;
 constexpr size_t kSmemBudget = 200u * 1024u;
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kUnroll = 8;
 
-struct StreamParams {
+__device__ __forceinline__ uint4 load_stream_u4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+struct DirectParams {
     const uint8_t *nibbles;
     const uint16_t *scales;
     uint32_t blocks;
-    uint32_t scale_stride;  // fp16 scales per column row (blocks rounded up to 8)
+    uint32_t scale_stride;
     ActivationView view;
     float *destination;
     size_t destination_stride;
     uint32_t col0;      // first weight column (resident-relative)
     uint32_t out_col0;  // destination column of weight column col0
     uint32_t count;
-    uint32_t slots;
-    uint32_t slot_bytes;
-    uint32_t act_bytes;  // activation area, 128-aligned
-    unsigned int *error_word;
 };
 
-template <int ROWS, int CONSUMERS>
-__global__ void __launch_bounds__(32 * (CONSUMERS + 1), 1) q4_0_stream_kernel(const StreamParams p) {
+// One warp per column; SPLIT warps share a column for long reductions: warp part p takes
+// blocks p*32 + lane + i*32*SPLIT and the SPLIT partial sums are added in part order
+// through shared memory (deterministic). Eight independent 16-byte loads per lane are in
+// flight before any of them is consumed.
+template <int ROWS, int SPLIT>
+__global__ void __launch_bounds__(kThreads) q4_0_direct_kernel(const DirectParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t full_bar[kMaxSlots];
-    __shared__ uint64_t empty_bar[kMaxSlots];
-    __shared__ volatile int abort_flag;
+    __shared__ float partial[kWarps][ROWS];
     int8_t *q = reinterpret_cast<int8_t *>(smem);
     float *d = reinterpret_cast<float *>(smem + static_cast<size_t>(ROWS) * p.blocks * 32);
     int *sum8 = reinterpret_cast<int *>(d + static_cast<size_t>(ROWS) * p.blocks);
-    uint8_t *ring = smem + p.act_bytes;
+    stage_activation(p.view, q, d, sum8, threadIdx.x, blockDim.x);
+    __syncthreads();
 
-    // This CTA's contiguous column range, balanced to within one column.
-    const uint32_t per = p.count / gridDim.x;
-    const uint32_t extra = p.count % gridDim.x;
-    const uint32_t begin = blockIdx.x * per + (blockIdx.x < extra ? blockIdx.x : extra);
-    const uint32_t columns = per + (blockIdx.x < extra ? 1u : 0u);
-    const uint32_t nibble_bytes = p.blocks * 16;
-    const uint32_t scale_bytes = p.scale_stride * 2;
-
+    constexpr uint32_t kSlots = kWarps / SPLIT;
+    constexpr uint32_t kStride = 32 * SPLIT;  // blocks between a lane's consecutive blocks
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < p.slots; ++s) {
-            mbar_init(smem_u32(&full_bar[s]), 1);
-            mbar_init(smem_u32(&empty_bar[s]), 1);
-        }
-        abort_flag = 0;
-        mbar_init_fence();
-    }
-    __syncthreads();
-
-    if (warp == CONSUMERS) {
-        // ---- producer: one thread streams every column of the range through the ring ----
-        if (lane == 0) {
-            bool ok = true;
-            uint32_t issued = 0;
-            for (uint32_t i = 0; i < columns; ++i) {
-                const uint32_t slot = i % p.slots;
-                const uint32_t round = i / p.slots;
-                if (round > 0 && !wait_bounded(smem_u32(&empty_bar[slot]), (round - 1) & 1u, &abort_flag, p.error_word)) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t bar = smem_u32(&full_bar[slot]);
-                const size_t column = p.col0 + begin + i;
-                uint8_t *destination = ring + static_cast<size_t>(slot) * p.slot_bytes;
-                mbar_expect_tx(bar, nibble_bytes + scale_bytes);
-                bulk_load(smem_u32(destination), p.nibbles + column * nibble_bytes, nibble_bytes, bar);
-                bulk_load(smem_u32(destination + nibble_bytes), p.scales + column * p.scale_stride, scale_bytes, bar);
-                issued = i + 1;
-            }
-            if (!ok) {
-                // Abort path: let this thread's copies land before the CTA exits.
-                for (uint32_t i = issued > p.slots ? issued - p.slots : 0; i < issued; ++i) {
-                    wait_drain(smem_u32(&full_bar[i % p.slots]), (i / p.slots) & 1u);
-                }
-            }
-        }
-        __syncwarp();  // reconverge before the CTA barrier below
-    } else {
-        // ---- consumers: stage the activation, then one column per warp from the ring ----
-        stage_activation(p.view, q, d, sum8, threadIdx.x, 32 * CONSUMERS);
-        asm volatile("bar.sync 1, %0;" ::"r"(32 * CONSUMERS) : "memory");
-        for (uint32_t i = warp; i < columns; i += CONSUMERS) {
-            const uint32_t slot = i % p.slots;
-            bool ok = true;
-            if (lane == 0) ok = wait_bounded(smem_u32(&full_bar[slot]), (i / p.slots) & 1u, &abort_flag, p.error_word);
-            if (__shfl_sync(0xffffffffu, ok ? 1 : 0, 0) == 0) break;
-            const uint8_t *slot_base = ring + static_cast<size_t>(slot) * p.slot_bytes;
-            const uint4 *w = reinterpret_cast<const uint4 *>(slot_base);
-            const uint16_t *s = reinterpret_cast<const uint16_t *>(slot_base + nibble_bytes);
-            float acc[ROWS];
+    const uint32_t part = warp % SPLIT;
+    const uint32_t slot = warp / SPLIT;
+    const uint32_t first = part * 32 + lane;
+    for (uint32_t j = blockIdx.x * kSlots + slot; j < p.count; j += gridDim.x * kSlots) {
+        const size_t column = p.col0 + j;
+        const uint8_t *w_col = p.nibbles + column * p.blocks * 16;
+        const uint16_t *s_col = p.scales + column * p.scale_stride;
+        float acc[ROWS];
 #pragma unroll
-            for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
-#pragma unroll 4
-            for (uint32_t b = lane; b < p.blocks; b += 32) accumulate_block<ROWS>(w[b], s[b], b, p.blocks, q, d, sum8, acc);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&empty_bar[slot]));
-            warp_sum<ROWS>(acc);
-            store_rows<ROWS>(acc, lane, p.destination, p.destination_stride, p.out_col0 + begin + i);
+        for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
+        uint32_t b = first;
+        for (; b + kStride * (kUnroll - 1) < p.blocks; b += kStride * kUnroll) {
+            uint4 w[kUnroll];
+            uint16_t s[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                w[u] = load_stream_u4(w_col + static_cast<size_t>(b + kStride * u) * 16);
+                s[u] = __ldg(s_col + b + kStride * u);
+            }
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) accumulate_block<ROWS>(w[u], s[u], b + kStride * u, p.blocks, q, d, sum8, acc);
+        }
+        for (; b < p.blocks; b += kStride) {
+            accumulate_block<ROWS>(load_stream_u4(w_col + static_cast<size_t>(b) * 16), __ldg(s_col + b), b, p.blocks, q, d,
+                                   sum8, acc);
+        }
+        warp_sum<ROWS>(acc);
+        if constexpr (SPLIT > 1) {
+            // The SPLIT warps of this slot run the same trip count, so the named barrier is safe.
+            if (lane == 0) {
+#pragma unroll
+                for (int r = 0; r < ROWS; ++r) partial[warp][r] = acc[r];
+            }
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + slot), "r"(32 * SPLIT) : "memory");
+            if (part == 0 && lane < static_cast<uint32_t>(ROWS)) {
+                float value = partial[slot * SPLIT][lane];
+#pragma unroll
+                for (int q_part = 1; q_part < SPLIT; ++q_part) value = __fadd_rn(value, partial[slot * SPLIT + q_part][lane]);
+                p.destination[static_cast<size_t>(lane) * p.destination_stride + p.out_col0 + j] = value;
+            }
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + slot), "r"(32 * SPLIT) : "memory");
+        } else {
+            store_rows<ROWS>(acc, lane, p.destination, p.destination_stride, p.out_col0 + j);
         }
     }
-    __syncthreads();
 }
 
 // ---- native-block kernel (single-kernel entry point) --------------------------------------
@@ -314,24 +296,37 @@ __global__ void __launch_bounds__(kNativeThreads) q4_0_native_kernel(const Nativ
     }
 }
 
-template <int ROWS, int CONSUMERS>
-cudaError_t launch_stream(StreamParams p, int sm_count, cudaStream_t stream) {
-    const size_t act = (activation_bytes(ROWS, p.blocks) + 127) & ~static_cast<size_t>(127);
-    const size_t slot = (static_cast<size_t>(p.blocks) * 16 + static_cast<size_t>(p.scale_stride) * 2 + 127) &
-                        ~static_cast<size_t>(127);
-    if (act + slot > kSmemBudget) return cudaErrorInvalidValue;
-    size_t slots = (kSmemBudget - act) / slot;
-    if (slots > static_cast<size_t>(kMaxSlots)) slots = kMaxSlots;
-    const size_t smem = act + slots * slot;
-    auto kernel = q4_0_stream_kernel<ROWS, CONSUMERS>;
-    cudaError_t error = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+template <int ROWS, int SPLIT>
+cudaError_t launch_direct(const DirectParams &p, int sm_count, cudaStream_t stream) {
+    const size_t smem = activation_bytes(ROWS, p.blocks);
+    if (smem > kSmemBudget) return cudaErrorInvalidValue;
+    auto kernel = q4_0_direct_kernel<ROWS, SPLIT>;
+    if (smem > 48u * 1024u) {
+        const cudaError_t error =
+            cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (error != cudaSuccess) return error;
+    }
+    // Persistent CTAs filling the SM's real residency (each stages the activation once); the
+    // grid is balanced so every column slot runs the same number of rounds (no straggling tail).
+    int per_sm = 0;
+    const cudaError_t error = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
     if (error != cudaSuccess) return error;
-    p.slots = static_cast<uint32_t>(slots);
-    p.slot_bytes = static_cast<uint32_t>(slot);
-    p.act_bytes = static_cast<uint32_t>(act);
-    const uint32_t grid = p.count < static_cast<uint32_t>(sm_count) ? p.count : static_cast<uint32_t>(sm_count);
-    kernel<<<grid, 32 * (CONSUMERS + 1), smem, stream>>>(p);
+    if (per_sm < 1) per_sm = 1;
+    constexpr uint32_t kSlots = kWarps / SPLIT;
+    const uint64_t capacity = static_cast<uint64_t>(sm_count) * static_cast<uint64_t>(per_sm);
+    const uint64_t rounds = (p.count + capacity * kSlots - 1) / (capacity * kSlots);
+    const uint32_t grid = static_cast<uint32_t>((p.count + kSlots * rounds - 1) / (kSlots * rounds));
+    kernel<<<grid, kThreads, smem, stream>>>(p);
     return cudaGetLastError();
+}
+
+template <int ROWS>
+cudaError_t launch_rows(const DirectParams &p, int sm_count, cudaStream_t stream) {
+    // Columns with many blocks are split over 2 or 4 warps so there are enough independent
+    // units to keep every SM busy without a long last round.
+    if (p.blocks >= 2048) return launch_direct<ROWS, 4>(p, sm_count, stream);
+    if (p.blocks >= 512) return launch_direct<ROWS, 2>(p, sm_count, stream);
+    return launch_direct<ROWS, 1>(p, sm_count, stream);
 }
 
 template <int ROWS>
@@ -363,7 +358,7 @@ cudaError_t launch_q4_0_q8_0_gemv(const Q40Weights &weights, const uint8_t *acti
         weights.scale_stride < weights.blocks) {
         return cudaErrorInvalidValue;
     }
-    StreamParams p{};
+    DirectParams p{};
     p.nibbles = weights.nibbles;
     p.scales = weights.scales;
     p.blocks = weights.blocks;
@@ -374,12 +369,12 @@ cudaError_t launch_q4_0_q8_0_gemv(const Q40Weights &weights, const uint8_t *acti
     p.col0 = col0;
     p.out_col0 = out_col0;
     p.count = count;
-    p.error_word = error_word;
+    (void)error_word;  // the direct kernel has no barrier waits to bound
     switch (rows) {
-        case 1: return launch_stream<1, 8>(p, sm_count, stream);
-        case 2: return launch_stream<2, 8>(p, sm_count, stream);
-        case 3: return launch_stream<3, 16>(p, sm_count, stream);
-        case 4: return launch_stream<4, 16>(p, sm_count, stream);
+        case 1: return launch_rows<1>(p, sm_count, stream);
+        case 2: return launch_rows<2>(p, sm_count, stream);
+        case 3: return launch_rows<3>(p, sm_count, stream);
+        case 4: return launch_rows<4>(p, sm_count, stream);
         default: return cudaErrorInvalidValue;
     }
 }

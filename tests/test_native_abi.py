@@ -85,5 +85,5 @@ def test_q4_0_kernel_source_hash_is_the_sha256_of_the_kernel_source() -> None:
     import hashlib
 
     csrc = REPO / "qpu-xla-triton_b200" / "csrc"
-    digest = hashlib.sha256((csrc / "q4_0_gemv.cu").read_bytes() + (csrc / "sm100_sync.cuh").read_bytes()).hexdigest()
+    digest = hashlib.sha256((csrc / "q4_0_gemv.cu").read_bytes()).hexdigest()
     assert _native.load().qpucuda_q4_0_kernel_source_hash().decode() == digest

@@ -12,8 +12,11 @@ inputs unsplit.
 
 One step = for each projection: quantize the fp32 rows (int8 kernel), tcgen05
 int8 GEMM with the fused dequant epilogue on the rank's column shard, and (N > 1)
-the all-gather of the fp32 outputs. L2 is flushed (256 MiB write) between timed
-steps, outside the per-step CUDA-event brackets; inputs also exceed L2.
+the all-gather of the fp32 outputs. L2 is flushed between timed steps, outside the
+per-step CUDA-event brackets: a 256 MiB write, then a 256 MiB read of a second
+buffer, so the timed kernels start on a cache of clean lines (as after the
+previous layer's weight stream) rather than paying the write-back of the flush's
+own dirty lines; inputs also exceed L2.
 
 ``python bench.py [--gpus N --steps K --warmup W]``; for N > 1 run under
 ``torch.distributed.run`` (one rank per GPU). ``--impl reference`` times the
@@ -206,11 +209,14 @@ def run_ours(args: argparse.Namespace) -> None:
         del weight, values, scales, q4_blocks
     torch.cuda.empty_cache()
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=cuda)
+    flush_clean = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=cuda)
 
     def prime() -> None:
-        """Flush L2, then hold the stream ~60 us so the host has queued the bracketed launches
+        """Flush L2 (write one buffer larger than L2, then read another so the lines left are
+        clean), then hold the stream ~60 us so the host has queued the bracketed launches
         before the start event executes (no host launch latency inside a timed bracket)."""
         flush.zero_()
+        flush_clean.sum()
         torch.cuda._sleep(120_000)
 
     def step() -> None:
@@ -376,7 +382,7 @@ def run_ours(args: argparse.Namespace) -> None:
             "tokens": TOKENS,
             "projections": [f"{name} {k}->{n}" for name, k, n in shapes()],
             "parallelism": f"output-channel split x{world}" + (" + NCCL all-gather" if world > 1 else ""),
-            "l2": "flushed between timed steps (256 MiB write, outside the CUDA-event brackets); inputs exceed L2",
+            "l2": "flushed between timed steps (256 MiB write, then 256 MiB read of a second buffer; outside the CUDA-event brackets); inputs exceed L2",
             "timing": "per-step CUDA events on the launching stream, summed over K steps, max over ranks",
             "wall_s_timed_loop": round(wall, 4),
         },

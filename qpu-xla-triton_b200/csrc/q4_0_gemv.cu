@@ -14,18 +14,16 @@
 //  * q4_0_direct_kernel (prepared weights, the operator's path). Prepared layout,
 //    made once at prepare with the same 18 bytes per block as the native format:
 //    nibbles [columns][blocks][16] and fp16 scales [columns][scale_stride]
-//    (scale_stride = blocks rounded up to 8). One warp per output column (2 or 4
-//    warps for long reductions, partials added in a fixed order); lane l takes
-//    blocks l, l + 32, ..., a warp reads 512 contiguous bytes per 16-byte load,
-//    eight loads in flight per lane; persistent CTAs sized from the occupancy
-//    API with a balanced number of rounds.
+//    (scale_stride = blocks rounded up to 8). A warp owns two adjacent columns; lane l
+//    takes blocks l, l + 32, ..., so a warp reads 512 contiguous bytes of each column per
+//    16-byte load, with eight such loads in flight per lane; persistent CTAs sized from the
+//    occupancy API with a balanced number of rounds.
 //  * q4_0_native_kernel (single-kernel entry point over native 18-byte blocks,
 //    which are only 2-byte aligned): lanes read each block as nine 16-bit loads.
 // Both keep the weight codes packed: dp4a(nibbles & 0x0F0F0F0F, a[0..3]) and
-// dp4a((nibbles >> 4) & 0x0F0F0F0F, a[16..19]) etc.; the -8 offset is one
-// subtraction of 8 * sum(a) per block, precomputed when the activation (rows x K
-// bytes, 16-byte aligned rows + fp32 block scales + block sums) is staged in
-// shared memory once per CTA.
+// dp4a((nibbles >> 4) & 0x0F0F0F0F, a[16..19]) etc.; the -8 offset seeds each block's
+// dp4a chain with -8 * sum(a), precomputed when the activation (rows x K bytes + fp32
+// block scales + block sums) is staged in shared memory once per CTA.
 #include <cuda_fp16.h>
 
 #include "qpucuda_internal.h"
@@ -67,51 +65,84 @@ __device__ __forceinline__ int8_t activation_value(const ActivationView &view, c
     return static_cast<int8_t>(values[(index / il) * 4 * il + (row % 4) * il + index % il]);
 }
 
-// Shared memory: q [rows][blocks * 32] int8, d [rows][blocks] fp32, sum8 [rows][blocks] int32.
-// One thread per (row, block): a native block is read with independent 16-bit loads (blocks
-// start on even bytes), so staging costs one round trip to L2 rather than one per block.
-__device__ __forceinline__ void stage_activation(const ActivationView &view, int8_t *q, float *d, int *sum8,
-                                                 uint32_t thread, uint32_t threads) {
-    const uint32_t total = view.rows * view.blocks;
+// Shared memory holds the activation in a split layout so that consecutive lanes, which
+// take consecutive blocks, read consecutive 16-byte words (no bank conflicts):
+//   lo   [rows * blocks] int4  values 0..15 of each (row, block)
+//   hi   [rows * blocks] int4  values 16..31
+//   meta [rows * blocks] int2  {fp32 bits of the block scale, -8 * sum of the 32 values}
+// The -8 * sum seeds the dp4a chain, which turns the unsigned 4-bit codes (0..15) into
+// code - 8 without unpacking them to signed bytes.
+struct StagedActivation {
+    int4 *lo;
+    int4 *hi;
+    int2 *meta;
+};
+
+__device__ __forceinline__ StagedActivation staged_activation(uint8_t *smem, uint32_t items) {
+    int4 *lo = reinterpret_cast<int4 *>(smem);
+    int4 *hi = lo + items;
+    return StagedActivation{lo, hi, reinterpret_cast<int2 *>(hi + items)};
+}
+
+size_t activation_bytes(uint32_t rows, uint32_t blocks) { return static_cast<size_t>(rows) * blocks * (16 + 16 + 8); }
+
+__device__ __forceinline__ void read_activation_item(const ActivationView &view, uint32_t item, uint32_t (&words)[8],
+                                                     uint16_t &scale_bits) {
+    const uint32_t row = item / view.blocks;
+    const uint32_t block = item % view.blocks;
     const uint32_t interleaved_rows = view.interleave == 0 ? 0 : view.rows - view.rows % 4;
-    for (uint32_t item = thread; item < total; item += threads) {
-        const uint32_t row = item / view.blocks;
-        const uint32_t block = item % view.blocks;
-        const uint8_t *scale_bytes;
-        const uint8_t *values;
-        activation_block(view, row, block, &scale_bytes, &values);
-        uint32_t words[8];
-        if (row >= interleaved_rows) {
-            const uint16_t *halves = reinterpret_cast<const uint16_t *>(values);
+    const uint8_t *scale_bytes;
+    const uint8_t *values;
+    activation_block(view, row, block, &scale_bytes, &values);
+    scale_bits = *reinterpret_cast<const uint16_t *>(scale_bytes);
+    if (row >= interleaved_rows) {
+        // Native blocks start on even bytes: sixteen independent 16-bit loads.
+        const uint16_t *halves = reinterpret_cast<const uint16_t *>(values);
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                words[i] = static_cast<uint32_t>(halves[2 * i]) | (static_cast<uint32_t>(halves[2 * i + 1]) << 16);
-        } else {
+        for (int i = 0; i < 8; ++i)
+            words[i] = static_cast<uint32_t>(halves[2 * i]) | (static_cast<uint32_t>(halves[2 * i + 1]) << 16);
+        return;
+    }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                uint32_t word = 0;
+    for (int i = 0; i < 8; ++i) {
+        uint32_t word = 0;
 #pragma unroll
-                for (int byte = 0; byte < 4; ++byte)
-                    word |= static_cast<uint32_t>(static_cast<uint8_t>(activation_value(view, values, row, 4 * i + byte)))
-                            << (8 * byte);
-                words[i] = word;
-            }
-        }
-        int sum = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) sum = __dp4a(static_cast<int>(words[i]), 0x01010101, sum);
-        uint4 *destination = reinterpret_cast<uint4 *>(q + static_cast<size_t>(item) * 32);
-        destination[0] = make_uint4(words[0], words[1], words[2], words[3]);
-        destination[1] = make_uint4(words[4], words[5], words[6], words[7]);
-        d[item] = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short *>(scale_bytes)));
-        sum8[item] = 8 * sum;
+        for (int byte = 0; byte < 4; ++byte)
+            word |= static_cast<uint32_t>(static_cast<uint8_t>(activation_value(view, values, row, 4 * i + byte)))
+                    << (8 * byte);
+        words[i] = word;
     }
 }
 
-__device__ __forceinline__ int block_dot(uint4 w, const int8_t *a) {
-    const int4 lo = *reinterpret_cast<const int4 *>(a);       // activation values 0..15
-    const int4 hi = *reinterpret_cast<const int4 *>(a + 16);  // activation values 16..31
-    int dot = 0;
+__device__ __forceinline__ void write_activation_item(const StagedActivation &staged, uint32_t item,
+                                                      const uint32_t (&words)[8], uint16_t scale_bits) {
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sum = __dp4a(static_cast<int>(words[i]), 0x01010101, sum);
+    staged.lo[item] = make_int4(words[0], words[1], words[2], words[3]);
+    staged.hi[item] = make_int4(words[4], words[5], words[6], words[7]);
+    staged.meta[item] = make_int2(__float_as_int(__half2float(__ushort_as_half(scale_bits))), -8 * sum);
+}
+
+// One thread per (row, block) item, two items per trip so two L2 round trips overlap.
+__device__ __forceinline__ void stage_activation(const ActivationView &view, const StagedActivation &staged,
+                                                 uint32_t thread, uint32_t threads) {
+    const uint32_t total = view.rows * view.blocks;
+    for (uint32_t item = thread; item < total; item += 2 * threads) {
+        uint32_t words0[8], words1[8];
+        uint16_t scale0, scale1 = 0;
+        const bool second = item + threads < total;
+        read_activation_item(view, item, words0, scale0);
+        if (second) read_activation_item(view, item + threads, words1, scale1);
+        write_activation_item(staged, item, words0, scale0);
+        if (second) write_activation_item(staged, item + threads, words1, scale1);
+    }
+}
+
+// Exact int32 dot of one block: sum of (code - 8) * a over the 32 values. Weight word i holds
+// codes i*4..i*4+3 in its low nibbles and codes 16+i*4.. in its high nibbles (GGML order).
+__device__ __forceinline__ int block_dot(uint4 w, int4 lo, int4 hi, int seed) {
+    int dot = seed;
     dot = __dp4a(static_cast<int>(w.x & 0x0F0F0F0Fu), lo.x, dot);
     dot = __dp4a(static_cast<int>((w.x >> 4) & 0x0F0F0F0Fu), hi.x, dot);
     dot = __dp4a(static_cast<int>(w.y & 0x0F0F0F0Fu), lo.y, dot);
@@ -123,47 +154,40 @@ __device__ __forceinline__ int block_dot(uint4 w, const int8_t *a) {
     return dot;
 }
 
-template <int ROWS>
-__device__ __forceinline__ void accumulate_block(uint4 w, uint16_t w_scale_bits, uint32_t block, uint32_t blocks,
-                                                 const int8_t *q, const float *d, const int *sum8, float (&acc)[ROWS]) {
-    const float dw = __half2float(__ushort_as_half(w_scale_bits));
+// acc[r][c] += ((float)dot * d_w[c]) * d_a[r], rounded step by step as the reference rounds
+// each block term (ggml_q4_0.py:81-100).
+template <int ROWS, int COLS>
+__device__ __forceinline__ void accumulate_block(const uint4 (&w)[COLS], const float (&dw)[COLS], uint32_t item,
+                                                 uint32_t blocks, const StagedActivation &staged,
+                                                 float (&acc)[ROWS][COLS]) {
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
-        const size_t item = static_cast<size_t>(r) * blocks + block;
-        const int dot = block_dot(w, q + item * 32) - sum8[item];
-        acc[r] = __fadd_rn(acc[r], __fmul_rn(__fmul_rn(__int2float_rn(dot), dw), d[item]));
+        const uint32_t at = static_cast<uint32_t>(r) * blocks + item;
+        const int4 lo = staged.lo[at];
+        const int4 hi = staged.hi[at];
+        const int2 meta = staged.meta[at];
+        const float da = __int_as_float(meta.x);
+#pragma unroll
+        for (int c = 0; c < COLS; ++c)
+            acc[r][c] = __fadd_rn(acc[r][c], __fmul_rn(__fmul_rn(__int2float_rn(block_dot(w[c], lo, hi, meta.y)), dw[c]), da));
     }
 }
 
-template <int ROWS>
-__device__ __forceinline__ void warp_sum(float (&acc)[ROWS]) {
+template <int N>
+__device__ __forceinline__ void warp_sum(float (&values)[N]) {
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
+    for (int i = 0; i < N; ++i) {
 #pragma unroll
-        for (int offset = 16; offset > 0; offset >>= 1) acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], offset));
+        for (int offset = 16; offset > 0; offset >>= 1)
+            values[i] = __fadd_rn(values[i], __shfl_xor_sync(0xffffffffu, values[i], offset));
     }
 }
-
-template <int ROWS>
-__device__ __forceinline__ void store_rows(const float (&acc)[ROWS], uint32_t lane, float *destination,
-                                           size_t destination_stride, size_t column) {
-    if (lane < static_cast<uint32_t>(ROWS)) {
-        float value = acc[0];
-#pragma unroll
-        for (int r = 1; r < ROWS; ++r)
-            if (lane == static_cast<uint32_t>(r)) value = acc[r];
-        destination[static_cast<size_t>(lane) * destination_stride + column] = value;
-    }
-}
-
-size_t activation_bytes(uint32_t rows, uint32_t blocks) { return static_cast<size_t>(rows) * blocks * (32 + 4 + 4); }
 
 // ---- direct-load kernel over the prepared layout -------------------------------------------
 
 constexpr size_t kSmemBudget = 200u * 1024u;
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kUnroll = 8;
 
 __device__ __forceinline__ uint4 load_stream_u4(const void *p) {
     uint4 v;
@@ -186,67 +210,121 @@ struct DirectParams {
     uint32_t count;
 };
 
-// One warp per column; SPLIT warps share a column for long reductions: warp part p takes
-// blocks p*32 + lane + i*32*SPLIT and the SPLIT partial sums are added in part order
-// through shared memory (deterministic). Eight independent 16-byte loads per lane are in
-// flight before any of them is consumed.
-template <int ROWS, int SPLIT>
-__global__ void __launch_bounds__(kThreads) q4_0_direct_kernel(const DirectParams p) {
+// A warp owns COLS adjacent columns (a "group"); SPLIT warps share a group for long
+// reductions. Lane l of part q takes blocks q*32 + l + i*32*SPLIT; each trip loads UNROLL such
+// blocks of every column of the group (UNROLL * COLS independent 16-byte loads in flight per
+// lane) before any is consumed, and each staged activation word read from shared memory
+// serves COLS weight blocks. The first trip of a warp's first group is loaded before the
+// activation is staged, and the first trip of its next group before the warp reduces the
+// current one, so the weight stream does not stop for either. Partial sums of a group's
+// SPLIT warps are added in part order through shared memory (deterministic). Registers per
+// thread are capped so that MIN_BLOCKS CTAs of 256 threads fit on an SM.
+template <int ROWS, int SPLIT, int COLS, int UNROLL, int MIN_BLOCKS>
+__global__ void __launch_bounds__(kThreads, MIN_BLOCKS) q4_0_direct_kernel(const DirectParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ float partial[kWarps][ROWS];
-    int8_t *q = reinterpret_cast<int8_t *>(smem);
-    float *d = reinterpret_cast<float *>(smem + static_cast<size_t>(ROWS) * p.blocks * 32);
-    int *sum8 = reinterpret_cast<int *>(d + static_cast<size_t>(ROWS) * p.blocks);
-    stage_activation(p.view, q, d, sum8, threadIdx.x, blockDim.x);
-    __syncthreads();
-
+    __shared__ float partial[kWarps][ROWS * COLS];
     constexpr uint32_t kSlots = kWarps / SPLIT;
     constexpr uint32_t kStride = 32 * SPLIT;  // blocks between a lane's consecutive blocks
+    constexpr uint32_t kTrip = kStride * UNROLL;
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t part = warp % SPLIT;
     const uint32_t slot = warp / SPLIT;
     const uint32_t first = part * 32 + lane;
-    for (uint32_t j = blockIdx.x * kSlots + slot; j < p.count; j += gridDim.x * kSlots) {
-        const size_t column = p.col0 + j;
-        const uint8_t *w_col = p.nibbles + column * p.blocks * 16;
-        const uint16_t *s_col = p.scales + column * p.scale_stride;
-        float acc[ROWS];
+    const uint32_t blocks = p.blocks;
+    const uint32_t groups = (p.count + COLS - 1) / COLS;
+    const size_t column_bytes = static_cast<size_t>(blocks) * 16;
+
+    uint4 w[UNROLL][COLS];
+    uint16_t s[UNROLL][COLS];
+    auto load_trip = [&](uint32_t group, uint32_t b) {
+        const uint32_t j0 = group * COLS;
+        const uint32_t valid = min(static_cast<uint32_t>(COLS), p.count - j0);
+        const uint8_t *wp = p.nibbles + static_cast<size_t>(p.col0 + j0) * column_bytes + static_cast<size_t>(b) * 16;
+        const uint16_t *sp = p.scales + static_cast<size_t>(p.col0 + j0) * p.scale_stride + b;
+        if (valid == static_cast<uint32_t>(COLS) && b + kStride * (UNROLL - 1) < blocks) {
 #pragma unroll
-        for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
-        uint32_t b = first;
-        for (; b + kStride * (kUnroll - 1) < p.blocks; b += kStride * kUnroll) {
-            uint4 w[kUnroll];
-            uint16_t s[kUnroll];
+            for (int u = 0; u < UNROLL; ++u) {
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) {
-                w[u] = load_stream_u4(w_col + static_cast<size_t>(b + kStride * u) * 16);
-                s[u] = __ldg(s_col + b + kStride * u);
+                for (int c = 0; c < COLS; ++c) {
+                    w[u][c] = load_stream_u4(wp + c * column_bytes + static_cast<size_t>(u) * kStride * 16);
+                    s[u][c] = __ldg(sp + static_cast<size_t>(c) * p.scale_stride + u * kStride);
+                }
             }
+            return;
+        }
 #pragma unroll
-            for (int u = 0; u < kUnroll; ++u) accumulate_block<ROWS>(w[u], s[u], b + kStride * u, p.blocks, q, d, sum8, acc);
+        for (int u = 0; u < UNROLL; ++u) {
+#pragma unroll
+            for (int c = 0; c < COLS; ++c) {
+                if (b + u * kStride < blocks && static_cast<uint32_t>(c) < valid) {
+                    w[u][c] = load_stream_u4(wp + c * column_bytes + static_cast<size_t>(u) * kStride * 16);
+                    s[u][c] = __ldg(sp + static_cast<size_t>(c) * p.scale_stride + u * kStride);
+                } else {
+                    w[u][c] = make_uint4(0, 0, 0, 0);
+                    s[u][c] = 0;
+                }
+            }
         }
-        for (; b < p.blocks; b += kStride) {
-            accumulate_block<ROWS>(load_stream_u4(w_col + static_cast<size_t>(b) * 16), __ldg(s_col + b), b, p.blocks, q, d,
-                                   sum8, acc);
+    };
+
+    uint32_t group = blockIdx.x * kSlots + slot;
+    if (group < groups) load_trip(group, first);
+    const StagedActivation staged = staged_activation(smem, ROWS * blocks);
+    stage_activation(p.view, staged, threadIdx.x, blockDim.x);
+    __syncthreads();
+
+    for (; group < groups; group += gridDim.x * kSlots) {
+        const uint32_t j0 = group * COLS;
+        const uint32_t valid = min(static_cast<uint32_t>(COLS), p.count - j0);
+        float acc[ROWS][COLS];
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+#pragma unroll
+            for (int c = 0; c < COLS; ++c) acc[r][c] = 0.0f;
         }
-        warp_sum<ROWS>(acc);
+        for (uint32_t b = first; b < blocks; b += kTrip) {
+            if (b != first) load_trip(group, b);
+#pragma unroll
+            for (int u = 0; u < UNROLL; ++u) {
+                if (b + u * kStride < blocks) {
+                    float dw[COLS];
+#pragma unroll
+                    for (int c = 0; c < COLS; ++c) dw[c] = __half2float(__ushort_as_half(s[u][c]));
+                    accumulate_block<ROWS, COLS>(w[u], dw, b + u * kStride, blocks, staged, acc);
+                }
+            }
+        }
+        const uint32_t next = group + gridDim.x * kSlots;
+        if (next < groups) load_trip(next, first);
+
+        float sums[ROWS * COLS];
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+#pragma unroll
+            for (int c = 0; c < COLS; ++c) sums[r * COLS + c] = acc[r][c];
+        }
+        warp_sum<ROWS * COLS>(sums);
+        float mine = sums[0];  // lane r * COLS + c keeps output (r, c)
+#pragma unroll
+        for (int i = 1; i < ROWS * COLS; ++i)
+            if (lane == static_cast<uint32_t>(i)) mine = sums[i];
+        const uint32_t out_row = lane / COLS;
+        const uint32_t out_col = lane % COLS;
+        const bool writer = lane < static_cast<uint32_t>(ROWS * COLS) && out_col < valid;
         if constexpr (SPLIT > 1) {
-            // The SPLIT warps of this slot run the same trip count, so the named barrier is safe.
-            if (lane == 0) {
-#pragma unroll
-                for (int r = 0; r < ROWS; ++r) partial[warp][r] = acc[r];
-            }
+            // The SPLIT warps of this slot run the same groups, so the named barrier is safe.
+            if (lane < static_cast<uint32_t>(ROWS * COLS)) partial[warp][lane] = mine;
             asm volatile("bar.sync %0, %1;" ::"r"(1 + slot), "r"(32 * SPLIT) : "memory");
-            if (part == 0 && lane < static_cast<uint32_t>(ROWS)) {
+            if (part == 0 && writer) {
                 float value = partial[slot * SPLIT][lane];
 #pragma unroll
-                for (int q_part = 1; q_part < SPLIT; ++q_part) value = __fadd_rn(value, partial[slot * SPLIT + q_part][lane]);
-                p.destination[static_cast<size_t>(lane) * p.destination_stride + p.out_col0 + j] = value;
+                for (int q = 1; q < SPLIT; ++q) value = __fadd_rn(value, partial[slot * SPLIT + q][lane]);
+                p.destination[static_cast<size_t>(out_row) * p.destination_stride + p.out_col0 + j0 + out_col] = value;
             }
             asm volatile("bar.sync %0, %1;" ::"r"(1 + slot), "r"(32 * SPLIT) : "memory");
-        } else {
-            store_rows<ROWS>(acc, lane, p.destination, p.destination_stride, p.out_col0 + j);
+        } else if (writer) {
+            p.destination[static_cast<size_t>(out_row) * p.destination_stride + p.out_col0 + j0 + out_col] = mine;
         }
     }
 }
@@ -270,63 +348,77 @@ struct NativeParams {
 template <int ROWS>
 __global__ void __launch_bounds__(kNativeThreads) q4_0_native_kernel(const NativeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
-    int8_t *q = reinterpret_cast<int8_t *>(smem);
-    float *d = reinterpret_cast<float *>(smem + static_cast<size_t>(ROWS) * p.blocks * 32);
-    int *sum8 = reinterpret_cast<int *>(d + static_cast<size_t>(ROWS) * p.blocks);
-    stage_activation(p.view, q, d, sum8, threadIdx.x, blockDim.x);
+    const StagedActivation staged = staged_activation(smem, ROWS * p.blocks);
+    stage_activation(p.view, staged, threadIdx.x, blockDim.x);
     __syncthreads();
     const uint32_t lane = threadIdx.x & 31;
     for (uint32_t j = blockIdx.x * kNativeWarps + (threadIdx.x >> 5); j < p.count; j += gridDim.x * kNativeWarps) {
         const size_t column = p.col0 + j;
-        float acc[ROWS];
+        float acc[ROWS][1];
 #pragma unroll
-        for (int r = 0; r < ROWS; ++r) acc[r] = 0.0f;
+        for (int r = 0; r < ROWS; ++r) acc[r][0] = 0.0f;
         for (uint32_t b = lane; b < p.blocks; b += 32) {
             // Native 18-byte blocks are 2-byte aligned: nine 16-bit loads.
             const uint16_t *src = reinterpret_cast<const uint16_t *>(p.weight + (column * p.blocks + b) * 18);
-            uint4 w;
-            w.x = static_cast<uint32_t>(src[1]) | (static_cast<uint32_t>(src[2]) << 16);
-            w.y = static_cast<uint32_t>(src[3]) | (static_cast<uint32_t>(src[4]) << 16);
-            w.z = static_cast<uint32_t>(src[5]) | (static_cast<uint32_t>(src[6]) << 16);
-            w.w = static_cast<uint32_t>(src[7]) | (static_cast<uint32_t>(src[8]) << 16);
-            accumulate_block<ROWS>(w, src[0], b, p.blocks, q, d, sum8, acc);
+            uint4 w[1];
+            w[0].x = static_cast<uint32_t>(src[1]) | (static_cast<uint32_t>(src[2]) << 16);
+            w[0].y = static_cast<uint32_t>(src[3]) | (static_cast<uint32_t>(src[4]) << 16);
+            w[0].z = static_cast<uint32_t>(src[5]) | (static_cast<uint32_t>(src[6]) << 16);
+            w[0].w = static_cast<uint32_t>(src[7]) | (static_cast<uint32_t>(src[8]) << 16);
+            const float dw[1] = {__half2float(__ushort_as_half(src[0]))};
+            accumulate_block<ROWS, 1>(w, dw, b, p.blocks, staged, acc);
         }
-        warp_sum<ROWS>(acc);
-        store_rows<ROWS>(acc, lane, p.destination, p.destination_stride, p.out_col0 + j);
+        float sums[ROWS];
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) sums[r] = acc[r][0];
+        warp_sum<ROWS>(sums);
+        float mine = sums[0];
+#pragma unroll
+        for (int r = 1; r < ROWS; ++r)
+            if (lane == static_cast<uint32_t>(r)) mine = sums[r];
+        if (lane < static_cast<uint32_t>(ROWS)) p.destination[static_cast<size_t>(lane) * p.destination_stride + p.out_col0 + j] = mine;
     }
 }
 
-template <int ROWS, int SPLIT>
+template <int ROWS, int SPLIT, int COLS, int UNROLL, int MIN_BLOCKS>
 cudaError_t launch_direct(const DirectParams &p, int sm_count, cudaStream_t stream) {
     const size_t smem = activation_bytes(ROWS, p.blocks);
     if (smem > kSmemBudget) return cudaErrorInvalidValue;
-    auto kernel = q4_0_direct_kernel<ROWS, SPLIT>;
+    auto kernel = q4_0_direct_kernel<ROWS, SPLIT, COLS, UNROLL, MIN_BLOCKS>;
     if (smem > 48u * 1024u) {
         const cudaError_t error =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (error != cudaSuccess) return error;
     }
     // Persistent CTAs filling the SM's real residency (each stages the activation once); the
-    // grid is balanced so every column slot runs the same number of rounds (no straggling tail).
+    // grid is balanced so every group slot runs the same number of rounds (no straggling tail).
     int per_sm = 0;
     const cudaError_t error = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem);
     if (error != cudaSuccess) return error;
     if (per_sm < 1) per_sm = 1;
     constexpr uint32_t kSlots = kWarps / SPLIT;
+    const uint64_t groups = (static_cast<uint64_t>(p.count) + COLS - 1) / COLS;
     const uint64_t capacity = static_cast<uint64_t>(sm_count) * static_cast<uint64_t>(per_sm);
-    const uint64_t rounds = (p.count + capacity * kSlots - 1) / (capacity * kSlots);
-    const uint32_t grid = static_cast<uint32_t>((p.count + kSlots * rounds - 1) / (kSlots * rounds));
+    const uint64_t rounds = (groups + capacity * kSlots - 1) / (capacity * kSlots);
+    const uint32_t grid = static_cast<uint32_t>((groups + kSlots * rounds - 1) / (kSlots * rounds));
     kernel<<<grid, kThreads, smem, stream>>>(p);
     return cudaGetLastError();
 }
 
 template <int ROWS>
 cudaError_t launch_rows(const DirectParams &p, int sm_count, cudaStream_t stream) {
-    // Columns with many blocks are split over 2 or 4 warps so there are enough independent
-    // units to keep every SM busy without a long last round.
-    if (p.blocks >= 2048) return launch_direct<ROWS, 4>(p, sm_count, stream);
-    if (p.blocks >= 512) return launch_direct<ROWS, 2>(p, sm_count, stream);
-    return launch_direct<ROWS, 1>(p, sm_count, stream);
+    // Two columns per warp halve the shared-memory reads per weight byte. One row: four blocks
+    // of each column in flight per lane within 80 registers (3 CTAs per SM). Two rows: two
+    // blocks at the same budget. Three or four rows are closer to issue-bound and keep four
+    // blocks in flight at 128 registers (2 CTAs per SM), which measured faster than either
+    // more CTAs or more columns per warp.
+    if constexpr (ROWS == 1) {
+        return launch_direct<ROWS, 1, 2, 4, 3>(p, sm_count, stream);
+    } else if constexpr (ROWS == 2) {
+        return launch_direct<ROWS, 1, 2, 2, 3>(p, sm_count, stream);
+    } else {
+        return launch_direct<ROWS, 1, 2, 4, 2>(p, sm_count, stream);
+    }
 }
 
 template <int ROWS>

@@ -270,6 +270,13 @@ __global__ void __launch_bounds__(kThreads, MIN_BLOCKS) q4_0_direct_kernel(const
 
     uint32_t group = blockIdx.x * kSlots + slot;
     if (group < groups) load_trip(group, first);
+    // Programmatic dependent launch: the kernel may start while the previous kernel on the
+    // stream drains. The prepared weights are immutable once prepare has returned, so the first
+    // trip above is issued before the wait; the activation may be the previous kernel's output
+    // and is read only after it. Every CTA of this grid is resident (persistent grid), so the
+    // next kernel may be scheduled into the SMs' free slots right away.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const StagedActivation staged = staged_activation(smem, ROWS * blocks);
     stage_activation(p.view, staged, threadIdx.x, blockDim.x);
     __syncthreads();
@@ -401,8 +408,17 @@ cudaError_t launch_direct(const DirectParams &p, int sm_count, cudaStream_t stre
     const uint64_t capacity = static_cast<uint64_t>(sm_count) * static_cast<uint64_t>(per_sm);
     const uint64_t rounds = (groups + capacity * kSlots - 1) / (capacity * kSlots);
     const uint32_t grid = static_cast<uint32_t>((groups + kSlots * rounds - 1) / (kSlots * rounds));
-    kernel<<<grid, kThreads, smem, stream>>>(p);
-    return cudaGetLastError();
+    cudaLaunchAttribute attribute{};
+    attribute.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute.val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(grid);
+    config.blockDim = dim3(kThreads);
+    config.dynamicSmemBytes = smem;
+    config.stream = stream;
+    config.attrs = &attribute;
+    config.numAttrs = 1;
+    return cudaLaunchKernelEx(&config, kernel, p);
 }
 
 template <int ROWS>
@@ -412,7 +428,12 @@ cudaError_t launch_rows(const DirectParams &p, int sm_count, cudaStream_t stream
     // blocks at the same budget. Three or four rows are closer to issue-bound and keep four
     // blocks in flight at 128 registers (2 CTAs per SM), which measured faster than either
     // more CTAs or more columns per warp.
+    // Long single-row reductions (>= 640 blocks, e.g. the 70B down projection with 896) are
+    // split over 4 warps with seven blocks per lane and column in one trip: four times the
+    // independent groups of the unsplit kernel, so the grid fills the SMs even when the matrix
+    // is narrow (a column shard), and 14 loads in flight per lane within 128 registers.
     if constexpr (ROWS == 1) {
+        if (p.blocks >= 640) return launch_direct<ROWS, 4, 2, 7, 2>(p, sm_count, stream);
         return launch_direct<ROWS, 1, 2, 4, 3>(p, sm_count, stream);
     } else if constexpr (ROWS == 2) {
         return launch_direct<ROWS, 1, 2, 2, 3>(p, sm_count, stream);

@@ -206,6 +206,42 @@ def test_cpu_repack_interleaved_activations(native, interleave: int, golden: dic
         native.lib.qpucuda_q4_0_linear_destroy(handle)
 
 
+@pytest.mark.parametrize(("k", "n"), [(20512, 96), (28672, 144)])
+@pytest.mark.parametrize("rows", (1, 2, 3, 4))
+def test_long_reductions_over_windows(native, k: int, n: int, rows: int) -> None:  # type: ignore[no-untyped-def]
+    """Long reductions (641 and 896 blocks: the K-split kernel at M = 1, with a partial last trip
+    at 641) over a resident window and an execution window inside it (both on the reference's
+    16-column grid) written at an odd output offset; every written column is checked and the
+    columns around the window stay untouched."""
+    import torch
+
+    from gpu_helpers import max_relative_error
+
+    source, weight = workloads.torch_linear_inputs(rows, k, n, seed=11, weight_std=0.02, device="cuda")
+    weight_blocks = native.quantize_blocks(weight, "q4_0").cpu().numpy()
+    activation = native.quantize_blocks(source, "q8_0")
+    start, count = 16, n - 32
+    status, handle = prepare(native, weight_blocks, rows=4, start=start, count=count)
+    assert status == _native.Status.OK
+    try:
+        column_start, column_count, out_start = start + 16, count - 16, 3
+        out = torch.full((rows, out_start + column_count + 1), float("nan"), dtype=torch.float32, device="cuda")
+        native.context.set_stream(torch.cuda.current_stream().cuda_stream)
+        native.context.check(
+            native.lib.qpucuda_q4_0_linear_execute_device(
+                handle, activation.data_ptr(), rows, out.data_ptr(), out.shape[1], column_start, column_count, out_start
+            ),
+            "execute_device",
+        )
+        native.sync()
+        got = out.cpu().numpy()
+        expected = oracle.q4_0_q8_0_linear(activation.cpu().numpy(), weight_blocks[column_start : column_start + column_count])
+        assert max_relative_error(got[:, out_start : out_start + column_count], expected) <= Q4_0_TOLERANCE
+        assert np.isnan(got[:, :out_start]).all() and np.isnan(got[:, out_start + column_count :]).all()
+    finally:
+        native.lib.qpucuda_q4_0_linear_destroy(handle)
+
+
 @pytest.mark.parametrize("shape", workloads.LLAMA2_70B_FFN + workloads.LLAMA2_7B_FFN, ids=lambda s: f"{s.name}_{s.in_features}x{s.out_features}")
 def test_decode_full_size_columns_sample(native, shape) -> None:  # type: ignore[no-untyped-def]
     """M=1 decode at the 70B / 7B shapes: the full output is computed, a column sample is checked

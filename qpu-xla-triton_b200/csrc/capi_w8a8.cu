@@ -14,6 +14,7 @@
 #include <new>
 
 #include "qpucuda_internal.h"
+#include "qpucuda_peer.h"
 #include "qpucuda_w8a8.h"
 
 using namespace qpucuda;
@@ -63,9 +64,12 @@ void free_linear(qpucuda_w8a8_linear *linear) {
 }
 
 // Enqueue quantize + GEMM/GEMV + epilogue for `rows` rows already resident on the device.
-qpucuda_status enqueue(qpucuda_w8a8_linear *linear, const float *source, size_t source_stride,
-                       const int8_t *quantized, size_t quantized_stride, const float *row_scales, uint32_t rows,
-                       float *destination, size_t destination_stride) {
+// With peers, the same outputs are also written to each peer destination at the same
+// offsets: by the GEMM epilogue itself, or, on the GEMV path (a few rows), by one 2-D copy
+// per peer after the local result.
+qpucuda_status enqueue_to(qpucuda_w8a8_linear *linear, const float *source, size_t source_stride,
+                          const int8_t *quantized, size_t quantized_stride, const float *row_scales, uint32_t rows,
+                          float *destination, size_t destination_stride, float *const *peers, uint32_t peer_count) {
     qpucuda_context *context = linear->context;
     cudaStream_t stream = context->stream;
     if (source != nullptr) {
@@ -88,16 +92,32 @@ qpucuda_status enqueue(qpucuda_w8a8_linear *linear, const float *source, size_t 
     if (rows <= kGemvMaxRows) {
         error = launch_w8a8_gemv(quantized, quantized_stride, linear->d_weight, linear->k_pad, rows, linear->columns,
                                  linear->k_pad, epilogue, context->sm_count, stream);
-    } else if (quantized == linear->d_quantized && linear->maps_ready) {
-        error = launch_w8a8_gemm_sm100(&linear->map_quantized, &linear->map_weight, rows, linear->columns,
-                                       linear->k_pad, epilogue, context->d_error, context->sm_count, stream);
+        for (uint32_t p = 0; error == cudaSuccess && p < peer_count; ++p) {
+            error = cudaMemcpy2DAsync(peers[p], destination_stride * sizeof(float), destination,
+                                      destination_stride * sizeof(float), static_cast<size_t>(linear->columns) * sizeof(float),
+                                      rows, cudaMemcpyDeviceToDevice, stream);
+        }
     } else {
-        error = run_w8a8_gemm(quantized, quantized_stride, linear->d_weight, linear->k_pad, rows, linear->columns,
-                              linear->k_pad, epilogue, context->d_error, context->sm_count, stream);
+        epilogue.peer_count = peer_count;
+        for (uint32_t p = 0; p < peer_count; ++p) epilogue.peer_out[p] = peers[p];
+        if (quantized == linear->d_quantized && linear->maps_ready) {
+            error = launch_w8a8_gemm_sm100(&linear->map_quantized, &linear->map_weight, rows, linear->columns,
+                                           linear->k_pad, epilogue, context->d_error, context->sm_count, stream);
+        } else {
+            error = run_w8a8_gemm(quantized, quantized_stride, linear->d_weight, linear->k_pad, rows, linear->columns,
+                                  linear->k_pad, epilogue, context->d_error, context->sm_count, stream);
+        }
     }
     if (error == cudaErrorInvalidValue) return cuda_fail(context, error, "W8A8 GEMM launch", QPUCUDA_INVALID_ARGUMENT);
     if (error != cudaSuccess) return cuda_fail(context, error, "W8A8 GEMM launch");
     return QPUCUDA_OK;
+}
+
+qpucuda_status enqueue(qpucuda_w8a8_linear *linear, const float *source, size_t source_stride,
+                       const int8_t *quantized, size_t quantized_stride, const float *row_scales, uint32_t rows,
+                       float *destination, size_t destination_stride) {
+    return enqueue_to(linear, source, source_stride, quantized, quantized_stride, row_scales, rows, destination,
+                      destination_stride, nullptr, 0);
 }
 
 }  // namespace
@@ -220,6 +240,31 @@ qpucuda_status qpucuda_w8a8_linear_execute_device(qpucuda_w8a8_linear *linear, c
     if (status != QPUCUDA_OK) return status;
     DeviceGuard guard(context->device);
     return enqueue(linear, source, source_stride, nullptr, 0, nullptr, rows, destination, destination_stride);
+}
+
+qpucuda_status qpucuda_w8a8_linear_execute_device_fanout(qpucuda_w8a8_linear *linear, const float *source,
+                                                         size_t source_stride, uint32_t rows, float *destination,
+                                                         float *const *peer_destinations, uint32_t peer_count,
+                                                         size_t destination_stride) {
+    if (linear == nullptr) return QPUCUDA_INVALID_ARGUMENT;
+    qpucuda_context *context = linear->context;
+    if (source == nullptr || destination == nullptr || rows == 0 || rows > linear->max_batch ||
+        source_stride < linear->k || destination_stride < linear->columns || peer_count > QPUCUDA_MAX_PEERS ||
+        (peer_count != 0 && peer_destinations == nullptr)) {
+        return fail(context, QPUCUDA_INVALID_ARGUMENT, "W8A8 fan-out: invalid arguments");
+    }
+    for (uint32_t p = 0; p < peer_count; ++p) {
+        if (peer_destinations[p] == nullptr) return fail(context, QPUCUDA_INVALID_ARGUMENT, "W8A8 fan-out: null peer");
+    }
+    if (rows > kGemvMaxRows && !(context->cc_major == 10 && context->cc_minor == 0)) {
+        return fail(context, QPUCUDA_CAPABILITY_MISSING, "the tcgen05 int8 GEMM needs an sm_100 device");
+    }
+    std::lock_guard<std::mutex> lock(context->mutex);
+    qpucuda_status status = begin_submit(context);
+    if (status != QPUCUDA_OK) return status;
+    DeviceGuard guard(context->device);
+    return enqueue_to(linear, source, source_stride, nullptr, 0, nullptr, rows, destination, destination_stride,
+                      peer_destinations, peer_count);
 }
 
 qpucuda_status qpucuda_w8a8_linear_execute_prepared_device(qpucuda_w8a8_linear *linear, const int8_t *quantized,

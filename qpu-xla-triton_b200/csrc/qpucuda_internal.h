@@ -90,6 +90,9 @@ cudaError_t launch_quantize_q4_0(const float *x, size_t x_stride, uint32_t rows,
 
 enum class EpilogueMode : int { kStoreS32 = 0, kDequantize = 1, kDequantizeBias = 2 };
 
+// Peer destinations one GEMM epilogue may write besides its own output (ranks of one node - 1).
+constexpr uint32_t kGemmMaxPeers = 7;
+
 struct GemmEpilogue {
     EpilogueMode mode = EpilogueMode::kDequantize;
     const float *row_scales = nullptr;
@@ -97,6 +100,9 @@ struct GemmEpilogue {
     const float *bias = nullptr;
     void *out = nullptr;  // float* or int32_t*
     size_t out_stride = 0;  // elements
+    // Other ranks' output buffers (mapped peer memory), each written at the same offsets as `out`.
+    void *peer_out[kGemmMaxPeers] = {};
+    uint32_t peer_count = 0;
 };
 
 // tcgen05 int8 GEMM: a [m][k] and w [n][k] int8, K-major, 16-byte aligned rows.

@@ -60,7 +60,10 @@ struct Control {
     volatile int abort_flag;
 };
 
-constexpr size_t kSmemBytes = static_cast<size_t>(STAGES) * STAGE_BYTES + 1024 + sizeof(Control);
+// Epilogue staging: each epilogue warp transposes its 32 rows x 32 columns chunk through 4 KB
+// of shared memory so that global stores leave as full 128-byte row segments.
+constexpr int EPILOGUE_STAGE_BYTES = (EPILOGUE_THREADS / 32) * 32 * 32 * 4;
+constexpr size_t kSmemBytes = static_cast<size_t>(STAGES) * STAGE_BYTES + EPILOGUE_STAGE_BYTES + 1024 + sizeof(Control);
 
 struct GemmParams {
     uint32_t m, n, k;
@@ -72,6 +75,10 @@ struct GemmParams {
     const float *bias;
     void *out;
     size_t out_stride;
+    // Further destinations written with the same (row, column) offsets and row stride as
+    // `out`: other ranks' output buffers for the fused GEMM + all-gather.
+    void *peer_out[kGemmMaxPeers];
+    uint32_t peer_count;
     unsigned int *error_word;
 };
 
@@ -130,6 +137,20 @@ __device__ __forceinline__ float dequant(uint32_t bits, float row_scale, float c
     return __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(bits)), row_scale), col_scale);
 }
 
+// Four consecutive 4-byte outputs of one row, columns col..col+3 (the caller guarantees
+// col < n); a 16-byte store when the whole group is in range and aligned.
+__device__ __forceinline__ void store_group(void *base, size_t offset, uint4 value, uint32_t valid, bool aligned) {
+    uint32_t *p = static_cast<uint32_t *>(base) + offset;
+    if (valid >= 4 && aligned) {
+        *reinterpret_cast<uint4 *>(p) = value;
+        return;
+    }
+    p[0] = value.x;
+    if (valid > 1) p[1] = value.y;
+    if (valid > 2) p[2] = value.z;
+    if (valid > 3) p[3] = value.w;
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     w8a8_gemm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                            const GemmParams params) {
@@ -137,7 +158,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *stage_a = smem;
     uint8_t *stage_b = smem + STAGES * A_STAGE_BYTES;
-    Control *control = reinterpret_cast<Control *>(smem + STAGES * STAGE_BYTES);
+    uint4 *epilogue_stage = reinterpret_cast<uint4 *>(smem + STAGES * STAGE_BYTES);
+    Control *control = reinterpret_cast<Control *>(smem + STAGES * STAGE_BYTES + EPILOGUE_STAGE_BYTES);
 
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
@@ -253,7 +275,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         __syncwarp();
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
+        // Lane l of warp w reads TMEM lane (w % 4) * 32 + l, i.e. one output row, 32 columns per
+        // tcgen05.ld. The values are converted in registers, written to this warp's 4 KB staging
+        // buffer as 8 x 16 bytes per row (16-byte slot c of row r at c ^ (r & 7): conflict-free
+        // both ways), then read back row-wise: 8 lanes cover one row's 32 columns, so each store
+        // instruction writes four 128-byte row segments, to `out` and to every peer destination.
         const uint32_t quarter = warp & 3u;  // TMEM lanes this warp may access
+        uint4 *staging = epilogue_stage + (warp - 2u) * 256u;
+        const bool s32 = params.mode == static_cast<int>(EpilogueMode::kStoreS32);
+        const bool with_bias = params.mode == static_cast<int>(EpilogueMode::kDequantizeBias);
+        bool aligned = (params.out_stride & 3u) == 0 && (reinterpret_cast<uintptr_t>(params.out) & 15u) == 0;
+#pragma unroll
+        for (uint32_t d = 0; d < kGemmMaxPeers; ++d)
+            if (d < params.peer_count) aligned = aligned && (reinterpret_cast<uintptr_t>(params.peer_out[d]) & 15u) == 0;
         uint32_t local_tile = 0;
         for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local_tile) {
             const uint32_t acc = local_tile & 1u;
@@ -267,57 +301,54 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (!ok) break;
             tc_fence_after();
 
-            const uint32_t m = m_block * BM + quarter * 32 + lane;
-            const bool row_ok = m < params.m;
-            const float row_scale =
-                (row_ok && params.mode != static_cast<int>(EpilogueMode::kStoreS32)) ? params.row_scales[m] : 0.0f;
+            const uint32_t row0 = m_block * BM + quarter * 32;  // first row of this warp
+            const uint32_t m = row0 + lane;
+            const float row_scale = (m < params.m && !s32) ? params.row_scales[m] : 0.0f;
             const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN;
 #pragma unroll 1
             for (uint32_t chunk = 0; chunk < BN / 32; ++chunk) {
                 uint32_t r[32];
                 tmem_load_32x32b_x32(taddr + chunk * 32, r);
                 const uint32_t n0 = n_base + chunk * 32;
-                if (!row_ok || n0 >= params.n) continue;
-                const bool full_chunk = n0 + 32 <= params.n;
-                if (params.mode == static_cast<int>(EpilogueMode::kStoreS32)) {
-                    int32_t *row = static_cast<int32_t *>(params.out) + static_cast<size_t>(m) * params.out_stride + n0;
-                    if (full_chunk && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<int4 *>(row + j) = make_int4(static_cast<int>(r[j]), static_cast<int>(r[j + 1]),
-                                                                           static_cast<int>(r[j + 2]), static_cast<int>(r[j + 3]));
-                    } else {
-                        for (uint32_t j = 0; j < 32 && n0 + j < params.n; ++j) row[j] = static_cast<int>(r[j]);
-                    }
-                } else {
+                if (n0 >= params.n) continue;  // warp-uniform
+                if (!s32) {
                     // Column scales / bias: every lane reads the same address (an L1 broadcast).
-                    const float *cs = params.col_scales + n0;
-                    const float *cb = params.bias + n0;
-                    const bool with_bias = params.mode == static_cast<int>(EpilogueMode::kDequantizeBias);
-                    float *row = static_cast<float *>(params.out) + static_cast<size_t>(m) * params.out_stride + n0;
-                    if (full_chunk && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
-                        float v[32];
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            v[j] = dequant(r[j], row_scale, __ldg(cs + j));
-                            if (with_bias) v[j] = __fadd_rn(v[j], __ldg(cb + j));
-                        }
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4 *>(row + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                    } else {
-                        for (uint32_t j = 0; j < 32 && n0 + j < params.n; ++j) {
-                            float v = dequant(r[j], row_scale, __ldg(cs + j));
-                            if (with_bias) v = __fadd_rn(v, __ldg(cb + j));
-                            row[j] = v;
-                        }
+                    for (uint32_t j = 0; j < 32; ++j) {
+                        const bool in_range = n0 + j < params.n;
+                        float v = dequant(r[j], row_scale, in_range ? __ldg(params.col_scales + n0 + j) : 0.0f);
+                        if (with_bias) v = __fadd_rn(v, in_range ? __ldg(params.bias + n0 + j) : 0.0f);
+                        r[j] = __float_as_uint(v);
                     }
                 }
+#pragma unroll
+                for (uint32_t c = 0; c < 8; ++c)
+                    staging[lane * 8u + (c ^ (lane & 7u))] = make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+                __syncwarp();
+                const uint32_t c = lane & 7u;
+                const uint32_t col = n0 + c * 4u;
+#pragma unroll
+                for (uint32_t k = 0; k < 8; ++k) {
+                    const uint32_t i = k * 4u + (lane >> 3);
+                    const uint4 value = staging[i * 8u + (c ^ (i & 7u))];
+                    const uint32_t row = row0 + i;
+                    if (row < params.m && col < params.n) {
+                        const size_t offset = static_cast<size_t>(row) * params.out_stride + col;
+                        const uint32_t valid = params.n - col;
+                        store_group(params.out, offset, value, valid, aligned);
+#pragma unroll
+                        for (uint32_t d = 0; d < kGemmMaxPeers; ++d)
+                            if (d < params.peer_count) store_group(params.peer_out[d], offset, value, valid, aligned);
+                    }
+                }
+                __syncwarp();
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(&control->tmem_empty[acc]));
         }
+        // Peer destinations: make this thread's remote stores visible system-wide before exit.
+        if (params.peer_count != 0) __threadfence_system();
     }
 
     tc_fence_before();
@@ -357,6 +388,9 @@ cudaError_t launch_w8a8_gemm_sm100(const CUtensorMap *map_a, const CUtensorMap *
     params.bias = epilogue.bias;
     params.out = epilogue.out;
     params.out_stride = epilogue.out_stride;
+    if (epilogue.peer_count > kGemmMaxPeers) return cudaErrorInvalidValue;
+    params.peer_count = epilogue.peer_count;
+    for (uint32_t d = 0; d < kGemmMaxPeers; ++d) params.peer_out[d] = d < epilogue.peer_count ? epilogue.peer_out[d] : nullptr;
     params.error_word = error_word;
     const uint32_t tiles = params.m_blocks * params.n_blocks;
     const uint32_t grid = tiles < static_cast<uint32_t>(sm_count) ? tiles : static_cast<uint32_t>(sm_count);

@@ -186,6 +186,12 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         _S,
         [_P, _P, c_size_t, c_uint32, _P, c_size_t, _P, _P, c_uint32, c_uint32, _P, c_size_t],
     ),
+    # qpucuda_peer.h
+    "qpucuda_peer_buffer_create": (_S, [_P, c_size_t, POINTER(c_void_p), c_char_p]),
+    "qpucuda_peer_buffer_open": (_S, [_P, c_char_p, POINTER(c_void_p)]),
+    "qpucuda_peer_buffer_close": (_S, [_P, _P]),
+    "qpucuda_peer_buffer_destroy": (_S, [_P, _P]),
+    "qpucuda_w8a8_linear_execute_device_fanout": (_S, [_P, _P, c_size_t, c_uint32, _P, POINTER(c_void_p), c_uint32, c_size_t]),
     # qpucuda_q4_0.h
     "qpucuda_q4_0_linear_prepare": (_S, [_P, POINTER(Q40LinearDesc), POINTER(c_void_p)]),
     "qpucuda_q4_0_linear_destroy": (None, [_P]),

@@ -17,7 +17,7 @@ across GPUs.
 from __future__ import annotations
 
 import ctypes
-from collections.abc import Iterable
+from collections.abc import Iterable, Sequence
 from dataclasses import dataclass
 from typing import Any, Self
 
@@ -320,6 +320,30 @@ class PreparedW8A8Linear:
             ),
         )
         return out
+
+    def forward_fanout(self: Self, source: Any, destination: int, peer_destinations: Sequence[int], destination_stride: int) -> None:
+        """``qpucuda_w8a8_linear_execute_device_fanout`` on the current stream: the fp32 outputs
+        ``[batch, count]`` go to ``destination`` (a device address) and to every address in
+        ``peer_destinations`` (other ranks' mapped buffers), rows ``destination_stride`` floats
+        apart. No counterpart in the reference (the fused GEMM + all-gather of the N-split)."""
+        import torch
+
+        if self._closed:
+            raise RuntimeError("prepared W8A8 linear plan is closed")
+        batch = source.shape[0]
+        if source.dtype != torch.float32 or source.dim() != 2 or source.shape[1] != self.weight.shape[1] or source.stride(1) != 1:
+            raise ValueError("prepared W8A8 linear requires a row-major float32 [batch, K] source")
+        peers = (ctypes.c_void_p * max(1, len(peer_destinations)))(*[ctypes.c_void_p(int(p)) for p in peer_destinations])
+        handle = self._handle
+        self._backend.launch(  # type: ignore[attr-defined]
+            torch.cuda.current_stream(source.device),
+            lambda native: native.check(
+                native.library.qpucuda_w8a8_linear_execute_device_fanout(
+                    handle, source.data_ptr(), source.stride(0), batch, int(destination), peers, len(peer_destinations), destination_stride
+                ),
+                "qpucuda_w8a8_linear_execute_device_fanout",
+            ),
+        )
 
     def execute_host(self: Self, source: npt.NDArray[np.float32], destination: npt.NDArray[np.float32] | None = None) -> npt.NDArray[np.float32]:
         """Host buffers through ``qpucuda_w8a8_linear_execute`` (synchronous, bounded wait)."""

@@ -7,13 +7,18 @@ them (src/qpu_xla/models/tinyllama/quantization.py:350-514; Q4_0
 Here the two sides become ``world_size`` GPUs, one process each: rank r holds
 weight rows ``[start_r, start_r + count_r)`` (a multiple of the tile width
 except for the last rank), every rank computes the same activations' product
-with its slice, and one all-gather over NVLink (NCCL) joins the column blocks.
-Ranks quantize identical activations with the same deterministic kernel, so
-the joined output equals the single-GPU output bit for bit.
+with its slice, and the column blocks are joined over NVLink: either by the GEMM
+itself (``PeerOutput`` + ``ShardedW8A8Linear.forward_fused``: the epilogue stores
+each finished tile into every rank's full output, mapped with CUDA IPC, followed
+by one small NCCL all-reduce as the barrier) or by an NCCL all-gather after the
+GEMM (``forward``). Ranks quantize identical activations with the same
+deterministic kernel, so the joined output equals the single-GPU output bit for
+bit.
 """
 
 from __future__ import annotations
 
+import ctypes
 import math
 from typing import Any, Self
 
@@ -73,6 +78,86 @@ class ColumnGather:
         return out
 
 
+class PeerOutput:
+    """One full ``[rows, total]`` fp32 output per rank, in device memory that every other rank
+    of the group maps (``qpucuda_peer_buffer_*``, CUDA IPC), for ``forward_fused``.
+
+    Collective: every rank of ``group`` constructs and closes it together. ``tensor`` is this
+    rank's buffer as a torch view (valid until ``close``). A buffer must not be written by a new
+    fused call until every rank has finished reading the previous result from it.
+    """
+
+    def __init__(self: Self, device: Device, rows: int, total: int, *, group: Any = None) -> None:
+        import torch
+        import torch.distributed as dist
+
+        self.world_size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rows = rows
+        self.total = total
+        self._group = group
+        self._native = device.backend.native  # type: ignore[attr-defined]
+        library, context = self._native.library, self._native.handle
+        pointer = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        self._native.check(library.qpucuda_peer_buffer_create(context, rows * total * 4, ctypes.byref(pointer), handle), "qpucuda_peer_buffer_create")
+        self._own = int(pointer.value)  # type: ignore[arg-type]
+        handles: list[Any] = [None] * self.world_size
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._bases: dict[int, int] = {self.rank: self._own}
+        self._opened: list[int] = []
+        try:
+            for peer, peer_handle in enumerate(handles):
+                if peer == self.rank:
+                    continue
+                mapped = ctypes.c_void_p()
+                self._native.check(library.qpucuda_peer_buffer_open(context, peer_handle, ctypes.byref(mapped)), "qpucuda_peer_buffer_open")
+                self._bases[peer] = int(mapped.value)  # type: ignore[arg-type]
+                self._opened.append(self._bases[peer])
+        except Exception:
+            self._release()
+            raise
+        interface = {"shape": (rows, total), "typestr": "<f4", "data": (self._own, False), "version": 3, "strides": None}
+        holder = type("PeerOutputView", (), {"__cuda_array_interface__": interface})()
+        self.tensor = torch.as_tensor(holder, device=device.backend.torch_device)  # type: ignore[attr-defined]
+        self._closed = False
+
+    def slice_pointers(self: Self, column_start: int) -> tuple[int, list[int]]:
+        """Device addresses of column ``column_start`` of row 0: this rank's buffer, then every
+        other rank's mapped buffer in rank order."""
+        offset = 4 * column_start
+        return self._own + offset, [self._bases[r] + offset for r in range(self.world_size) if r != self.rank]
+
+    def _release(self: Self) -> None:
+        library, context = self._native.library, self._native.handle
+        for mapped in self._opened:
+            library.qpucuda_peer_buffer_close(context, mapped)
+        self._opened = []
+        if self._own:
+            library.qpucuda_peer_buffer_destroy(context, self._own)
+            self._own = 0
+
+    def close(self: Self) -> None:
+        """Collective: no rank writes into any buffer after the first barrier, and no buffer is
+        freed before every rank has unmapped it."""
+        import torch
+        import torch.distributed as dist
+
+        if self._closed:
+            return
+        self._closed = True
+        torch.cuda.synchronize()
+        dist.barrier(group=self._group)
+        library, context = self._native.library, self._native.handle
+        for mapped in self._opened:
+            library.qpucuda_peer_buffer_close(context, mapped)
+        self._opened = []
+        dist.barrier(group=self._group)
+        del self.tensor
+        library.qpucuda_peer_buffer_destroy(context, self._own)
+        self._own = 0
+
+
 class ShardedW8A8Linear:
     """One W8A8 linear split along N over the ranks of a process group (NCCL, one GPU per rank)."""
 
@@ -112,6 +197,24 @@ class ShardedW8A8Linear:
     def forward(self: Self, source: Any, out: Any = None) -> Any:
         """Full ``[rows, N]`` output on every rank."""
         return self.gather.gather(self.forward_local(source), out)
+
+    def forward_fused(self: Self, source: Any, output: PeerOutput) -> Any:
+        """Full ``[rows, N]`` output on every rank, joined by the GEMM epilogue itself: this
+        rank's columns are stored into every rank's ``output`` buffer as each tile finishes,
+        then a one-element NCCL all-reduce on the same stream orders every rank's stores before
+        anything that follows. Returns ``output.tensor``."""
+        import torch
+        import torch.distributed as dist
+
+        if output.total != self.out_features or source.shape[0] > output.rows:
+            raise ValueError("peer output must be [rows >= batch, out_features]")
+        if self.local is not None:
+            destination, peers = output.slice_pointers(self.gather.start)
+            self.local.forward_fanout(source, destination, peers, output.total)
+        if getattr(self, "_barrier", None) is None:
+            self._barrier = torch.zeros(1, dtype=torch.float32, device=source.device)
+        dist.all_reduce(self._barrier, group=self.gather.group)
+        return output.tensor[: source.shape[0]]
 
     def close(self: Self) -> None:
         if self.local is not None:
@@ -153,4 +256,4 @@ class ShardedQ4_0Linear:
             self.local.close()
 
 
-__all__ = ["ColumnGather", "ShardedQ4_0Linear", "ShardedW8A8Linear", "shard_bounds", "shard_width"]
+__all__ = ["ColumnGather", "PeerOutput", "ShardedQ4_0Linear", "ShardedW8A8Linear", "shard_bounds", "shard_width"]

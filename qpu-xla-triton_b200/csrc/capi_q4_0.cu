@@ -380,11 +380,11 @@ qpucuda_status qpucuda_q4_0_linear_execute_f32_device(qpucuda_q4_0_linear *linea
     qpucuda_status status = begin_submit(context);
     if (status != QPUCUDA_OK) return status;
     DeviceGuard guard(context->device);
-    cudaError_t error = launch_quantize_q8_0(source, source_stride, rows, k, linear->d_activation, context->stream);
-    if (error == cudaSuccess)
-        error = launch_q4_0_q8_0_gemv(weights_of(linear), linear->d_activation, rows, 0, destination,
-                                      destination_stride, local_start, output_column_start, column_count,
-                                      context->d_error, context->sm_count, context->stream);
+    // One launch: each CTA quantizes the fp32 blocks to Q8_0 as it stages them (the same
+    // arithmetic as qpucuda_quantize_q8_0, so the result is that of quantize-then-execute).
+    const cudaError_t error = launch_q4_0_f32_gemv(weights_of(linear), source, source_stride, rows, destination,
+                                                   destination_stride, local_start, output_column_start, column_count,
+                                                   context->sm_count, context->stream);
     if (error != cudaSuccess) return cuda_fail(context, error, "launch Q4_0 linear");
     return QPUCUDA_OK;
 }

@@ -37,6 +37,9 @@ struct ActivationView {
     uint32_t rows;
     uint32_t blocks;
     uint32_t interleave;  // 0 native; 4 / 8 CPU_REPACK block_q8_0x4 groups
+    // fp32 rows instead of Q8_0 blocks: each block is quantized to Q8_0 while it is staged.
+    const float *f32;
+    size_t f32_stride;  // elements
 };
 
 // Address of the fp16 scale and of value `index` of (row, block), following the
@@ -86,6 +89,44 @@ __device__ __forceinline__ StagedActivation staged_activation(uint8_t *smem, uin
 
 size_t activation_bytes(uint32_t rows, uint32_t blocks) { return static_cast<size_t>(rows) * blocks * (16 + 16 + 8); }
 
+// Q8_0 quantization of one block of 32 fp32 values, exactly as quantize_q8_0_kernel (and the
+// reference's restatement of ggml's quantize_row_q8_0, examples/benchmark_llama_cpp_qpu_
+// persistent_q4.py:42-54): d = amax / 127, q = rint(x * (1/d)) clamped to +-127, fp16(d) kept.
+__device__ __forceinline__ void quantize_f32_block(const float *x, bool vector, uint32_t (&words)[8],
+                                                   uint16_t &scale_bits) {
+    float v[32];
+    if (vector) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 f = __ldg(reinterpret_cast<const float4 *>(x) + i);
+            v[4 * i] = f.x;
+            v[4 * i + 1] = f.y;
+            v[4 * i + 2] = f.z;
+            v[4 * i + 3] = f.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __ldg(x + i);
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const float d = __fdiv_rn(amax, 127.0f);
+    const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            int q = __float2int_rn(__fmul_rn(v[4 * w + b], id));
+            q = q < -127 ? -127 : (q > 127 ? 127 : q);
+            word |= static_cast<uint32_t>(static_cast<uint8_t>(static_cast<int8_t>(q))) << (8 * b);
+        }
+        words[w] = word;
+    }
+    scale_bits = __half_as_ushort(__float2half_rn(d));
+}
+
 __device__ __forceinline__ void read_activation_item(const ActivationView &view, uint32_t item, uint32_t (&words)[8],
                                                      uint16_t &scale_bits) {
     const uint32_t row = item / view.blocks;
@@ -124,10 +165,25 @@ __device__ __forceinline__ void write_activation_item(const StagedActivation &st
     staged.meta[item] = make_int2(__float_as_int(__half2float(__ushort_as_half(scale_bits))), -8 * sum);
 }
 
-// One thread per (row, block) item, two items per trip so two L2 round trips overlap.
+// One thread per (row, block) item, two items per trip so two L2 round trips overlap. With
+// F32, the items are quantized from fp32 rows (one per trip: 32 values in registers each).
+template <bool F32>
 __device__ __forceinline__ void stage_activation(const ActivationView &view, const StagedActivation &staged,
                                                  uint32_t thread, uint32_t threads) {
     const uint32_t total = view.rows * view.blocks;
+    if constexpr (F32) {
+        const bool vector = (reinterpret_cast<uintptr_t>(view.f32) & 15u) == 0 && (view.f32_stride & 3u) == 0;
+        for (uint32_t item = thread; item < total; item += threads) {
+            const uint32_t row = item / view.blocks;
+            const uint32_t block = item % view.blocks;
+            uint32_t words[8];
+            uint16_t scale;
+            quantize_f32_block(view.f32 + static_cast<size_t>(row) * view.f32_stride + static_cast<size_t>(block) * 32,
+                               vector, words, scale);
+            write_activation_item(staged, item, words, scale);
+        }
+        return;
+    }
     for (uint32_t item = thread; item < total; item += 2 * threads) {
         uint32_t words0[8], words1[8];
         uint16_t scale0, scale1 = 0;
@@ -219,7 +275,7 @@ struct DirectParams {
 // current one, so the weight stream does not stop for either. Partial sums of a group's
 // SPLIT warps are added in part order through shared memory (deterministic). Registers per
 // thread are capped so that MIN_BLOCKS CTAs of 256 threads fit on an SM.
-template <int ROWS, int SPLIT, int COLS, int UNROLL, int MIN_BLOCKS>
+template <int ROWS, int SPLIT, int COLS, int UNROLL, int MIN_BLOCKS, bool F32>
 __global__ void __launch_bounds__(kThreads, MIN_BLOCKS) q4_0_direct_kernel(const DirectParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float partial[kWarps][ROWS * COLS];
@@ -278,7 +334,7 @@ __global__ void __launch_bounds__(kThreads, MIN_BLOCKS) q4_0_direct_kernel(const
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const StagedActivation staged = staged_activation(smem, ROWS * blocks);
-    stage_activation(p.view, staged, threadIdx.x, blockDim.x);
+    stage_activation<F32>(p.view, staged, threadIdx.x, blockDim.x);
     __syncthreads();
 
     for (; group < groups; group += gridDim.x * kSlots) {
@@ -356,7 +412,7 @@ template <int ROWS>
 __global__ void __launch_bounds__(kNativeThreads) q4_0_native_kernel(const NativeParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const StagedActivation staged = staged_activation(smem, ROWS * p.blocks);
-    stage_activation(p.view, staged, threadIdx.x, blockDim.x);
+    stage_activation<false>(p.view, staged, threadIdx.x, blockDim.x);
     __syncthreads();
     const uint32_t lane = threadIdx.x & 31;
     for (uint32_t j = blockIdx.x * kNativeWarps + (threadIdx.x >> 5); j < p.count; j += gridDim.x * kNativeWarps) {
@@ -387,11 +443,11 @@ __global__ void __launch_bounds__(kNativeThreads) q4_0_native_kernel(const Nativ
     }
 }
 
-template <int ROWS, int SPLIT, int COLS, int UNROLL, int MIN_BLOCKS>
+template <int ROWS, int SPLIT, int COLS, int UNROLL, int MIN_BLOCKS, bool F32>
 cudaError_t launch_direct(const DirectParams &p, int sm_count, cudaStream_t stream) {
     const size_t smem = activation_bytes(ROWS, p.blocks);
     if (smem > kSmemBudget) return cudaErrorInvalidValue;
-    auto kernel = q4_0_direct_kernel<ROWS, SPLIT, COLS, UNROLL, MIN_BLOCKS>;
+    auto kernel = q4_0_direct_kernel<ROWS, SPLIT, COLS, UNROLL, MIN_BLOCKS, F32>;
     if (smem > 48u * 1024u) {
         const cudaError_t error =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -421,7 +477,7 @@ cudaError_t launch_direct(const DirectParams &p, int sm_count, cudaStream_t stre
     return cudaLaunchKernelEx(&config, kernel, p);
 }
 
-template <int ROWS>
+template <int ROWS, bool F32 = false>
 cudaError_t launch_rows(const DirectParams &p, int sm_count, cudaStream_t stream) {
     // Two columns per warp halve the shared-memory reads per weight byte. One row: four blocks
     // of each column in flight per lane within 80 registers (3 CTAs per SM). Two rows: two
@@ -433,12 +489,12 @@ cudaError_t launch_rows(const DirectParams &p, int sm_count, cudaStream_t stream
     // independent groups of the unsplit kernel, so the grid fills the SMs even when the matrix
     // is narrow (a column shard), and 14 loads in flight per lane within 128 registers.
     if constexpr (ROWS == 1) {
-        if (p.blocks >= 640) return launch_direct<ROWS, 4, 2, 7, 2>(p, sm_count, stream);
-        return launch_direct<ROWS, 1, 2, 4, 3>(p, sm_count, stream);
+        if (p.blocks >= 640) return launch_direct<ROWS, 4, 2, 7, 2, F32>(p, sm_count, stream);
+        return launch_direct<ROWS, 1, 2, 4, 3, F32>(p, sm_count, stream);
     } else if constexpr (ROWS == 2) {
-        return launch_direct<ROWS, 1, 2, 2, 3>(p, sm_count, stream);
+        return launch_direct<ROWS, 1, 2, 2, 3, F32>(p, sm_count, stream);
     } else {
-        return launch_direct<ROWS, 1, 2, 4, 2>(p, sm_count, stream);
+        return launch_direct<ROWS, 1, 2, 4, 2, F32>(p, sm_count, stream);
     }
 }
 
@@ -476,7 +532,7 @@ cudaError_t launch_q4_0_q8_0_gemv(const Q40Weights &weights, const uint8_t *acti
     p.scales = weights.scales;
     p.blocks = weights.blocks;
     p.scale_stride = weights.scale_stride;
-    p.view = ActivationView{activation, rows, weights.blocks, interleave};
+    p.view = ActivationView{activation, rows, weights.blocks, interleave, nullptr, 0};
     p.destination = destination;
     p.destination_stride = destination_stride;
     p.col0 = col0;
@@ -492,6 +548,35 @@ cudaError_t launch_q4_0_q8_0_gemv(const Q40Weights &weights, const uint8_t *acti
     }
 }
 
+cudaError_t launch_q4_0_f32_gemv(const Q40Weights &weights, const float *source, size_t source_stride, uint32_t rows,
+                                 float *destination, size_t destination_stride, uint32_t col0, uint32_t out_col0,
+                                 uint32_t count, int sm_count, cudaStream_t stream) {
+    if (count == 0 || rows == 0) return cudaSuccess;
+    if ((reinterpret_cast<uintptr_t>(weights.nibbles) & 15u) != 0 || (reinterpret_cast<uintptr_t>(weights.scales) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(source) & 3u) != 0 || weights.scale_stride % 8 != 0 ||
+        weights.scale_stride < weights.blocks || source_stride < static_cast<size_t>(weights.blocks) * 32) {
+        return cudaErrorInvalidValue;
+    }
+    DirectParams p{};
+    p.nibbles = weights.nibbles;
+    p.scales = weights.scales;
+    p.blocks = weights.blocks;
+    p.scale_stride = weights.scale_stride;
+    p.view = ActivationView{nullptr, rows, weights.blocks, 0, source, source_stride};
+    p.destination = destination;
+    p.destination_stride = destination_stride;
+    p.col0 = col0;
+    p.out_col0 = out_col0;
+    p.count = count;
+    switch (rows) {
+        case 1: return launch_rows<1, true>(p, sm_count, stream);
+        case 2: return launch_rows<2, true>(p, sm_count, stream);
+        case 3: return launch_rows<3, true>(p, sm_count, stream);
+        case 4: return launch_rows<4, true>(p, sm_count, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
 cudaError_t launch_q4_0_q8_0_gemv_native(const uint8_t *activation, uint32_t rows, uint32_t blocks,
                                          const uint8_t *weight, float *destination, size_t destination_stride,
                                          uint32_t col0, uint32_t out_col0, uint32_t count, int sm_count,
@@ -500,8 +585,8 @@ cudaError_t launch_q4_0_q8_0_gemv_native(const uint8_t *activation, uint32_t row
     if ((reinterpret_cast<uintptr_t>(weight) & 1u) != 0 || (reinterpret_cast<uintptr_t>(activation) & 1u) != 0) {
         return cudaErrorInvalidValue;
     }
-    const NativeParams p{weight, blocks, ActivationView{activation, rows, blocks, 0}, destination, destination_stride,
-                         col0, out_col0, count};
+    const NativeParams p{weight, blocks, ActivationView{activation, rows, blocks, 0, nullptr, 0}, destination,
+                         destination_stride, col0, out_col0, count};
     switch (rows) {
         case 1: return launch_native<1>(p, sm_count, stream);
         case 2: return launch_native<2>(p, sm_count, stream);

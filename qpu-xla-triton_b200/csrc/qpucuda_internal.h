@@ -139,6 +139,11 @@ cudaError_t launch_q4_0_q8_0_gemv(const Q40Weights &weights, const uint8_t *acti
                                   uint32_t interleave, float *destination, size_t destination_stride,
                                   uint32_t col0, uint32_t out_col0, uint32_t count, unsigned int *error_word,
                                   int sm_count, cudaStream_t stream);
+// Same, with fp32 activation rows quantized to Q8_0 block by block while each CTA stages them
+// (bit-identical to quantizing first and running the Q8_0 kernel, in one launch).
+cudaError_t launch_q4_0_f32_gemv(const Q40Weights &weights, const float *source, size_t source_stride, uint32_t rows,
+                                 float *destination, size_t destination_stride, uint32_t col0, uint32_t out_col0,
+                                 uint32_t count, int sm_count, cudaStream_t stream);
 // Native 18-byte blocks [columns][blocks][18] -> prepared layout (scales rows of scale_stride,
 // the padding must be zeroed beforehand).
 cudaError_t launch_q4_0_repack(const uint8_t *native, uint32_t columns, uint32_t blocks, uint32_t scale_stride,

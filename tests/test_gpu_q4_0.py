@@ -238,6 +238,20 @@ def test_long_reductions_over_windows(native, k: int, n: int, rows: int) -> None
         expected = oracle.q4_0_q8_0_linear(activation.cpu().numpy(), weight_blocks[column_start : column_start + column_count])
         assert max_relative_error(got[:, out_start : out_start + column_count], expected) <= Q4_0_TOLERANCE
         assert np.isnan(got[:, :out_start]).all() and np.isnan(got[:, out_start + column_count :]).all()
+        # fp32 rows quantized inside the kernel: bit-identical to quantize-then-execute, also from
+        # rows whose stride is not a multiple of 4 floats (scalar loads)
+        for pad in (0, 1):
+            padded = torch.empty((rows, k + pad), dtype=torch.float32, device="cuda")
+            padded[:, :k].copy_(source)
+            fused = torch.full_like(out, float("nan"))
+            native.context.check(
+                native.lib.qpucuda_q4_0_linear_execute_f32_device(
+                    handle, padded.data_ptr(), padded.stride(0), rows, fused.data_ptr(), fused.shape[1], column_start, column_count, out_start
+                ),
+                "execute_f32_device",
+            )
+            native.sync()
+            np.testing.assert_array_equal(fused.cpu().numpy(), got)
     finally:
         native.lib.qpucuda_q4_0_linear_destroy(handle)
 

@@ -102,6 +102,19 @@ qpucuda_status qpucuda_quantize_q8_0(
     const float *x, size_t x_stride, uint32_t rows, uint32_t cols,
     uint8_t *blocks);
 
+/* im2col of one channel group of an NCHW fp32 tensor for a convolution, as the
+ * reference's _im2col_nchw (src/qpu_xla/ops/conv2d.py:47-79): row (b, oh, ow) of the
+ * [batch * output_height * output_width][group_channels * kernel_height * kernel_width]
+ * destination holds, at column (c * kernel_height + i) * kernel_width + j, the source
+ * value at channel channel_offset + c, row oh * stride_h - pad_h + i * dilation_h,
+ * column ow * stride_w - pad_w + j * dilation_w, or 0 inside the padding. */
+qpucuda_status qpucuda_im2col_nchw_f32(
+    qpucuda_context *context,
+    const float *source, uint32_t batch, uint32_t channels, uint32_t height, uint32_t width,
+    uint32_t channel_offset, uint32_t group_channels, uint32_t kernel_height, uint32_t kernel_width,
+    uint32_t stride_h, uint32_t stride_w, uint32_t pad_h, uint32_t pad_w, uint32_t dilation_h,
+    uint32_t dilation_w, float *destination, size_t destination_stride);
+
 /* fp32 rows -> native block_q4_0 [rows][cols/32][18] (ggml's published
  * quantize_row_q4_0_ref: d = signed max-magnitude / -8, codes min(15, trunc(x/d + 8.5))). */
 qpucuda_status qpucuda_quantize_q4_0(

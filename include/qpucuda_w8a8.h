@@ -105,6 +105,28 @@ qpucuda_status qpucuda_w8a8_linear_execute_prepared_device(
     float *destination,
     size_t destination_stride);
 
+/* A matrix view over device memory: element (r, c) lies at
+ *   (r / rows_per_batch) * batch_stride + (r % rows_per_batch) * row_stride + c * column_stride
+ * elements from the base pointer (rows_per_batch 0 = all rows in one batch).
+ * Row-major [rows][ld] is {0, 0, ld, 1}; an NCHW tensor seen as pixels x channels
+ * (the reference's pointwise lowering, src/qpu_xla/ops/conv2d.py:93-96) is
+ * {H*W, C*H*W, 1, H*W} with the base at channel 0 of the range used. */
+typedef struct qpucuda_matrix_layout {
+    uint64_t rows_per_batch;
+    uint64_t batch_stride;
+    uint64_t row_stride;
+    uint64_t column_stride;
+} qpucuda_matrix_layout;
+
+/* qpucuda_w8a8_linear_execute_device over arbitrary source and destination layouts
+ * (source: rows x input features, destination: rows x resident columns). Used by the
+ * W8A8 convolution plan to read NCHW pixels and write NCHW outputs in place, with no
+ * transpose copies. Non row-major destinations always take the tcgen05 GEMM path. */
+qpucuda_status qpucuda_w8a8_linear_execute_device_layout(
+    qpucuda_w8a8_linear *linear,
+    const float *source, const qpucuda_matrix_layout *source_layout, uint32_t rows,
+    float *destination, const qpucuda_matrix_layout *destination_layout);
+
 /* Read back the plan scratch after an execute (device pointers, valid until
  * the next call): int8 activations [max_batch][padded K] and fp32 row scales. */
 qpucuda_status qpucuda_w8a8_linear_scratch(

@@ -114,6 +114,66 @@ def w8a8_linear(
 
 
 # --------------------------------------------------------------------------
+# W8A8 convolution (src/qpu_xla/ops/conv2d.py, src/qpu_xla/ops/conv2d_w8a8.py)
+# --------------------------------------------------------------------------
+
+
+def conv_output_hw(height: int, width: int, kernel: tuple[int, int], stride: tuple[int, int], padding: tuple[int, int], dilation: tuple[int, int]) -> tuple[int, int]:
+    """Valid NCHW output size (conv2d.py:25-39)."""
+    output_height = (height + 2 * padding[0] - dilation[0] * (kernel[0] - 1) - 1) // stride[0] + 1
+    output_width = (width + 2 * padding[1] - dilation[1] * (kernel[1] - 1) - 1) // stride[1] + 1
+    if output_height <= 0 or output_width <= 0:
+        raise ValueError("convolution parameters produce an empty output")
+    return output_height, output_width
+
+
+def im2col_nchw(
+    source: npt.NDArray[np.float32], kernel: tuple[int, int], *, stride: tuple[int, int], padding: tuple[int, int], dilation: tuple[int, int]
+) -> npt.NDArray[np.float32]:
+    """Rows (b, oh, ow), columns (c, i, j): the source value at (c, oh*s - p + i*d, ow*s - p + j*d),
+    zero in the padding (``_im2col_nchw``, conv2d.py:47-79), written as explicit gathers."""
+    batch, channels, height, width = source.shape
+    output_height, output_width = conv_output_hw(height, width, kernel, stride, padding, dilation)
+    padded = np.zeros((batch, channels, height + 2 * padding[0], width + 2 * padding[1]), dtype=source.dtype)
+    padded[:, :, padding[0] : padding[0] + height, padding[1] : padding[1] + width] = source
+    columns = np.empty((batch, output_height, output_width, channels, kernel[0], kernel[1]), dtype=source.dtype)
+    rows_index = np.arange(output_height) * stride[0]
+    cols_index = np.arange(output_width) * stride[1]
+    for i in range(kernel[0]):
+        for j in range(kernel[1]):
+            window = padded[:, :, rows_index[:, None] + i * dilation[0], cols_index[None, :] + j * dilation[1]]
+            columns[:, :, :, :, i, j] = window.transpose(0, 2, 3, 1)
+    return np.ascontiguousarray(columns.reshape(batch * output_height * output_width, channels * kernel[0] * kernel[1]))
+
+
+def conv2d_w8a8(
+    source: npt.NDArray[np.float32],
+    weight: npt.NDArray[np.float32],
+    *,
+    stride: tuple[int, int] = (1, 1),
+    padding: tuple[int, int] = (0, 0),
+    dilation: tuple[int, int] = (1, 1),
+    groups: int = 1,
+) -> npt.NDArray[np.float32]:
+    """Per-group dynamic W8A8 convolution, NCHW in and out: each group's im2col rows through
+    ``w8a8_linear`` with its output channels' weights quantized per channel, then the pixels x
+    channels matrix back to NCHW (conv2d_w8a8.py:111-137, :171-305; the reference test's
+    ``_dynamic_group_reference``, tests/test_qpu_xla_conv2d_w8a8.py:14-54)."""
+    batch, channels, height, width = source.shape
+    outputs, group_channels, kernel_height, kernel_width = weight.shape
+    output_height, output_width = conv_output_hw(height, width, (kernel_height, kernel_width), stride, padding, dilation)
+    rows = batch * output_height * output_width
+    lowered = im2col_nchw(source, (kernel_height, kernel_width), stride=stride, padding=padding, dilation=dilation).reshape(rows, channels, kernel_height, kernel_width)
+    output_group = outputs // groups
+    results = []
+    for group in range(groups):
+        matrix = np.ascontiguousarray(lowered[:, group * group_channels : (group + 1) * group_channels].reshape(rows, -1))
+        values, scales = quantize_per_output_channel_int8(np.ascontiguousarray(weight[group * output_group : (group + 1) * output_group].reshape(output_group, -1)))
+        results.append(w8a8_linear(matrix, values, scales))
+    return np.ascontiguousarray(np.concatenate(results, axis=1).reshape(batch, output_height, output_width, outputs).transpose(0, 3, 1, 2))
+
+
+# --------------------------------------------------------------------------
 # GGML Q4_0 / Q8_0 (src/qpu_xla/kernels/ggml_q4_0.py)
 # --------------------------------------------------------------------------
 

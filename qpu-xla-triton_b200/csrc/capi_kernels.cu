@@ -206,4 +206,36 @@ qpucuda_status qpucuda_quantize_q4_0(qpucuda_context *context, const float *x, s
     return launched(context, launch_quantize_q4_0(x, x_stride, rows, cols, blocks, context->stream), "quantize_q4_0");
 }
 
+qpucuda_status qpucuda_im2col_nchw_f32(qpucuda_context *context, const float *source, uint32_t batch, uint32_t channels,
+                                       uint32_t height, uint32_t width, uint32_t channel_offset,
+                                       uint32_t group_channels, uint32_t kernel_height, uint32_t kernel_width,
+                                       uint32_t stride_h, uint32_t stride_w, uint32_t pad_h, uint32_t pad_w,
+                                       uint32_t dilation_h, uint32_t dilation_w, float *destination,
+                                       size_t destination_stride) {
+    if (context == nullptr) return QPUCUDA_INVALID_ARGUMENT;
+    const uint64_t span_h = static_cast<uint64_t>(dilation_h) * (kernel_height == 0 ? 0 : kernel_height - 1) + 1;
+    const uint64_t span_w = static_cast<uint64_t>(dilation_w) * (kernel_width == 0 ? 0 : kernel_width - 1) + 1;
+    if (source == nullptr || destination == nullptr || batch == 0 || channels == 0 || height == 0 || width == 0 ||
+        group_channels == 0 || kernel_height == 0 || kernel_width == 0 || stride_h == 0 || stride_w == 0 ||
+        dilation_h == 0 || dilation_w == 0 || static_cast<uint64_t>(channel_offset) + group_channels > channels ||
+        static_cast<uint64_t>(height) + 2ull * pad_h < span_h || static_cast<uint64_t>(width) + 2ull * pad_w < span_w) {
+        return fail(context, QPUCUDA_INVALID_ARGUMENT, "im2col: invalid convolution shape");
+    }
+    const uint32_t output_height = static_cast<uint32_t>((height + 2ull * pad_h - span_h) / stride_h + 1);
+    const uint32_t output_width = static_cast<uint32_t>((width + 2ull * pad_w - span_w) / stride_w + 1);
+    if (destination_stride < static_cast<uint64_t>(group_channels) * kernel_height * kernel_width) {
+        return fail(context, QPUCUDA_INVALID_ARGUMENT, "im2col: destination rows are too short");
+    }
+    std::lock_guard<std::mutex> lock(context->mutex);
+    qpucuda_status status = begin_submit(context);
+    if (status != QPUCUDA_OK) return status;
+    DeviceGuard guard(context->device);
+    return launched(context,
+                    launch_im2col_nchw_f32(source, batch, channels, height, width, channel_offset, group_channels,
+                                           kernel_height, kernel_width, stride_h, stride_w, pad_h, pad_w, dilation_h,
+                                           dilation_w, output_height, output_width, destination, destination_stride,
+                                           context->stream),
+                    "im2col");
+}
+
 }  // extern "C"

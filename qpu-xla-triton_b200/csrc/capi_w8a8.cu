@@ -267,6 +267,62 @@ qpucuda_status qpucuda_w8a8_linear_execute_device_fanout(qpucuda_w8a8_linear *li
                       peer_destinations, peer_count);
 }
 
+qpucuda_status qpucuda_w8a8_linear_execute_device_layout(qpucuda_w8a8_linear *linear, const float *source,
+                                                         const qpucuda_matrix_layout *source_layout, uint32_t rows,
+                                                         float *destination,
+                                                         const qpucuda_matrix_layout *destination_layout) {
+    if (linear == nullptr) return QPUCUDA_INVALID_ARGUMENT;
+    qpucuda_context *context = linear->context;
+    if (source == nullptr || destination == nullptr || source_layout == nullptr || destination_layout == nullptr ||
+        rows == 0 || rows > linear->max_batch || source_layout->column_stride == 0 ||
+        destination_layout->column_stride == 0) {
+        return fail(context, QPUCUDA_INVALID_ARGUMENT, "W8A8 layout execute: invalid arguments");
+    }
+    // A layout whose rows would overlap (e.g. row-major with a row stride shorter than the row)
+    // is rejected; batches are taken as given.
+    if ((source_layout->column_stride == 1 && source_layout->row_stride < linear->k &&
+         (source_layout->rows_per_batch == 0 || source_layout->rows_per_batch > 1)) ||
+        (destination_layout->column_stride == 1 && destination_layout->row_stride < linear->columns &&
+         (destination_layout->rows_per_batch == 0 || destination_layout->rows_per_batch > 1))) {
+        return fail(context, QPUCUDA_INVALID_ARGUMENT, "W8A8 layout execute: rows overlap");
+    }
+    if (!(context->cc_major == 10 && context->cc_minor == 0)) {
+        return fail(context, QPUCUDA_CAPABILITY_MISSING, "the tcgen05 int8 GEMM needs an sm_100 device");
+    }
+    auto batch_rows = [rows](uint64_t value) {
+        return value == 0 || value >= rows ? 0xFFFFFFFFu : static_cast<uint32_t>(value);
+    };
+    std::lock_guard<std::mutex> lock(context->mutex);
+    qpucuda_status status = begin_submit(context);
+    if (status != QPUCUDA_OK) return status;
+    DeviceGuard guard(context->device);
+    cudaStream_t stream = context->stream;
+    const uint32_t source_rows_per_batch = batch_rows(source_layout->rows_per_batch);
+    cudaError_t error = launch_quantize_rows_int8_layout(
+        source, rows, linear->k, linear->k_pad, source_rows_per_batch == 0xFFFFFFFFu ? rows : source_rows_per_batch,
+        source_layout->batch_stride, source_layout->row_stride, source_layout->column_stride, linear->d_quantized,
+        linear->k_pad, linear->d_row_scales, stream);
+    if (error != cudaSuccess) return cuda_fail(context, error, "quantize activations");
+    GemmEpilogue epilogue;
+    epilogue.mode = linear->has_bias ? EpilogueMode::kDequantizeBias : EpilogueMode::kDequantize;
+    epilogue.row_scales = linear->d_row_scales;
+    epilogue.col_scales = linear->d_weight_scales;
+    epilogue.bias = linear->d_bias;
+    epilogue.out = destination;
+    epilogue.out_stride = destination_layout->row_stride;
+    epilogue.rows_per_batch = batch_rows(destination_layout->rows_per_batch);
+    epilogue.batch_stride = destination_layout->batch_stride;
+    epilogue.col_stride = destination_layout->column_stride;
+    error = linear->maps_ready
+                ? launch_w8a8_gemm_sm100(&linear->map_quantized, &linear->map_weight, rows, linear->columns,
+                                         linear->k_pad, epilogue, context->d_error, context->sm_count, stream)
+                : run_w8a8_gemm(linear->d_quantized, linear->k_pad, linear->d_weight, linear->k_pad, rows,
+                                linear->columns, linear->k_pad, epilogue, context->d_error, context->sm_count, stream);
+    if (error == cudaErrorInvalidValue) return cuda_fail(context, error, "W8A8 GEMM launch", QPUCUDA_INVALID_ARGUMENT);
+    if (error != cudaSuccess) return cuda_fail(context, error, "W8A8 GEMM launch");
+    return QPUCUDA_OK;
+}
+
 qpucuda_status qpucuda_w8a8_linear_execute_prepared_device(qpucuda_w8a8_linear *linear, const int8_t *quantized,
                                                            size_t quantized_stride, const float *row_scales,
                                                            uint32_t rows, float *destination,

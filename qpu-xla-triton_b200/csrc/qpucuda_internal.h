@@ -83,8 +83,21 @@ bool encode_tensor_map_2d_u8(CUtensorMap *map, const void *base, uint64_t inner_
 cudaError_t launch_quantize_rows_int8(const float *x, size_t x_stride, uint32_t rows, uint32_t cols,
                                       uint32_t padded_cols, int8_t *q, size_t q_stride, float *scales,
                                       cudaStream_t stream);
+// Same quantizer over rows whose elements need not be contiguous: element (r, c) at
+// (r / rows_per_batch) * batch_stride + (r % rows_per_batch) * row_stride + c * col_stride.
+cudaError_t launch_quantize_rows_int8_layout(const float *x, uint32_t rows, uint32_t cols, uint32_t padded_cols,
+                                             uint32_t rows_per_batch, size_t batch_stride, size_t row_stride,
+                                             size_t col_stride, int8_t *q, size_t q_stride, float *scales,
+                                             cudaStream_t stream);
 cudaError_t launch_quantize_q8_0(const float *x, size_t x_stride, uint32_t rows, uint32_t cols, uint8_t *blocks,
                                  cudaStream_t stream);
+// im2col of an NCHW fp32 tensor (row = output pixel, column = (channel, kernel row, kernel col)).
+cudaError_t launch_im2col_nchw_f32(const float *source, uint32_t batch, uint32_t channels, uint32_t height,
+                                   uint32_t width, uint32_t channel_offset, uint32_t group_channels,
+                                   uint32_t kernel_height, uint32_t kernel_width, uint32_t stride_h,
+                                   uint32_t stride_w, uint32_t pad_h, uint32_t pad_w, uint32_t dilation_h,
+                                   uint32_t dilation_w, uint32_t output_height, uint32_t output_width,
+                                   float *destination, size_t destination_stride, cudaStream_t stream);
 cudaError_t launch_quantize_q4_0(const float *x, size_t x_stride, uint32_t rows, uint32_t cols, uint8_t *blocks,
                                  cudaStream_t stream);
 
@@ -103,6 +116,11 @@ struct GemmEpilogue {
     // Other ranks' output buffers (mapped peer memory), each written at the same offsets as `out`.
     void *peer_out[kGemmMaxPeers] = {};
     uint32_t peer_count = 0;
+    // Output (m, n) lies at (m / rows_per_batch) * batch_stride + (m % rows_per_batch) * out_stride
+    // + n * col_stride elements from `out` (row-major by default; NCHW pixels-as-rows for convs).
+    uint32_t rows_per_batch = 0xFFFFFFFFu;
+    size_t batch_stride = 0;
+    size_t col_stride = 1;
 };
 
 // tcgen05 int8 GEMM: a [m][k] and w [n][k] int8, K-major, 16-byte aligned rows.

@@ -121,6 +121,32 @@ cudaError_t launch_vec(const float *x, size_t x_stride, uint32_t rows, uint32_t 
     return cudaGetLastError();
 }
 
+// Layout path: one thread per row; consecutive threads take consecutive rows, so for NCHW
+// pixels (row step 1, element = channel, element stride H*W) every channel read is coalesced
+// across the warp. Two passes over the row (max, then quantize; the second hits L1/L2); the
+// int8 row is written four bytes at a time, zero-padded to padded_cols (a multiple of 4).
+__global__ void __launch_bounds__(256) quantize_rows_int8_layout_kernel(
+    const float *__restrict__ x, uint32_t rows, uint32_t cols, uint32_t padded_cols, uint32_t rows_per_batch,
+    size_t batch_stride, size_t row_stride, size_t col_stride, int8_t *__restrict__ q, size_t q_stride,
+    float *__restrict__ scales) {
+    const uint32_t row = blockIdx.x * blockDim.x + threadIdx.x;
+    if (row >= rows) return;
+    const float *source = x + static_cast<size_t>(row / rows_per_batch) * batch_stride +
+                          static_cast<size_t>(row % rows_per_batch) * row_stride;
+    float amax = 0.0f;
+    for (uint32_t c = 0; c < cols; ++c) amax = fmaxf(amax, fabsf(__ldg(source + c * col_stride)));
+    const float scale = fmaxf(__fdiv_rn(amax, 127.0f), scale_floor());
+    uint32_t *destination = reinterpret_cast<uint32_t *>(q + static_cast<size_t>(row) * q_stride);
+    for (uint32_t c = 0; c < padded_cols; c += 4) {
+        int v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            v[i] = c + i < cols ? quantize_value(__ldg(source + (c + i) * col_stride), scale) : 0;
+        destination[c / 4] = pack4(v[0], v[1], v[2], v[3]);
+    }
+    scales[row] = scale;
+}
+
 // ---- Q8_0 -------------------------------------------------------------------------------
 
 // One warp per 32-element block: d = amax / 127 (fp32), id = 1/d (0 when d == 0),
@@ -238,6 +264,24 @@ cudaError_t launch_quantize_q8_0(const float *x, size_t x_stride, uint32_t rows,
     const size_t total = static_cast<size_t>(rows) * (cols / 32);
     if (total == 0) return cudaSuccess;
     quantize_q8_0_kernel<<<grid_for(total, 8), 256, 0, stream>>>(x, x_stride, rows, cols / 32, blocks);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows_int8_layout(const float *x, uint32_t rows, uint32_t cols, uint32_t padded_cols,
+                                             uint32_t rows_per_batch, size_t batch_stride, size_t row_stride,
+                                             size_t col_stride, int8_t *q, size_t q_stride, float *scales,
+                                             cudaStream_t stream) {
+    if (rows == 0) return cudaSuccess;
+    if (rows_per_batch == 0 || rows_per_batch >= rows) {
+        rows_per_batch = rows;
+        batch_stride = 0;
+    }
+    if (col_stride == 1 && rows_per_batch == rows) {
+        return launch_quantize_rows_int8(x, row_stride, rows, cols, padded_cols, q, q_stride, scales, stream);
+    }
+    if (padded_cols % 4 != 0 || q_stride % 4 != 0 || (reinterpret_cast<uintptr_t>(q) & 3u) != 0) return cudaErrorInvalidValue;
+    quantize_rows_int8_layout_kernel<<<(rows + 255) / 256, 256, 0, stream>>>(
+        x, rows, cols, padded_cols, rows_per_batch, batch_stride, row_stride, col_stride, q, q_stride, scales);
     return cudaGetLastError();
 }
 

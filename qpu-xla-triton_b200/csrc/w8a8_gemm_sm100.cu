@@ -79,6 +79,11 @@ struct GemmParams {
     // `out`: other ranks' output buffers for the fused GEMM + all-gather.
     void *peer_out[kGemmMaxPeers];
     uint32_t peer_count;
+    // Output (m, n) at (m / rows_per_batch) * batch_stride + (m % rows_per_batch) * out_stride
+    // + n * col_stride elements (row-major: rows_per_batch >= m, col_stride 1).
+    uint32_t rows_per_batch;
+    size_t batch_stride;
+    size_t col_stride;
     unsigned int *error_word;
 };
 
@@ -284,7 +289,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         uint4 *staging = epilogue_stage + (warp - 2u) * 256u;
         const bool s32 = params.mode == static_cast<int>(EpilogueMode::kStoreS32);
         const bool with_bias = params.mode == static_cast<int>(EpilogueMode::kDequantizeBias);
-        bool aligned = (params.out_stride & 3u) == 0 && (reinterpret_cast<uintptr_t>(params.out) & 15u) == 0;
+        // Row-segment stores need unit column stride; otherwise (NCHW outputs) each lane stores its
+        // own row's values straight from registers, which is coalesced when rows are adjacent.
+        const bool row_segments = params.col_stride == 1;
+        bool aligned = (params.out_stride & 3u) == 0 && (params.batch_stride & 3u) == 0 &&
+                       (reinterpret_cast<uintptr_t>(params.out) & 15u) == 0;
 #pragma unroll
         for (uint32_t d = 0; d < kGemmMaxPeers; ++d)
             if (d < params.peer_count) aligned = aligned && (reinterpret_cast<uintptr_t>(params.peer_out[d]) & 15u) == 0;
@@ -321,6 +330,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         r[j] = __float_as_uint(v);
                     }
                 }
+                if (!row_segments) {
+                    if (m < params.m) {
+                        const size_t base = static_cast<size_t>(m / params.rows_per_batch) * params.batch_stride +
+                                            static_cast<size_t>(m % params.rows_per_batch) * params.out_stride;
+#pragma unroll
+                        for (uint32_t j = 0; j < 32; ++j) {
+                            if (n0 + j < params.n) {
+                                const size_t offset = base + static_cast<size_t>(n0 + j) * params.col_stride;
+                                static_cast<uint32_t *>(params.out)[offset] = r[j];
+#pragma unroll
+                                for (uint32_t d = 0; d < kGemmMaxPeers; ++d)
+                                    if (d < params.peer_count) static_cast<uint32_t *>(params.peer_out[d])[offset] = r[j];
+                            }
+                        }
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (uint32_t c = 0; c < 8; ++c)
                     staging[lane * 8u + (c ^ (lane & 7u))] = make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
@@ -333,7 +359,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint4 value = staging[i * 8u + (c ^ (i & 7u))];
                     const uint32_t row = row0 + i;
                     if (row < params.m && col < params.n) {
-                        const size_t offset = static_cast<size_t>(row) * params.out_stride + col;
+                        const size_t offset = static_cast<size_t>(row / params.rows_per_batch) * params.batch_stride +
+                                              static_cast<size_t>(row % params.rows_per_batch) * params.out_stride + col;
                         const uint32_t valid = params.n - col;
                         store_group(params.out, offset, value, valid, aligned);
 #pragma unroll
@@ -391,6 +418,10 @@ cudaError_t launch_w8a8_gemm_sm100(const CUtensorMap *map_a, const CUtensorMap *
     if (epilogue.peer_count > kGemmMaxPeers) return cudaErrorInvalidValue;
     params.peer_count = epilogue.peer_count;
     for (uint32_t d = 0; d < kGemmMaxPeers; ++d) params.peer_out[d] = d < epilogue.peer_count ? epilogue.peer_out[d] : nullptr;
+    if (epilogue.rows_per_batch == 0 || epilogue.col_stride == 0) return cudaErrorInvalidValue;
+    params.rows_per_batch = epilogue.rows_per_batch;
+    params.batch_stride = epilogue.batch_stride;
+    params.col_stride = epilogue.col_stride;
     params.error_word = error_word;
     const uint32_t tiles = params.m_blocks * params.n_blocks;
     const uint32_t grid = tiles < static_cast<uint32_t>(sm_count) ? tiles : static_cast<uint32_t>(sm_count);

@@ -135,6 +135,18 @@ class W8A8Execution(Structure):
     ]
 
 
+class MatrixLayout(Structure):
+    """``qpucuda_matrix_layout``: element (r, c) at (r // rows_per_batch) * batch_stride
+    + (r % rows_per_batch) * row_stride + c * column_stride elements from the base."""
+
+    _fields_ = [
+        ("rows_per_batch", c_uint64),
+        ("batch_stride", c_uint64),
+        ("row_stride", c_uint64),
+        ("column_stride", c_uint64),
+    ]
+
+
 MEMORY_HOST = 0
 MEMORY_DEVICE = 1
 
@@ -174,6 +186,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "qpucuda_quantize_q8_0": (_S, [_P, _P, c_size_t, c_uint32, c_uint32, _P]),
     "qpucuda_quantize_q4_0": (_S, [_P, _P, c_size_t, c_uint32, c_uint32, _P]),
+    "qpucuda_im2col_nchw_f32": (_S, [_P, _P] + [c_uint32] * 14 + [_P, c_size_t]),
     # qpucuda_w8a8.h
     "qpucuda_w8a8_linear_prepare": (_S, [_P, POINTER(W8A8LinearDesc), POINTER(c_void_p)]),
     "qpucuda_w8a8_linear_destroy": (None, [_P]),
@@ -181,6 +194,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "qpucuda_w8a8_linear_execute": (_S, [_P, POINTER(W8A8Execution)]),
     "qpucuda_w8a8_linear_execute_device": (_S, [_P, _P, c_size_t, c_uint32, _P, c_size_t]),
     "qpucuda_w8a8_linear_execute_prepared_device": (_S, [_P, _P, c_size_t, _P, c_uint32, _P, c_size_t]),
+    "qpucuda_w8a8_linear_execute_device_layout": (_S, [_P, _P, POINTER(MatrixLayout), c_uint32, _P, POINTER(MatrixLayout)]),
     "qpucuda_w8a8_linear_scratch": (_S, [_P, POINTER(c_void_p), POINTER(c_size_t), POINTER(c_void_p)]),
     "qpucuda_w8a8_linear_execute_static": (
         _S,
@@ -351,6 +365,7 @@ __all__ = [
     "SIGNATURES",
     "Status",
     "W8A8Execution",
+    "MatrixLayout",
     "W8A8LinearDesc",
     "header_function_names",
     "load",

@@ -69,6 +69,10 @@ def import_reference(checkout: Path) -> dict[str, object]:
     from qpu_xla.models.tinyllama.quantization import CalibratedW8A8Linear, quantize_per_output_channel_int8
 
     import benchmark_llama_cpp_qpu_persistent_q4 as persistent_example
+    from qpu_xla.ops.conv2d import _im2col_nchw
+
+    sys.path.insert(0, str(checkout / "tests"))
+    import test_qpu_xla_conv2d_w8a8 as conv_tests
 
     assert Path(reference_qpu_xla.__file__).is_relative_to(checkout), "imported the wrong qpu_xla"
     sys.path = saved
@@ -80,6 +84,8 @@ def import_reference(checkout: Path) -> dict[str, object]:
         "staged_cpu": _StagedW8A8Linear._cpu,
         "ggml": ggml_q4_0,
         "quantize_q8_0_split": persistent_example.quantize_q8_0_split,
+        "im2col_nchw": _im2col_nchw,
+        "conv_dynamic_group_reference": conv_tests._dynamic_group_reference,
     }
 
 
@@ -191,6 +197,32 @@ def main() -> int:
         q8_decoded_values=np.array(q8_decoded[1]),
     )
     print("codec extremes")
+
+    # W8A8 convolution: the reference test's own per-group dynamic reference
+    # (tests/test_qpu_xla_conv2d_w8a8.py:14-54) on the inputs of its plan test (:55-89) and of
+    # its hybrid-partition test (:92-130), plus _im2col_nchw (src/qpu_xla/ops/conv2d.py:47-79)
+    # on a strided, dilated case.
+    conv: dict[str, np.ndarray] = {}
+    cases = [(f"plan_g{groups}", 1200 + groups, (1, 4, 4, 4), (4, 4 // groups, 3, 3), 1, 1, groups) for groups in (1, 2, 4)]
+    for channels, outputs, kernel, stride, groups, size in ((16, 1, 1, 1, 1, 5), (4, 32, 1, 1, 1, 5), (4, 32, 3, 2, 1, 12), (4, 64, 3, 1, 2, 5), (16, 16, 3, 1, 16, 5)):
+        seed = 3100 + channels + outputs + kernel + stride + groups + size
+        cases.append((f"hybrid_c{channels}_o{outputs}_k{kernel}_s{stride}_g{groups}_n{size}", seed, (1, channels, size, size), (outputs, channels // groups, kernel, kernel), stride, kernel // 2, groups))
+    for name, seed, source_shape, weight_shape, stride, padding, groups in cases:
+        rng = np.random.default_rng(seed)
+        source = rng.standard_normal(source_shape, dtype=np.float32)
+        weight = np.ascontiguousarray(rng.standard_normal(weight_shape, dtype=np.float32))
+        expected = ref["conv_dynamic_group_reference"](source, weight, groups=groups, stride=stride, padding=padding)  # type: ignore[operator]
+        conv[f"{name}_source"] = source
+        conv[f"{name}_weight"] = weight
+        conv[f"{name}_params"] = np.array([stride, padding, groups], dtype=np.int64)
+        conv[f"{name}_expected"] = np.ascontiguousarray(expected, dtype=np.float32)
+    rng = np.random.default_rng(77)
+    im2col_source = rng.standard_normal((2, 3, 9, 7), dtype=np.float32)
+    conv["im2col_source"] = im2col_source
+    conv["im2col_expected"] = ref["im2col_nchw"](im2col_source, 3, 2, stride=(2, 1), padding=(1, 2), dilation=(2, 1))  # type: ignore[operator]
+    conv["case_names"] = np.array([c[0] for c in cases])
+    np.savez_compressed(HERE / "conv2d_w8a8.npz", **conv)
+    print("conv2d w8a8:", len(cases), "cases")
     return 0
 
 

@@ -147,3 +147,16 @@ def test_int8_quantizer_scale_floor_and_zero_rows() -> None:
     np.testing.assert_array_equal(quantized[0], 0)
     assert scales[2] == np.float32(4.0) / np.float32(127.0)
     assert quantized[2].tolist() == [64, -127, 32, 16]
+
+
+def test_conv2d_oracle_matches_the_reference_dynamic_group_reference(golden: dict) -> None:
+    """oracle.conv2d_w8a8 against the reference test's own per-group dynamic reference
+    (tests/test_qpu_xla_conv2d_w8a8.py:14-54) on its plan and hybrid-partition inputs, and
+    oracle.im2col_nchw against _im2col_nchw (src/qpu_xla/ops/conv2d.py:47-79), bit for bit."""
+    conv = golden["conv2d_w8a8"]
+    lowered = oracle.im2col_nchw(conv["im2col_source"], (3, 2), stride=(2, 1), padding=(1, 2), dilation=(2, 1))
+    np.testing.assert_array_equal(lowered, conv["im2col_expected"])
+    for name in conv["case_names"]:
+        stride, padding, groups = (int(v) for v in conv[f"{name}_params"])
+        result = oracle.conv2d_w8a8(conv[f"{name}_source"], conv[f"{name}_weight"], stride=(stride, stride), padding=(padding, padding), groups=groups)
+        np.testing.assert_array_equal(result, conv[f"{name}_expected"], err_msg=str(name))

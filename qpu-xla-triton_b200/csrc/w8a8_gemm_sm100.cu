@@ -62,8 +62,11 @@ struct Control {
 
 // Epilogue staging: each epilogue warp transposes its 32 rows x 32 columns chunk through 4 KB
 // of shared memory so that global stores leave as full 128-byte row segments.
+// Only the fan-out variant (peer destinations) has it.
 constexpr int EPILOGUE_STAGE_BYTES = (EPILOGUE_THREADS / 32) * 32 * 32 * 4;
-constexpr size_t kSmemBytes = static_cast<size_t>(STAGES) * STAGE_BYTES + EPILOGUE_STAGE_BYTES + 1024 + sizeof(Control);
+constexpr size_t smem_bytes(bool fanout) {
+    return static_cast<size_t>(STAGES) * STAGE_BYTES + (fanout ? EPILOGUE_STAGE_BYTES : 0) + 1024 + sizeof(Control);
+}
 
 struct GemmParams {
     uint32_t m, n, k;
@@ -156,6 +159,8 @@ __device__ __forceinline__ void store_group(void *base, size_t offset, uint4 val
     if (valid > 3) p[3] = value.w;
 }
 
+// FANOUT: the epilogue also writes every peer destination (fused GEMM + all-gather).
+template <bool FANOUT>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     w8a8_gemm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                            const GemmParams params) {
@@ -164,7 +169,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t *stage_a = smem;
     uint8_t *stage_b = smem + STAGES * A_STAGE_BYTES;
     uint4 *epilogue_stage = reinterpret_cast<uint4 *>(smem + STAGES * STAGE_BYTES);
-    Control *control = reinterpret_cast<Control *>(smem + STAGES * STAGE_BYTES + EPILOGUE_STAGE_BYTES);
+    Control *control = reinterpret_cast<Control *>(smem + STAGES * STAGE_BYTES + (FANOUT ? EPILOGUE_STAGE_BYTES : 0));
 
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
@@ -281,10 +286,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
         // Lane l of warp w reads TMEM lane (w % 4) * 32 + l, i.e. one output row, 32 columns per
-        // tcgen05.ld. The values are converted in registers, written to this warp's 4 KB staging
-        // buffer as 8 x 16 bytes per row (16-byte slot c of row r at c ^ (r & 7): conflict-free
-        // both ways), then read back row-wise: 8 lanes cover one row's 32 columns, so each store
-        // instruction writes four 128-byte row segments, to `out` and to every peer destination.
+        // tcgen05.ld, and converts the values in registers. A local row-major output is stored
+        // straight from registers. With peer destinations the values are written to this warp's
+        // 4 KB staging buffer as 8 x 16 bytes per row (16-byte slot c of row r at c ^ (r & 7):
+        // conflict-free both ways) and read back row-wise: 8 lanes cover one row's 32 columns,
+        // so each store instruction writes four 128-byte row segments, to `out` and to every
+        // peer (full-line writes over NVLink).
         const uint32_t quarter = warp & 3u;  // TMEM lanes this warp may access
         uint4 *staging = epilogue_stage + (warp - 2u) * 256u;
         const bool s32 = params.mode == static_cast<int>(EpilogueMode::kStoreS32);
@@ -292,11 +299,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // Row-segment stores need unit column stride; otherwise (NCHW outputs) each lane stores its
         // own row's values straight from registers, which is coalesced when rows are adjacent.
         const bool row_segments = params.col_stride == 1;
+        // Batched rows (NCHW outputs) need a division per row; plain row-major outputs do not.
+        const bool batched = params.rows_per_batch != 0xFFFFFFFFu;
+        const uint32_t peers = FANOUT ? params.peer_count : 0u;
         bool aligned = (params.out_stride & 3u) == 0 && (params.batch_stride & 3u) == 0 &&
                        (reinterpret_cast<uintptr_t>(params.out) & 15u) == 0;
+        if constexpr (FANOUT) {
 #pragma unroll
-        for (uint32_t d = 0; d < kGemmMaxPeers; ++d)
-            if (d < params.peer_count) aligned = aligned && (reinterpret_cast<uintptr_t>(params.peer_out[d]) & 15u) == 0;
+            for (uint32_t d = 0; d < kGemmMaxPeers; ++d)
+                if (d < peers) aligned = aligned && (reinterpret_cast<uintptr_t>(params.peer_out[d]) & 15u) == 0;
+        }
         uint32_t local_tile = 0;
         for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local_tile) {
             const uint32_t acc = local_tile & 1u;
@@ -313,6 +325,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint32_t row0 = m_block * BM + quarter * 32;  // first row of this warp
             const uint32_t m = row0 + lane;
             const float row_scale = (m < params.m && !s32) ? params.row_scales[m] : 0.0f;
+            const size_t row_base = batched ? static_cast<size_t>(m / params.rows_per_batch) * params.batch_stride +
+                                                  static_cast<size_t>(m % params.rows_per_batch) * params.out_stride
+                                            : static_cast<size_t>(m) * params.out_stride;
             const uint32_t taddr = tmem_base + ((quarter * 32u) << 16) + acc * BN;
 #pragma unroll 1
             for (uint32_t chunk = 0; chunk < BN / 32; ++chunk) {
@@ -320,33 +335,90 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tmem_load_32x32b_x32(taddr + chunk * 32, r);
                 const uint32_t n0 = n_base + chunk * 32;
                 if (n0 >= params.n) continue;  // warp-uniform
-                if (!s32) {
-                    // Column scales / bias: every lane reads the same address (an L1 broadcast).
+                const bool full_chunk = n0 + 32 <= params.n;
+                if (!FANOUT && row_segments) {
+                    // Local row-major output: each lane converts and stores its own row's 32 values
+                    // as eight 16-byte stores (measured faster than a shared-memory transpose when
+                    // nothing crosses NVLink).
+                    if (m >= params.m) continue;
+                    if (s32) {
+                        int32_t *row = static_cast<int32_t *>(params.out) + row_base + n0;
+                        if (full_chunk && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
 #pragma unroll
-                    for (uint32_t j = 0; j < 32; ++j) {
-                        const bool in_range = n0 + j < params.n;
-                        float v = dequant(r[j], row_scale, in_range ? __ldg(params.col_scales + n0 + j) : 0.0f);
-                        if (with_bias) v = __fadd_rn(v, in_range ? __ldg(params.bias + n0 + j) : 0.0f);
-                        r[j] = __float_as_uint(v);
-                    }
-                }
-                if (!row_segments) {
-                    if (m < params.m) {
-                        const size_t base = static_cast<size_t>(m / params.rows_per_batch) * params.batch_stride +
-                                            static_cast<size_t>(m % params.rows_per_batch) * params.out_stride;
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<int4 *>(row + j) =
+                                    make_int4(static_cast<int>(r[j]), static_cast<int>(r[j + 1]), static_cast<int>(r[j + 2]),
+                                              static_cast<int>(r[j + 3]));
+                        } else {
+                            for (uint32_t j = 0; j < 32 && n0 + j < params.n; ++j) row[j] = static_cast<int>(r[j]);
+                        }
+                    } else {
+                        // Column scales / bias: every lane reads the same address (an L1 broadcast).
+                        const float *cs = params.col_scales + n0;
+                        const float *cb = params.bias + n0;
+                        float *row = static_cast<float *>(params.out) + row_base + n0;
+                        if (full_chunk && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
+                            float v[32];
 #pragma unroll
-                        for (uint32_t j = 0; j < 32; ++j) {
-                            if (n0 + j < params.n) {
-                                const size_t offset = base + static_cast<size_t>(n0 + j) * params.col_stride;
-                                static_cast<uint32_t *>(params.out)[offset] = r[j];
+                            for (int j = 0; j < 32; ++j) {
+                                v[j] = dequant(r[j], row_scale, __ldg(cs + j));
+                                if (with_bias) v[j] = __fadd_rn(v[j], __ldg(cb + j));
+                            }
 #pragma unroll
-                                for (uint32_t d = 0; d < kGemmMaxPeers; ++d)
-                                    if (d < params.peer_count) static_cast<uint32_t *>(params.peer_out[d])[offset] = r[j];
+                            for (int j = 0; j < 32; j += 4)
+                                *reinterpret_cast<float4 *>(row + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                        } else {
+                            for (uint32_t j = 0; j < 32 && n0 + j < params.n; ++j) {
+                                float v = dequant(r[j], row_scale, __ldg(cs + j));
+                                if (with_bias) v = __fadd_rn(v, __ldg(cb + j));
+                                row[j] = v;
                             }
                         }
                     }
                     continue;
                 }
+                if (!s32) {
+                    // Column scales / bias: every lane reads the same address (an L1 broadcast).
+                    if (full_chunk) {
+#pragma unroll
+                        for (uint32_t j = 0; j < 32; ++j) {
+                            float v = dequant(r[j], row_scale, __ldg(params.col_scales + n0 + j));
+                            if (with_bias) v = __fadd_rn(v, __ldg(params.bias + n0 + j));
+                            r[j] = __float_as_uint(v);
+                        }
+                    } else {
+#pragma unroll
+                        for (uint32_t j = 0; j < 32; ++j) {
+                            const bool in_range = n0 + j < params.n;
+                            float v = dequant(r[j], row_scale, in_range ? __ldg(params.col_scales + n0 + j) : 0.0f);
+                            if (with_bias) v = __fadd_rn(v, in_range ? __ldg(params.bias + n0 + j) : 0.0f);
+                            r[j] = __float_as_uint(v);
+                        }
+                    }
+                }
+                if (!row_segments) {
+                    // Column-strided (NCHW) output: each lane stores its own row's values element by
+                    // element; adjacent lanes (adjacent pixels) write adjacent addresses.
+                    if (m < params.m) {
+                        {
+#pragma unroll
+                            for (uint32_t j = 0; j < 32; ++j) {
+                                if (n0 + j < params.n) {
+                                    const size_t offset = row_base + static_cast<size_t>(n0 + j) * params.col_stride;
+                                    static_cast<uint32_t *>(params.out)[offset] = r[j];
+                                    if constexpr (FANOUT) {
+#pragma unroll
+                                        for (uint32_t d = 0; d < kGemmMaxPeers; ++d)
+                                            if (d < peers) static_cast<uint32_t *>(params.peer_out[d])[offset] = r[j];
+                                    }
+                                }
+                            }
+                        }
+                    }
+                    continue;
+                }
+                // Fan-out, row-major: transpose through shared memory so that every store
+                // instruction writes four full 128-byte row segments, locally and to each peer.
 #pragma unroll
                 for (uint32_t c = 0; c < 8; ++c)
                     staging[lane * 8u + (c ^ (lane & 7u))] = make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
@@ -359,13 +431,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const uint4 value = staging[i * 8u + (c ^ (i & 7u))];
                     const uint32_t row = row0 + i;
                     if (row < params.m && col < params.n) {
-                        const size_t offset = static_cast<size_t>(row / params.rows_per_batch) * params.batch_stride +
-                                              static_cast<size_t>(row % params.rows_per_batch) * params.out_stride + col;
+                        const size_t offset =
+                            (batched ? static_cast<size_t>(row / params.rows_per_batch) * params.batch_stride +
+                                           static_cast<size_t>(row % params.rows_per_batch) * params.out_stride
+                                     : static_cast<size_t>(row) * params.out_stride) +
+                            col;
                         const uint32_t valid = params.n - col;
                         store_group(params.out, offset, value, valid, aligned);
 #pragma unroll
                         for (uint32_t d = 0; d < kGemmMaxPeers; ++d)
-                            if (d < params.peer_count) store_group(params.peer_out[d], offset, value, valid, aligned);
+                            if (d < peers) store_group(params.peer_out[d], offset, value, valid, aligned);
                     }
                 }
                 __syncwarp();
@@ -375,7 +450,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (lane == 0) mbar_arrive(smem_u32(&control->tmem_empty[acc]));
         }
         // Peer destinations: make this thread's remote stores visible system-wide before exit.
-        if (params.peer_count != 0) __threadfence_system();
+        if (FANOUT && params.peer_count != 0) __threadfence_system();
     }
 
     tc_fence_before();
@@ -396,9 +471,11 @@ cudaError_t launch_w8a8_gemm_sm100(const CUtensorMap *map_a, const CUtensorMap *
     if (k == 0) return cudaErrorInvalidValue;
     static bool configured = false;
     if (!configured) {
-        const cudaError_t error = cudaFuncSetAttribute(w8a8_gemm_sm100_kernel,
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                       static_cast<int>(kSmemBytes));
+        cudaError_t error = cudaFuncSetAttribute(w8a8_gemm_sm100_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(smem_bytes(false)));
+        if (error == cudaSuccess)
+            error = cudaFuncSetAttribute(w8a8_gemm_sm100_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem_bytes(true)));
         if (error != cudaSuccess) return error;
         configured = true;
     }
@@ -425,7 +502,11 @@ cudaError_t launch_w8a8_gemm_sm100(const CUtensorMap *map_a, const CUtensorMap *
     params.error_word = error_word;
     const uint32_t tiles = params.m_blocks * params.n_blocks;
     const uint32_t grid = tiles < static_cast<uint32_t>(sm_count) ? tiles : static_cast<uint32_t>(sm_count);
-    w8a8_gemm_sm100_kernel<<<grid, NUM_THREADS, kSmemBytes, stream>>>(*map_a, *map_w, params);
+    if (params.peer_count != 0) {
+        w8a8_gemm_sm100_kernel<true><<<grid, NUM_THREADS, smem_bytes(true), stream>>>(*map_a, *map_w, params);
+    } else {
+        w8a8_gemm_sm100_kernel<false><<<grid, NUM_THREADS, smem_bytes(false), stream>>>(*map_a, *map_w, params);
+    }
     return cudaGetLastError();
 }
 

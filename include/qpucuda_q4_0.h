@@ -6,14 +6,18 @@
  * program replaced by an sm_100a CUDA kernel. Differences that a caller sees:
  *   - expected_source_hash is checked against qpucuda_q4_0_kernel_source_hash()
  *     (the SHA-256 of this library's kernel source), not a QPU program hash;
- *   - rows is limited to 1..4 (the M=1 / M=4 decode path); larger row counts
- *     return QPUCUDA_CAPABILITY_MISSING;
- *   - weight_mode must be EXACT: the reference accepts the re-quantized modes
- *     only for rows > 4 (qpu_llama_q4_0.c:217-219), which is outside 1..4;
+ *   - rows 1..4 run the decode matvec; rows 5..4*65535 run the tiled tensor-core
+ *     path (the reference's MX path, qpu_llama_q4_0.c:238-290) with the exact
+ *     per-block scaling of its program, ((float)dot * d_a) * d_w added block by
+ *     block; prepare then also reserves the split-activation scratch;
+ *   - weight_mode must be EXACT: the re-quantized COLUMN_W8 / ROWCOL_W8A8 modes
+ *     (rows > 4 only in the reference, qpu_llama_q4_0.c:217-219) return
+ *     QPUCUDA_CAPABILITY_MISSING;
  *   - workgroups_per_supergroup is a QPU dispatch knob and is ignored;
- *   - submission_cpu_fallback always returns QPUCUDA_INVALID_ARGUMENT, exactly
- *     as the reference does for every non-MX (rows <= 4) linear
- *     (qpu_llama_q4_0.c:834-839): this library has no CPU fallback.
+ *   - submission_cpu_fallback returns QPUCUDA_INVALID_ARGUMENT for rows <= 4,
+ *     exactly as the reference does (qpu_llama_q4_0.c:834-839), and
+ *     QPUCUDA_CAPABILITY_MISSING for rows > 4, where the reference would compute
+ *     on the host: this library has no CPU path.
  *
  * Host pointers: desc->weights, execution->activation and
  * execution->destination are host memory, as in the reference. The
@@ -53,7 +57,7 @@ typedef struct qpucuda_q4_0_linear_desc {
     size_t weight_size;
     uint32_t input_columns;          /* K, multiple of 32 */
     uint32_t output_columns;         /* N of the full matrix */
-    uint32_t rows;                   /* maximum M per call, 1..4 */
+    uint32_t rows;                   /* maximum M per call, 1..4*65535 */
     uint32_t resident_column_start;  /* multiple of 16 */
     uint32_t resident_column_count;  /* multiple of 16, > 0 */
     qpucuda_q4_0_weight_mode weight_mode;
@@ -117,8 +121,8 @@ qpucuda_status qpucuda_q4_0_linear_submit(
 qpucuda_status qpucuda_q4_0_submission_wait(
     qpucuda_q4_0_submission *submission,
     qpucuda_q4_0_timing *timing);
-/* qpu_llama_q4_0_submission_cpu_fallback (qpu_llama_q4_0.h:79-80): always
- * QPUCUDA_INVALID_ARGUMENT (no CPU path; see the file comment). */
+/* qpu_llama_q4_0_submission_cpu_fallback (qpu_llama_q4_0.h:79-80): never
+ * computes (no CPU path; see the file comment). */
 qpucuda_status qpucuda_q4_0_submission_cpu_fallback(qpucuda_q4_0_submission *submission);
 /* qpu_llama_q4_0_submission_destroy (qpu_llama_q4_0.h:81); NULL-safe, waits if active. */
 void qpucuda_q4_0_submission_destroy(qpucuda_q4_0_submission *submission);

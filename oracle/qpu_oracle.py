@@ -244,6 +244,26 @@ def q4_0_q8_0_linear(activation_blocks: npt.NDArray[np.uint8], weight_blocks: np
     return result
 
 
+def q4_0_q8_0_linear_mx(activation_blocks: npt.NDArray[np.uint8], weight_blocks: npt.NDArray[np.uint8]) -> npt.NDArray[np.float32]:
+    """The reference's tiled (MX, rows > 4) program: per output one fp32 accumulator over the blocks
+    in order, ``acc += ((float)dot_b * d_a[m, b]) * d_w[n, b]`` (activation scale first;
+    src/qpu_xla/kernels/ggml_q4_0.py:506-513). Same exact block dots as ``q4_0_q8_0_linear``."""
+    if activation_blocks.ndim != 3 or weight_blocks.ndim != 3:
+        raise ValueError("activation and weight blocks must both be rank three")
+    rows, blocks, _ = activation_blocks.shape
+    if weight_blocks.shape[1] != blocks:
+        raise ValueError("reduction block counts do not match")
+    activation_scales, activations = unpack_q8_0_blocks(activation_blocks)
+    weight_scales, weights = unpack_q4_0_blocks(weight_blocks)
+    result = np.zeros((rows, weight_blocks.shape[0]), dtype=np.float32)
+    for block in range(blocks):
+        dots = (activations[:, block].astype(np.float64) @ weights[:, block].astype(np.float64).T).astype(np.int32)
+        contribution = dots.astype(np.float32) * activation_scales[:, block, None]
+        contribution *= weight_scales[None, :, block]
+        result += contribution
+    return result
+
+
 def q4_0_q8_0_block_dots(activation_blocks: npt.NDArray[np.uint8], weight_blocks: npt.NDArray[np.uint8]) -> npt.NDArray[np.int32]:
     """Per-block exact integer dots ``[rows, outputs, blocks]`` (the int part of ggml_q4_0.py:96)."""
     _, activations = unpack_q8_0_blocks(activation_blocks)

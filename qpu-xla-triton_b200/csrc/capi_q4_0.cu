@@ -33,6 +33,7 @@ struct qpucuda_q4_0_linear {
     uint8_t *d_nibbles = nullptr;     // [resident][blocks][16]
     uint16_t *d_scales = nullptr;     // [resident][scale_stride], zero padded
     uint8_t *d_activation = nullptr;  // [rows][blocks][34] staging
+    uint8_t *d_mx = nullptr;          // rows > 4: split activation for the tensor-core path
     float *d_output = nullptr;        // [rows][resident] staging
     uint8_t *h_activation = nullptr;  // pinned
     float *h_output = nullptr;        // pinned
@@ -64,6 +65,7 @@ void free_linear(qpucuda_q4_0_linear *linear) {
     cudaFree(linear->d_nibbles);
     cudaFree(linear->d_scales);
     cudaFree(linear->d_activation);
+    cudaFree(linear->d_mx);
     cudaFree(linear->d_output);
     cudaFreeHost(linear->h_activation);
     cudaFreeHost(linear->h_output);
@@ -84,6 +86,26 @@ Q40Weights weights_of(const qpucuda_q4_0_linear *linear) {
     weights.blocks = linear->blocks;
     weights.scale_stride = q4_0_scale_stride(linear->blocks);
     return weights;
+}
+
+// rows <= 4: the decode matvec over Q8_0 blocks (or fp32 rows); more rows: the tiled
+// tensor-core path through the plan's split-activation scratch.
+cudaError_t launch_linear(const qpucuda_q4_0_linear *linear, const uint8_t *q8_0, const float *f32, size_t f32_stride,
+                          uint32_t rows, uint32_t interleave, float *destination, size_t destination_stride,
+                          uint32_t local_start, uint32_t output_column_start, uint32_t column_count) {
+    qpucuda_context *context = linear->context;
+    if (rows > kMaxRows) {
+        return launch_q4_0_mx(weights_of(linear), q8_0, f32, f32_stride, rows, interleave, linear->d_mx, destination,
+                              destination_stride, local_start, output_column_start, column_count, context->sm_count,
+                              context->stream);
+    }
+    if (f32 != nullptr) {
+        return launch_q4_0_f32_gemv(weights_of(linear), f32, f32_stride, rows, destination, destination_stride,
+                                    local_start, output_column_start, column_count, context->sm_count, context->stream);
+    }
+    return launch_q4_0_q8_0_gemv(weights_of(linear), q8_0, rows, interleave, destination, destination_stride,
+                                 local_start, output_column_start, column_count, context->d_error, context->sm_count,
+                                 context->stream);
 }
 
 bool window_ok(const qpucuda_q4_0_linear *linear, uint32_t column_start, uint32_t column_count) {
@@ -114,9 +136,9 @@ qpucuda_status qpucuda_q4_0_linear_prepare(qpucuda_context *context, const qpucu
         return QPUCUDA_INVALID_ARGUMENT;
     }
     *result = nullptr;
-    if (desc->rows > kMaxRows || desc->weight_mode != QPUCUDA_Q4_0_WEIGHT_EXACT) {
+    if (desc->weight_mode != QPUCUDA_Q4_0_WEIGHT_EXACT) {
         return fail(context, QPUCUDA_CAPABILITY_MISSING,
-                    "Q4_0 linear: this library implements the exact M <= 4 decode path only");
+                    "Q4_0 linear: only the exact weight mode is implemented (no re-quantized W8 modes)");
     }
     const size_t blocks = desc->input_columns / kBlockElements;
     size_t weight_row_bytes = 0, required_source_bytes = 0;
@@ -148,13 +170,15 @@ qpucuda_status qpucuda_q4_0_linear_prepare(qpucuda_context *context, const qpucu
     const size_t resident_blocks = static_cast<size_t>(desc->resident_column_count) * blocks;
     const size_t scale_bytes = static_cast<size_t>(desc->resident_column_count) * q4_0_scale_stride(linear->blocks) * 2;
     const size_t native_bytes = resident_blocks * kWeightBlockBytes;
-    const size_t activation_bytes = static_cast<size_t>(kMaxRows) * blocks * kActivationBlockBytes;
-    const size_t output_bytes = static_cast<size_t>(kMaxRows) * desc->resident_column_count * sizeof(float);
+    const size_t activation_bytes = static_cast<size_t>(desc->rows) * blocks * kActivationBlockBytes;
+    const size_t output_bytes = static_cast<size_t>(desc->rows) * desc->resident_column_count * sizeof(float);
+    const size_t mx_bytes = desc->rows > kMaxRows ? q4_0_mx_scratch_bytes(desc->rows, linear->blocks) : 0;
     uint8_t *d_native = nullptr;
     cudaError_t error = cudaMalloc(reinterpret_cast<void **>(&linear->d_nibbles), resident_blocks * 16);
     if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_scales), scale_bytes);
     if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_activation), activation_bytes);
     if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_output), output_bytes);
+    if (error == cudaSuccess && mx_bytes != 0) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_mx), mx_bytes);
     if (error == cudaSuccess) error = cudaMallocHost(reinterpret_cast<void **>(&linear->h_activation), activation_bytes);
     if (error == cudaSuccess) error = cudaMallocHost(reinterpret_cast<void **>(&linear->h_output), output_bytes);
     if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&d_native), native_bytes);
@@ -179,7 +203,7 @@ qpucuda_status qpucuda_q4_0_linear_prepare(qpucuda_context *context, const qpucu
         free_linear(linear);
         return status;
     }
-    linear->resident_bytes = resident_blocks * kWeightBlockBytes + activation_bytes + output_bytes;
+    linear->resident_bytes = resident_blocks * kWeightBlockBytes + activation_bytes + output_bytes + mx_bytes;
     *result = linear;
     return QPUCUDA_OK;
 }
@@ -244,11 +268,9 @@ qpucuda_status qpucuda_q4_0_linear_submit(qpucuda_q4_0_linear *linear, const qpu
         submission->submit_start = submission->input_copy_end;
         const uint32_t local_start = execution->column_start - linear->resident_column_start;
         if (error == cudaSuccess) {
-            error = launch_q4_0_q8_0_gemv(weights_of(linear), linear->d_activation, rows,
-                                          execution->activation_interleave, linear->d_output,
-                                          linear->resident_column_count, local_start, local_start,
-                                          execution->column_count, context->d_error, context->sm_count,
-                                          context->stream);
+            error = launch_linear(linear, linear->d_activation, nullptr, 0, rows, execution->activation_interleave,
+                                  linear->d_output, linear->resident_column_count, local_start, local_start,
+                                  execution->column_count);
         }
         if (error == cudaSuccess) {
             // Only the requested window crosses back to the host.
@@ -319,8 +341,11 @@ qpucuda_status qpucuda_q4_0_submission_wait(qpucuda_q4_0_submission *submission,
 }
 
 qpucuda_status qpucuda_q4_0_submission_cpu_fallback(qpucuda_q4_0_submission *submission) {
-    // The reference rejects this for every non-MX linear (qpu_llama_q4_0.c:836-839); all linears here are M <= 4.
-    (void)submission;
+    // The reference rejects this for every non-MX linear (qpu_llama_q4_0.c:836-839) and computes MX
+    // linears on the host; this library has no host compute path.
+    if (submission != nullptr && submission->linear != nullptr && submission->linear->rows > kMaxRows) {
+        return fail(submission->linear->context, QPUCUDA_CAPABILITY_MISSING, "Q4_0 linear: no CPU path in this library");
+    }
     return QPUCUDA_INVALID_ARGUMENT;
 }
 
@@ -355,10 +380,9 @@ qpucuda_status qpucuda_q4_0_linear_execute_device(qpucuda_q4_0_linear *linear, c
     qpucuda_status status = begin_submit(context);
     if (status != QPUCUDA_OK) return status;
     DeviceGuard guard(context->device);
-    const cudaError_t error = launch_q4_0_q8_0_gemv(weights_of(linear), static_cast<const uint8_t *>(activation), rows,
-                                                    0, destination, destination_stride, local_start,
-                                                    output_column_start, column_count, context->d_error,
-                                                    context->sm_count, context->stream);
+    const cudaError_t error = launch_linear(linear, static_cast<const uint8_t *>(activation), nullptr, 0, rows, 0,
+                                            destination, destination_stride, local_start, output_column_start,
+                                            column_count);
     if (error != cudaSuccess) return cuda_fail(context, error, "launch Q4_0 linear");
     return QPUCUDA_OK;
 }
@@ -382,9 +406,8 @@ qpucuda_status qpucuda_q4_0_linear_execute_f32_device(qpucuda_q4_0_linear *linea
     DeviceGuard guard(context->device);
     // One launch: each CTA quantizes the fp32 blocks to Q8_0 as it stages them (the same
     // arithmetic as qpucuda_quantize_q8_0, so the result is that of quantize-then-execute).
-    const cudaError_t error = launch_q4_0_f32_gemv(weights_of(linear), source, source_stride, rows, destination,
-                                                   destination_stride, local_start, output_column_start, column_count,
-                                                   context->sm_count, context->stream);
+    const cudaError_t error = launch_linear(linear, nullptr, source, source_stride, rows, 0, destination,
+                                            destination_stride, local_start, output_column_start, column_count);
     if (error != cudaSuccess) return cuda_fail(context, error, "launch Q4_0 linear");
     return QPUCUDA_OK;
 }

@@ -10,7 +10,7 @@
 // followed by a warp tree, a different order from the reference's sequential
 // sum, so the result agrees to ~1e-6 relative rather than bit for bit.
 //
-// Two kernels:
+// Kernels:
 //  * q4_0_direct_kernel (prepared weights, the operator's path). Prepared layout,
 //    made once at prepare with the same 18 bytes per block as the native format:
 //    nibbles [columns][blocks][16] and fp16 scales [columns][scale_stride]
@@ -20,7 +20,9 @@
 //    occupancy API with a balanced number of rounds.
 //  * q4_0_native_kernel (single-kernel entry point over native 18-byte blocks,
 //    which are only 2-byte aligned): lanes read each block as nine 16-bit loads.
-// Both keep the weight codes packed: dp4a(nibbles & 0x0F0F0F0F, a[0..3]) and
+//  * q4_0_mx_kernel (rows > 4, the reference's MX path): int8 tensor-core MMAs per
+//    32-value block with the exact per-block scaling of the reference program (see below).
+// The two matvec kernels keep the weight codes packed: dp4a(nibbles & 0x0F0F0F0F, a[0..3]) and
 // dp4a((nibbles >> 4) & 0x0F0F0F0F, a[16..19]) etc.; the -8 offset seeds each block's
 // dp4a chain with -8 * sum(a), precomputed when the activation (rows x K bytes + fp32
 // block scales + block sums) is staged in shared memory once per CTA.
@@ -515,6 +517,326 @@ cudaError_t launch_native(const NativeParams &p, int sm_count, cudaStream_t stre
     return cudaGetLastError();
 }
 
+// ---- MX path: rows > 4 on the tensor cores -------------------------------------------------
+//
+// The reference's tiled Q4_0 x Q8_0 program (src/qpu_xla/kernels/ggml_q4_0.py:310-547, prepared
+// by qpu_llama_q4_0.c:238-290 for rows > 4, EXACT weight mode) computes, for every output, one
+// fp32 accumulator over the blocks in order: acc += ((float)dot_b * d_a[m, b]) * d_w[n, b]
+// (itof, fmul by the activation scale, fmul by the weight scale, fadd; :506-513). Here each
+// block's exact int32 dots come from mma.sync m16n8k32 (s8 x s8 -> s32) with a fresh accumulator
+// per block, and each thread applies those three roundings and the add to the outputs it owns,
+// in block order, so the result follows the reference program's arithmetic exactly.
+//
+// GGML's nibble order is already the m16n8k32 B-fragment order: word t of a block holds codes
+// 4t..4t+3 in its low nibbles and 16+4t.. in its high nibbles, which are exactly the two B
+// registers of the lane with threadID_in_group t. The codes enter the MMA as unsigned 0..15;
+// the -8 offset is removed by subtracting 8 * sum(q) of the activation block.
+//
+// Activation (split once per call by q4_0_mx_split_kernel, rows and blocks zero-padded):
+//   q    int8 [rows_pad][blocks_pad * 32]
+//   meta int2 [rows_pad][blocks_pad]   {fp32 bits of d_a, 8 * sum of the block's 32 values}
+constexpr int kMxKB = 4;        // Q4_0 blocks per pipeline stage (128 bytes of K)
+constexpr int kMxThreads = 256; // 8 warps
+constexpr int kMxRowAlign = 64; // the split activation is padded to the largest row tile
+constexpr int kMxAPitch = 144;  // bytes per staged activation row (128 + 16: conflict-free fragments)
+constexpr int kMxBPitch = 80;   // bytes per staged weight column (64 + 16)
+// BM rows x BN columns per CTA. Small row counts take narrow column tiles so that a narrow
+// matrix still gives every SM work (each output's block sum stays in one thread, in order, so
+// K is never split), and deeper pipelines since their stages are small.
+template <int BM>
+struct MxTile {
+    static constexpr int kBN = BM >= 64 ? 128 : 64;
+    static constexpr int kStages = BM >= 64 ? 4 : 6;
+    static constexpr int kWarpsM = BM >= 64 ? 2 : 1;             // warps along rows
+    static constexpr int kWarpsN = 8 / kWarpsM;                  // warps along columns
+    static constexpr int kM16 = BM / kWarpsM / 16;               // m16 tiles per warp
+    static constexpr int kN8 = kBN / kWarpsN / 8;                // n8 tiles per warp
+    static constexpr int kStageA = BM * kMxAPitch;
+    static constexpr int kStageMeta = BM * kMxKB * 8;
+    static constexpr int kStageB = kBN * kMxBPitch;
+    static constexpr int kStageScale = kBN * kMxKB * 2;
+    static constexpr int kStageBytes = kStageA + kStageMeta + kStageB + kStageScale;
+    static constexpr int kSmemBytes = kStages * kStageBytes;
+};
+
+uint32_t mx_rows_pad(uint32_t rows) { return (rows + kMxRowAlign - 1) / kMxRowAlign * kMxRowAlign; }
+uint32_t mx_blocks_pad(uint32_t blocks) { return (blocks + kMxKB - 1) / kMxKB * kMxKB; }
+
+struct MxSplitParams {
+    ActivationView view;  // Q8_0 blocks, or fp32 rows when view.f32 is set
+    uint32_t rows_pad, blocks_pad;
+    int8_t *q;
+    int2 *meta;
+};
+
+// One thread per (row, block) of the padded split activation; padding is written as zeros.
+__global__ void __launch_bounds__(256) q4_0_mx_split_kernel(const MxSplitParams p) {
+    const uint64_t total = static_cast<uint64_t>(p.rows_pad) * p.blocks_pad;
+    const bool vector = p.view.f32 != nullptr && (reinterpret_cast<uintptr_t>(p.view.f32) & 15u) == 0 &&
+                        (p.view.f32_stride & 3u) == 0;
+    for (uint64_t item = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; item < total;
+         item += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t row = static_cast<uint32_t>(item / p.blocks_pad);
+        const uint32_t block = static_cast<uint32_t>(item % p.blocks_pad);
+        uint32_t words[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        float d = 0.0f;
+        int sum = 0;
+        if (row < p.view.rows && block < p.view.blocks) {
+            uint16_t scale_bits;
+            if (p.view.f32 != nullptr) {
+                quantize_f32_block(p.view.f32 + static_cast<size_t>(row) * p.view.f32_stride + static_cast<size_t>(block) * 32,
+                                   vector, words, scale_bits);
+            } else {
+                read_activation_item(p.view, row * p.view.blocks + block, words, scale_bits);
+            }
+            d = __half2float(__ushort_as_half(scale_bits));
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sum = __dp4a(static_cast<int>(words[i]), 0x01010101, sum);
+        }
+        uint4 *q = reinterpret_cast<uint4 *>(p.q + (static_cast<size_t>(row) * p.blocks_pad + block) * 32);
+        q[0] = make_uint4(words[0], words[1], words[2], words[3]);
+        q[1] = make_uint4(words[4], words[5], words[6], words[7]);
+        p.meta[static_cast<size_t>(row) * p.blocks_pad + block] = make_int2(__float_as_int(d), 8 * sum);
+    }
+}
+
+struct MxParams {
+    const int8_t *q;
+    const int2 *meta;
+    uint32_t rows, blocks_pad;
+    const uint8_t *nibbles;
+    const uint16_t *scales;
+    uint32_t blocks, scale_stride;
+    uint32_t col0, out_col0, count;
+    float *destination;
+    size_t destination_stride;
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void *src, uint32_t bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "r"(bytes) : "memory");
+}
+
+// d = a . b + c (s32). c carries 0x4B400000 - 8 * sum(q) for the row: the MMA then returns the
+// bit pattern of the float 1.5 * 2^23 + dot, where dot = sum (code - 8) * q is the block's exact
+// integer dot (|dot| < 2^22, so that float is exact with a unit ulp), and one subtraction of
+// 1.5 * 2^23 yields (float)dot exactly.
+__device__ __forceinline__ void mma_s8(const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int c_lo, int c_hi, int (&d)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%10, %10, %11, %11};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c_lo), "r"(c_hi));
+}
+
+constexpr int kFloatMagic = 0x4B400000;  // bits of 1.5 * 2^23 = 12582912.0f
+
+// Packed fp32 pairs (sm_100 add/mul .f32x2): each lane rounds to nearest exactly as
+// __fadd_rn / __fmul_rn, two values per instruction.
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+    return static_cast<unsigned long long>(__float_as_uint(lo)) | (static_cast<unsigned long long>(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// BM rows x BN columns per CTA, 8 warps tiled over it (MxTile), kStages stages of 4 blocks.
+template <int BM>
+__global__ void __launch_bounds__(kMxThreads) q4_0_mx_kernel(const MxParams p) {
+    using Tile = MxTile<BM>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    const uint32_t tid = threadIdx.x;
+    const uint32_t warp = tid >> 5, lane = tid & 31;
+    const uint32_t group = lane >> 2, tig = lane & 3;
+    const uint32_t warp_m = warp / Tile::kWarpsN, warp_n = warp % Tile::kWarpsN;
+    const uint32_t warp_row0 = warp_m * (BM / Tile::kWarpsM);
+    const uint32_t warp_col0 = warp_n * (Tile::kBN / Tile::kWarpsN);
+    const uint32_t m0 = blockIdx.y * BM;
+    const uint32_t n0 = blockIdx.x * Tile::kBN;
+    const uint32_t chunks = p.blocks_pad / kMxKB;
+    const uint32_t k_bytes = p.blocks_pad * 32;
+
+    auto load_stage = [&](uint32_t s, uint32_t chunk) {
+        const uint32_t a_smem = static_cast<uint32_t>(__cvta_generic_to_shared(smem + s * Tile::kStageBytes));
+        // activation: BM rows x 128 bytes (in bounds: the split buffer is padded to 64 rows)
+        for (uint32_t i = tid; i < BM * 8; i += kMxThreads) {
+            const uint32_t row = i >> 3, seg = i & 7;
+            cp_async16(a_smem + row * kMxAPitch + seg * 16,
+                       p.q + static_cast<size_t>(m0 + row) * k_bytes + chunk * 128 + seg * 16, 16);
+        }
+        const uint32_t meta_smem = a_smem + Tile::kStageA;
+        for (uint32_t i = tid; i < BM * 2; i += kMxThreads) {
+            const uint32_t row = i >> 1, half = i & 1;
+            cp_async16(meta_smem + row * 32 + half * 16,
+                       p.meta + static_cast<size_t>(m0 + row) * p.blocks_pad + chunk * kMxKB + half * 2, 16);
+        }
+        // weights: 128 columns x 4 blocks of 16 bytes; columns or blocks past the end are zero-filled
+        const uint32_t b_smem = meta_smem + Tile::kStageMeta;
+        for (uint32_t i = tid; i < Tile::kBN * kMxKB; i += kMxThreads) {
+            const uint32_t col = i >> 2, blk = i & 3;
+            const uint32_t block = chunk * kMxKB + blk;
+            const bool valid = n0 + col < p.count && block < p.blocks;
+            const uint8_t *src = valid ? p.nibbles + (static_cast<size_t>(p.col0 + n0 + col) * p.blocks + block) * 16 : p.nibbles;
+            cp_async16(b_smem + col * kMxBPitch + blk * 16, src, valid ? 16u : 0u);
+        }
+        const uint32_t scale_smem = b_smem + Tile::kStageB;
+        for (uint32_t col = tid; col < Tile::kBN; col += kMxThreads) {
+            const bool valid = n0 + col < p.count;
+            const uint16_t *src = valid ? p.scales + static_cast<size_t>(p.col0 + n0 + col) * p.scale_stride + chunk * kMxKB : p.scales;
+            cp_async8(scale_smem + col * 8, src, valid ? 8u : 0u);
+        }
+    };
+
+    // acc[mt][nt][h]: the thread's two adjacent columns of row group (h = 0) or group + 8 (h = 1).
+    unsigned long long acc[Tile::kM16][Tile::kN8][2];
+#pragma unroll
+    for (int mt = 0; mt < Tile::kM16; ++mt)
+#pragma unroll
+        for (int nt = 0; nt < Tile::kN8; ++nt) acc[mt][nt][0] = acc[mt][nt][1] = 0ull;
+
+    // Tile::kStages - 1 chunks in flight ahead of the one being computed. Every iteration commits one
+    // group (empty past the end) so that wait_group counts stay uniform.
+#pragma unroll
+    for (int s = 0; s < Tile::kStages - 1; ++s) {
+        if (static_cast<uint32_t>(s) < chunks) load_stage(s, s);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    for (uint32_t chunk = 0; chunk < chunks; ++chunk) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(Tile::kStages - 2) : "memory");
+        __syncthreads();  // chunk's stage is complete for all threads; the stage loaded next was computed last iteration
+        const uint32_t next = chunk + Tile::kStages - 1;
+        if (next < chunks) load_stage(next % Tile::kStages, next);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+
+        const uint8_t *base = smem + (chunk % Tile::kStages) * Tile::kStageBytes;
+        const uint8_t *stage_a = base;
+        const int2 *stage_meta = reinterpret_cast<const int2 *>(base + Tile::kStageA);
+        const uint8_t *stage_b = base + Tile::kStageA + Tile::kStageMeta;
+        const uint16_t *stage_scale = reinterpret_cast<const uint16_t *>(stage_b + Tile::kStageB);
+        const uint32_t valid_blocks = min(static_cast<uint32_t>(kMxKB), p.blocks - chunk * kMxKB);
+        for (uint32_t bb = 0; bb < valid_blocks; ++bb) {
+            uint32_t b[Tile::kN8][2];
+            unsigned long long dw[Tile::kN8];  // weight scales of the thread's two output columns
+#pragma unroll
+            for (int nt = 0; nt < Tile::kN8; ++nt) {
+                const uint32_t col = warp_col0 + nt * 8 + group;
+                const uint32_t w = *reinterpret_cast<const uint32_t *>(stage_b + col * kMxBPitch + bb * 16 + tig * 4);
+                b[nt][0] = w & 0x0F0F0F0Fu;
+                b[nt][1] = (w >> 4) & 0x0F0F0F0Fu;
+                const uint32_t out_col = warp_col0 + nt * 8 + tig * 2;
+                dw[nt] = pack2(__half2float(__ushort_as_half(stage_scale[out_col * kMxKB + bb])),
+                               __half2float(__ushort_as_half(stage_scale[(out_col + 1) * kMxKB + bb])));
+            }
+#pragma unroll
+            for (int mt = 0; mt < Tile::kM16; ++mt) {
+                const uint32_t row_lo = warp_row0 + mt * 16 + group;
+                const uint8_t *a_lo = stage_a + row_lo * kMxAPitch + bb * 32 + tig * 4;
+                const uint8_t *a_hi = a_lo + 8 * kMxAPitch;
+                const uint32_t a[4] = {*reinterpret_cast<const uint32_t *>(a_lo), *reinterpret_cast<const uint32_t *>(a_hi),
+                                       *reinterpret_cast<const uint32_t *>(a_lo + 16), *reinterpret_cast<const uint32_t *>(a_hi + 16)};
+                const int2 meta_lo = stage_meta[row_lo * kMxKB + bb];
+                const int2 meta_hi = stage_meta[(row_lo + 8) * kMxKB + bb];
+                const unsigned long long da[2] = {pack2(__int_as_float(meta_lo.x), __int_as_float(meta_lo.x)),
+                                                  pack2(__int_as_float(meta_hi.x), __int_as_float(meta_hi.x))};
+                const unsigned long long unbias = pack2(-12582912.0f, -12582912.0f);
+#pragma unroll
+                for (int nt = 0; nt < Tile::kN8; ++nt) {
+                    int d[4];
+                    mma_s8(a, b[nt][0], b[nt][1], kFloatMagic - meta_lo.y, kFloatMagic - meta_hi.y, d);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        // ((float)dot * d_a) * d_w, then the add: the reference program's roundings.
+                        unsigned long long v = add2(pack2(__int_as_float(d[2 * h]), __int_as_float(d[2 * h + 1])), unbias);
+                        v = mul2(v, da[h]);
+                        v = mul2(v, dw[nt]);
+                        // The accumulate stays scalar: a packed add after a packed multiply may be
+                        // contracted into a fused multiply-add, which would drop the product's rounding.
+                        const unsigned long long a_pair = acc[mt][nt][h];
+                        acc[mt][nt][h] = pack2(__fadd_rn(__uint_as_float(static_cast<uint32_t>(a_pair)), __uint_as_float(static_cast<uint32_t>(v))),
+                                               __fadd_rn(__uint_as_float(static_cast<uint32_t>(a_pair >> 32)), __uint_as_float(static_cast<uint32_t>(v >> 32))));
+                    }
+                }
+            }
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+
+#pragma unroll
+    for (int mt = 0; mt < Tile::kM16; ++mt) {
+#pragma unroll
+        for (int nt = 0; nt < Tile::kN8; ++nt) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t row = m0 + warp_row0 + mt * 16 + group + (i < 2 ? 0 : 8);
+                const uint32_t col = n0 + warp_col0 + nt * 8 + tig * 2 + (i & 1);
+                const unsigned long long pair = acc[mt][nt][i >> 1];
+                const float value = __uint_as_float(static_cast<uint32_t>((i & 1) ? pair >> 32 : pair));
+                if (row < p.rows && col < p.count)
+                    p.destination[static_cast<size_t>(row) * p.destination_stride + p.out_col0 + col] = value;
+            }
+        }
+    }
+}
+
+template <int BM>
+cudaError_t launch_mx_tiles(const MxParams &p, uint32_t rows_pad, uint32_t count, cudaStream_t stream) {
+    static bool configured = false;
+    if (!configured) {
+        const cudaError_t error = cudaFuncSetAttribute(q4_0_mx_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       MxTile<BM>::kSmemBytes);
+        if (error != cudaSuccess) return error;
+        configured = true;
+    }
+    const dim3 grid((count + MxTile<BM>::kBN - 1) / MxTile<BM>::kBN, (p.rows + BM - 1) / BM);
+    (void)rows_pad;
+    q4_0_mx_kernel<BM><<<grid, kMxThreads, MxTile<BM>::kSmemBytes, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_mx(const Q40Weights &weights, const ActivationView &view, uint8_t *scratch, float *destination,
+                      size_t destination_stride, uint32_t col0, uint32_t out_col0, uint32_t count, int sm_count,
+                      cudaStream_t stream) {
+    const uint32_t rows_pad = mx_rows_pad(view.rows);
+    const uint32_t blocks_pad = mx_blocks_pad(weights.blocks);
+    MxSplitParams split{view, rows_pad, blocks_pad, reinterpret_cast<int8_t *>(scratch),
+                        reinterpret_cast<int2 *>(scratch + static_cast<size_t>(rows_pad) * blocks_pad * 32)};
+    const uint64_t items = static_cast<uint64_t>(rows_pad) * blocks_pad;
+    const uint32_t split_grid = static_cast<uint32_t>(items / 256 + 1 < 148ull * 32ull ? items / 256 + 1 : 148ull * 32ull);
+    q4_0_mx_split_kernel<<<split_grid, 256, 0, stream>>>(split);
+    cudaError_t error = cudaGetLastError();
+    if (error != cudaSuccess) return error;
+    MxParams p{};
+    p.q = split.q;
+    p.meta = split.meta;
+    p.rows = view.rows;
+    p.blocks_pad = blocks_pad;
+    p.nibbles = weights.nibbles;
+    p.scales = weights.scales;
+    p.blocks = weights.blocks;
+    p.scale_stride = weights.scale_stride;
+    p.col0 = col0;
+    p.out_col0 = out_col0;
+    p.count = count;
+    p.destination = destination;
+    p.destination_stride = destination_stride;
+    // Few rows: the smallest row tile that holds them (fewer padded rows computed, more CTAs);
+    // 33..64 rows keep the wide 64 x 128 tiles only when those fill a wave of SMs.
+    if (view.rows <= 16) return launch_mx_tiles<16>(p, rows_pad, count, stream);
+    const uint64_t wide_ctas = static_cast<uint64_t>((count + MxTile<64>::kBN - 1) / MxTile<64>::kBN) * ((view.rows + 63) / 64);
+    if (view.rows <= 32 || (view.rows <= 64 && wide_ctas < static_cast<uint64_t>(sm_count)))
+        return launch_mx_tiles<32>(p, rows_pad, count, stream);
+    return launch_mx_tiles<64>(p, rows_pad, count, stream);
+}
+
 }  // namespace
 
 cudaError_t launch_q4_0_q8_0_gemv(const Q40Weights &weights, const uint8_t *activation, uint32_t rows,
@@ -575,6 +897,28 @@ cudaError_t launch_q4_0_f32_gemv(const Q40Weights &weights, const float *source,
         case 4: return launch_rows<4, true>(p, sm_count, stream);
         default: return cudaErrorInvalidValue;
     }
+}
+
+size_t q4_0_mx_scratch_bytes(uint32_t rows, uint32_t blocks) {
+    return static_cast<size_t>(mx_rows_pad(rows)) * mx_blocks_pad(blocks) * (32 + 8);
+}
+
+cudaError_t launch_q4_0_mx(const Q40Weights &weights, const uint8_t *activation, const float *f32_source,
+                           size_t f32_stride, uint32_t rows, uint32_t interleave, uint8_t *scratch, float *destination,
+                           size_t destination_stride, uint32_t col0, uint32_t out_col0, uint32_t count, int sm_count,
+                           cudaStream_t stream) {
+    if (count == 0 || rows == 0) return cudaSuccess;
+    if ((reinterpret_cast<uintptr_t>(weights.nibbles) & 15u) != 0 || (reinterpret_cast<uintptr_t>(weights.scales) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(scratch) & 15u) != 0 || weights.scale_stride % 8 != 0 ||
+        weights.scale_stride < weights.blocks || (activation == nullptr) == (f32_source == nullptr) ||
+        (activation != nullptr && (reinterpret_cast<uintptr_t>(activation) & 1u) != 0) ||
+        (f32_source != nullptr && ((reinterpret_cast<uintptr_t>(f32_source) & 3u) != 0 ||
+                                   f32_stride < static_cast<size_t>(weights.blocks) * 32))) {
+        return cudaErrorInvalidValue;
+    }
+    const ActivationView view{activation, rows, weights.blocks, f32_source != nullptr ? 0u : interleave, f32_source,
+                              f32_stride};
+    return launch_mx(weights, view, scratch, destination, destination_stride, col0, out_col0, count, sm_count, stream);
 }
 
 cudaError_t launch_q4_0_q8_0_gemv_native(const uint8_t *activation, uint32_t rows, uint32_t blocks,

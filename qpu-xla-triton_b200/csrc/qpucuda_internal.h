@@ -162,6 +162,14 @@ cudaError_t launch_q4_0_q8_0_gemv(const Q40Weights &weights, const uint8_t *acti
 cudaError_t launch_q4_0_f32_gemv(const Q40Weights &weights, const float *source, size_t source_stride, uint32_t rows,
                                  float *destination, size_t destination_stride, uint32_t col0, uint32_t out_col0,
                                  uint32_t count, int sm_count, cudaStream_t stream);
+// Rows > 4 (the reference's MX path) on the tensor cores: splits the activation (Q8_0 blocks, or
+// fp32 rows quantized on the fly; exactly one of the two) into `scratch` of
+// q4_0_mx_scratch_bytes(rows, blocks) bytes (16-byte aligned), then the tiled mma.sync kernel.
+size_t q4_0_mx_scratch_bytes(uint32_t rows, uint32_t blocks);
+cudaError_t launch_q4_0_mx(const Q40Weights &weights, const uint8_t *activation, const float *f32_source,
+                           size_t f32_stride, uint32_t rows, uint32_t interleave, uint8_t *scratch, float *destination,
+                           size_t destination_stride, uint32_t col0, uint32_t out_col0, uint32_t count, int sm_count,
+                           cudaStream_t stream);
 // Native 18-byte blocks [columns][blocks][18] -> prepared layout (scales rows of scale_stride,
 // the padding must be zeroed beforehand).
 cudaError_t launch_q4_0_repack(const uint8_t *native, uint32_t columns, uint32_t blocks, uint32_t scale_stride,

@@ -97,8 +97,12 @@ def test_argument_rules_follow_the_reference(native) -> None:  # type: ignore[no
     assert status == _native.Status.INVALID_ARGUMENT  # unaligned window
     status, _ = prepare(native, weights, rows=1, start=48, count=32)
     assert status == _native.Status.INVALID_ARGUMENT  # window past the matrix
-    status, _ = prepare(native, weights, rows=16)
-    assert status == _native.Status.CAPABILITY_MISSING  # the MX (M >= 16) path is not built
+    status, _ = prepare(native, weights, rows=4 * 65535 + 1)
+    assert status == _native.Status.INVALID_ARGUMENT  # past the reference's row limit
+    for mode in (1, 2):  # COLUMN_W8, ROWCOL_W8A8: re-quantized modes are not built
+        desc = _native.Q40LinearDesc(weights.ctypes.data, weights.nbytes, 64, 64, 16, 0, 64, mode, 0, native.lib.qpucuda_q4_0_kernel_source_hash())
+        handle = ctypes.c_void_p()
+        assert native.call("qpucuda_q4_0_linear_prepare", ctypes.byref(desc), ctypes.byref(handle)) == _native.Status.CAPABILITY_MISSING
     status, handle = prepare(native, weights, rows=4, start=16, count=32)
     assert status == _native.Status.OK
     activation = np.zeros((4, 2, 34), dtype=np.uint8)
@@ -280,5 +284,67 @@ def test_decode_full_size_columns_sample(native, shape) -> None:  # type: ignore
         sample = np.sort(np.random.default_rng(1).choice(shape.out_features, 96, replace=False))
         expected = oracle.q4_0_q8_0_linear(activation.cpu().numpy(), weight_blocks[sample])
         assert max_relative_error(out.cpu().numpy()[:, sample], expected) <= Q4_0_TOLERANCE
+    finally:
+        native.lib.qpucuda_q4_0_linear_destroy(handle)
+
+
+@pytest.mark.parametrize(
+    "rows,k,n,start,count",
+    [
+        (5, 2048, 96, 16, 64),  # fewest MX rows, one partial 16-row tile
+        (20, 2048, 256, 0, 256),  # a 32-row tile
+        (64, 4128, 160, 0, 160),  # 129 blocks: a partial last K stage
+        (100, 5632, 2048, 512, 1024),  # ragged rows, a column window
+        (300, 8192, 384, 128, 256),  # several row tiles, a partial column tile
+    ],
+)
+def test_mx_rows_match_the_reference_program(native, rows: int, k: int, n: int, start: int, count: int) -> None:  # type: ignore[no-untyped-def]
+    """Rows > 4 (the reference's MX path) on the tensor cores through every entry point: bit for bit
+    against the reference program's arithmetic (oracle.q4_0_q8_0_linear_mx) and within the stated
+    tolerance of ggml_q4_0_q8_0_reference (oracle.q4_0_q8_0_linear)."""
+    import torch
+
+    from gpu_helpers import max_relative_error
+
+    source, weight = workloads.torch_linear_inputs(rows, k, n, seed=rows + k, weight_std=0.02, device="cuda")
+    weight_blocks = native.quantize_blocks(weight, "q4_0").cpu().numpy()
+    activation = native.quantize_blocks(source, "q8_0")
+    activation_host = np.ascontiguousarray(activation.cpu().numpy())
+    status, handle = prepare(native, weight_blocks, rows=rows, start=start, count=count)
+    assert status == _native.Status.OK
+    try:
+        window = slice(start, start + count)
+        expected = oracle.q4_0_q8_0_linear_mx(activation_host, weight_blocks[window])
+        assert max_relative_error(expected, oracle.q4_0_q8_0_linear(activation_host, weight_blocks[window])) <= Q4_0_TOLERANCE
+        native.context.set_stream(torch.cuda.current_stream().cuda_stream)
+        device_out = torch.full((rows, count + 3), float("nan"), dtype=torch.float32, device="cuda")
+        native.context.check(
+            native.lib.qpucuda_q4_0_linear_execute_device(handle, activation.data_ptr(), rows, device_out.data_ptr(), count + 3, start, count, 2),
+            "execute_device",
+        )
+        fused_out = torch.full((rows, count), float("nan"), dtype=torch.float32, device="cuda")
+        native.context.check(
+            native.lib.qpucuda_q4_0_linear_execute_f32_device(handle, source.data_ptr(), source.stride(0), rows, fused_out.data_ptr(), count, start, count, 0),
+            "execute_f32_device",
+        )
+        native.sync()
+        got = device_out.cpu().numpy()
+        np.testing.assert_array_equal(got[:, 2 : 2 + count], expected)
+        assert np.isnan(got[:, :2]).all() and np.isnan(got[:, 2 + count :]).all()
+        np.testing.assert_array_equal(fused_out.cpu().numpy(), expected)
+        host = np.full((rows, n), np.nan, dtype=np.float32)
+        assert execute_host(native, handle, activation_host, host, start, count) == _native.Status.OK
+        np.testing.assert_array_equal(host[:, window], expected)
+        if rows % 4 == 0:
+            grouped = np.concatenate([interleave_q8_0x4(activation_host[r : r + 4], 8) for r in range(0, rows, 4)], axis=0)
+            packed = np.full((rows, n), np.nan, dtype=np.float32)
+            assert execute_host(native, handle, grouped, packed, start, count, interleave=8) == _native.Status.OK
+            np.testing.assert_array_equal(packed[:, window], expected)
+        submission = ctypes.c_void_p()
+        execution = _native.Q40Execution(activation_host.ctypes.data, activation_host.nbytes, 0, host.ctypes.data, host.nbytes, 0, start, count, rows, 0)
+        assert native.lib.qpucuda_q4_0_linear_submit(handle, ctypes.byref(execution), ctypes.byref(submission)) == _native.Status.OK
+        assert native.lib.qpucuda_q4_0_submission_cpu_fallback(submission) == _native.Status.CAPABILITY_MISSING
+        assert native.lib.qpucuda_q4_0_submission_wait(submission, None) == _native.Status.OK
+        native.lib.qpucuda_q4_0_submission_destroy(submission)
     finally:
         native.lib.qpucuda_q4_0_linear_destroy(handle)

@@ -212,7 +212,10 @@ def run_ours(args: argparse.Namespace) -> None:
         projections.append({"name": name, "k": k, "n": n, "gather": gather, "plan": plan, "q4": q4, "local": local, "full": full, "source": sources[k]})
         del weight, values, scales, q4_blocks
     exchange = "none"
-    if world > 1:
+    if world > 1 and args.exchange == "nccl":
+        exchange = "NCCL all-gather after the GEMM (selected with --exchange nccl)"
+        barrier_flag = None
+    elif world > 1:
         from qpu_xla.sharded import PeerOutput
 
         exchange = "fused GEMM epilogue stores into every rank's output (CUDA IPC over NVLink) + NCCL all-reduce barrier"
@@ -585,6 +588,12 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=15.0)
     parser.add_argument("--only", default="", help="comma-separated projections (profiling captures only)")
+    parser.add_argument(
+        "--exchange",
+        choices=("fused", "nccl"),
+        default="fused",
+        help="N > 1: fused GEMM + all-gather over NVLink (default) or NCCL all-gather after the GEMM",
+    )
     args = parser.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

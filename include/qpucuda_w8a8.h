@@ -78,7 +78,10 @@ qpucuda_status qpucuda_w8a8_linear_prepare(
 void qpucuda_w8a8_linear_destroy(qpucuda_w8a8_linear *linear);
 size_t qpucuda_w8a8_linear_resident_bytes(const qpucuda_w8a8_linear *linear);
 /* Host buffers in and out; copies through pinned staging; on a failed wait
- * the destination is left untouched and the context is poisoned. */
+ * the destination is left untouched and the context is poisoned. Batches of
+ * more than 1024 rows are pipelined in 1024-row slices (host-to-device copy,
+ * GEMM and device-to-host copy overlap); the destination is written only after
+ * the wait for the whole call has succeeded. */
 qpucuda_status qpucuda_w8a8_linear_execute(qpucuda_w8a8_linear *linear, const qpucuda_w8a8_execution *execution);
 
 /* Device pointers, asynchronous on the context stream:

@@ -12,6 +12,9 @@
 #include <cstdlib>
 #include <cstring>
 #include <new>
+#include <chrono>
+#include <thread>
+#include <vector>
 
 #include "qpucuda_internal.h"
 #include "qpucuda_peer.h"
@@ -38,6 +41,10 @@ struct qpucuda_w8a8_linear {
     float *h_destination = nullptr;
     float *d_source = nullptr;
     float *d_destination = nullptr;
+    // Host-buffer path for large batches: copy streams and per-slice events, made on first use.
+    cudaStream_t copy_in = nullptr;
+    cudaStream_t copy_out = nullptr;
+    std::vector<cudaEvent_t> events;
     size_t resident_bytes = 0;
     bool busy = false;
     std::mutex mutex;
@@ -59,8 +66,90 @@ void free_linear(qpucuda_w8a8_linear *linear) {
     cudaFree(linear->d_source);
     cudaFree(linear->d_destination);
     cudaFreeHost(linear->h_destination);
+    if (linear->copy_in != nullptr) cudaStreamDestroy(linear->copy_in);
+    if (linear->copy_out != nullptr) cudaStreamDestroy(linear->copy_out);
+    for (cudaEvent_t event : linear->events) cudaEventDestroy(event);
     (void)cudaGetLastError();
     delete linear;
+}
+
+constexpr uint32_t kSliceRows = 1024;
+
+bool ensure_pipeline(qpucuda_w8a8_linear *linear, uint32_t slices) {
+    if (linear->copy_in == nullptr &&
+        (cudaStreamCreateWithFlags(&linear->copy_in, cudaStreamNonBlocking) != cudaSuccess ||
+         cudaStreamCreateWithFlags(&linear->copy_out, cudaStreamNonBlocking) != cudaSuccess)) {
+        (void)cudaGetLastError();
+        return false;
+    }
+    const size_t needed = 2u * slices + 2u;
+    while (linear->events.size() < needed) {
+        cudaEvent_t event = nullptr;
+        if (cudaEventCreateWithFlags(&event, cudaEventDisableTiming) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return false;
+        }
+        linear->events.push_back(event);
+    }
+    return true;
+}
+
+qpucuda_status enqueue(qpucuda_w8a8_linear *linear, const float *source, size_t source_stride,
+                       const int8_t *quantized, size_t quantized_stride, const float *row_scales, uint32_t rows,
+                       float *destination, size_t destination_stride);
+
+// Pipelined host-buffer execution: slice s is copied in on copy_in, quantized and multiplied on
+// the context stream after its copy, and copied out to the pinned staging on copy_out after its
+// GEMM (events 1 + 2s copied in, 2 + 2s computed); the last copy-out is joined back into the
+// context stream, whose bounded wait then covers every copy and kernel of the call.
+qpucuda_status enqueue_sliced(qpucuda_w8a8_linear *linear, const float *source, uint32_t rows, uint32_t slices) {
+    qpucuda_context *context = linear->context;
+    cudaEvent_t *events = linear->events.data();
+    cudaError_t error = cudaEventRecord(events[0], context->stream);  // earlier work on the stream comes first
+    if (error == cudaSuccess) error = cudaStreamWaitEvent(linear->copy_in, events[0], 0);
+    if (error == cudaSuccess) error = cudaStreamWaitEvent(linear->copy_out, events[0], 0);
+    if (error != cudaSuccess) return cuda_fail(context, error, "order W8A8 copy streams");
+    for (uint32_t s = 0; s < slices; ++s) {
+        const uint32_t first = s * kSliceRows;
+        const uint32_t count = rows - first < kSliceRows ? rows - first : kSliceRows;
+        cudaEvent_t copied = events[1 + 2 * s], computed = events[2 + 2 * s];
+        error = cudaMemcpyAsync(linear->d_source + static_cast<size_t>(first) * linear->k,
+                                source + static_cast<size_t>(first) * linear->k,
+                                static_cast<size_t>(count) * linear->k * sizeof(float), cudaMemcpyHostToDevice,
+                                linear->copy_in);
+        if (error == cudaSuccess) error = cudaEventRecord(copied, linear->copy_in);
+        if (error == cudaSuccess) error = cudaStreamWaitEvent(context->stream, copied, 0);
+        if (error != cudaSuccess) return cuda_fail(context, error, "copy W8A8 source slice");
+        const qpucuda_status status =
+            enqueue(linear, linear->d_source + static_cast<size_t>(first) * linear->k, linear->k, nullptr, 0, nullptr,
+                    count, linear->d_destination + static_cast<size_t>(first) * linear->columns, linear->columns);
+        if (status != QPUCUDA_OK) return status;
+        error = cudaEventRecord(computed, context->stream);
+        if (error == cudaSuccess) error = cudaStreamWaitEvent(linear->copy_out, computed, 0);
+        if (error == cudaSuccess)
+            error = cudaMemcpyAsync(linear->h_destination + static_cast<size_t>(first) * linear->columns,
+                                    linear->d_destination + static_cast<size_t>(first) * linear->columns,
+                                    static_cast<size_t>(count) * linear->columns * sizeof(float),
+                                    cudaMemcpyDeviceToHost, linear->copy_out);
+        if (error != cudaSuccess) return cuda_fail(context, error, "copy W8A8 destination slice");
+    }
+    cudaEvent_t done = events[1 + 2 * slices];
+    error = cudaEventRecord(done, linear->copy_out);
+    if (error == cudaSuccess) error = cudaStreamWaitEvent(context->stream, done, 0);
+    if (error != cudaSuccess) return cuda_fail(context, error, "join W8A8 copy streams");
+    return QPUCUDA_OK;
+}
+
+// Bounded drain of both copy streams after a failure, so the plan's staging is not reused while
+// a copy into or out of it may still be running (the context is poisoned or failed by then).
+void drain_copies(qpucuda_w8a8_linear *linear) {
+    const uint64_t start = monotonic_ns();
+    for (cudaStream_t stream : {linear->copy_in, linear->copy_out}) {
+        while (cudaStreamQuery(stream) == cudaErrorNotReady && monotonic_ns() - start <= linear->context->timeout_ns) {
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
+        }
+    }
+    (void)cudaGetLastError();
 }
 
 // Enqueue quantize + GEMM/GEMV + epilogue for `rows` rows already resident on the device.
@@ -395,17 +484,38 @@ qpucuda_status qpucuda_w8a8_linear_execute(qpucuda_w8a8_linear *linear, const qp
     // The source is copied straight from the caller's buffer (a DMA when it is pinned). The
     // result lands in plan-owned pinned staging first and reaches the caller only after a
     // successful wait, so a failed or timed-out wait never writes the caller's destination.
-    cudaError_t error =
-        cudaMemcpyAsync(linear->d_source, execution->source, source_bytes, cudaMemcpyHostToDevice, context->stream);
-    if (error != cudaSuccess) return release(cuda_fail(context, error, "copy W8A8 source"));
-    status = enqueue(linear, linear->d_source, linear->k, nullptr, 0, nullptr, rows, linear->d_destination,
-                     linear->columns);
-    if (status != QPUCUDA_OK) return release(status);
-    error = cudaMemcpyAsync(linear->h_destination, linear->d_destination, destination_bytes, cudaMemcpyDeviceToHost,
-                            context->stream);
-    if (error != cudaSuccess) return release(cuda_fail(context, error, "copy W8A8 destination"));
+    // Batches above kSliceRows rows are pipelined in row slices: host-to-device copies on one
+    // stream, quantize + GEMM on the context stream and device-to-host copies on another, so
+    // the two PCIe directions overlap each other and the compute.
+    const uint32_t slices = rows > kSliceRows ? (rows + kSliceRows - 1) / kSliceRows : 1;
+    if (slices > 1 && !ensure_pipeline(linear, slices)) {
+        return release(fail(context, QPUCUDA_ALLOCATION_FAILED, "create W8A8 copy streams"));
+    }
+    cudaError_t error = cudaSuccess;
+    if (slices == 1) {
+        error = cudaMemcpyAsync(linear->d_source, execution->source, source_bytes, cudaMemcpyHostToDevice,
+                                context->stream);
+        if (error != cudaSuccess) return release(cuda_fail(context, error, "copy W8A8 source"));
+        status = enqueue(linear, linear->d_source, linear->k, nullptr, 0, nullptr, rows, linear->d_destination,
+                         linear->columns);
+        if (status != QPUCUDA_OK) return release(status);
+        error = cudaMemcpyAsync(linear->h_destination, linear->d_destination, destination_bytes,
+                                cudaMemcpyDeviceToHost, context->stream);
+        if (error != cudaSuccess) return release(cuda_fail(context, error, "copy W8A8 destination"));
+    } else {
+        status = enqueue_sliced(linear, static_cast<const float *>(execution->source), rows, slices);
+        if (status != QPUCUDA_OK) {
+            (void)wait_stream(context);  // drain whatever was issued before the failure (bounded)
+            drain_copies(linear);
+            return release(status);
+        }
+    }
     status = wait_stream(context);
-    if (status == QPUCUDA_OK) parallel_memcpy(execution->destination, linear->h_destination, destination_bytes);
+    if (status == QPUCUDA_OK) {
+        parallel_memcpy(execution->destination, linear->h_destination, destination_bytes);
+    } else if (slices > 1) {
+        drain_copies(linear);
+    }
     return release(status);
 }
 

@@ -67,6 +67,21 @@ def test_prepared_linear_on_a_queue_matches_the_reference(cuda_device: Device, g
         np.testing.assert_array_equal(plan.execute_host(case.source), ref["output"])
 
 
+def test_host_execute_of_a_large_batch_is_sliced_and_exact(cuda_device: Device) -> None:
+    """Batches above 1024 rows go through the pipelined host path (copy in, GEMM, copy out in
+    row slices on three streams); a ragged last slice and a reused plan stay bit-exact."""
+    rng = np.random.default_rng(71)
+    rows, k, n = 2500, 320, 384
+    weight = rng.standard_normal((n, k)).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32)
+    values, scales = oracle.quantize_per_output_channel_int8(weight)
+    with PreparedW8A8Linear(cuda_device, QuantizedMatrixInt8(values, scales), max_batch=rows, bias=bias) as plan:
+        for batch in (rows, 1025, 2048):
+            source = (rng.standard_normal((batch, k)) * rng.uniform(0.1, 8.0, (batch, 1))).astype(np.float32)
+            expected = oracle.w8a8_linear(source, values, scales, bias)
+            np.testing.assert_array_equal(plan.execute_host(source), expected)
+
+
 def test_plan_binding_and_in_flight_rules(cuda_device: Device) -> None:
     from qpu_xla import DependencyError
 

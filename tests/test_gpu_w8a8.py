@@ -244,31 +244,35 @@ def test_sharded_case_full_size_rows_and_columns_sample(native, shape) -> None: 
         native.lib.qpucuda_w8a8_linear_destroy(handle)
 
 
-def test_host_buffer_execute_and_injected_failures() -> None:
+@pytest.mark.parametrize("rows", (512, 2500), ids=("one-slice", "pipelined-slices"))
+def test_host_buffer_execute_and_injected_failures(rows: int) -> None:
     """qpucuda_w8a8_linear_execute with host buffers; FAIL_SUBMISSION and FAIL_WAIT leave the
-    destination untouched, and a failed wait poisons the context (qpu_llama_runtime.c:688-727)."""
+    destination untouched, and a failed wait poisons the context (qpu_llama_runtime.c:688-727).
+    2500 rows take the pipelined path (row slices of 1024 on separate copy streams)."""
     from gpu_helpers import Native
 
     native = Native()
     try:
         case = workloads.square_case(512)
         values, scales = oracle.quantize_per_output_channel_int8(case.weight)
-        handle = native.w8a8_prepare(values, scales, case.bias, max_batch=512)
-        destination = np.full((512, 512), -777.0, dtype=np.float32)
+        source = np.ascontiguousarray(np.tile(case.source, ((rows + 511) // 512, 1))[:rows])
+        source[512:] *= np.float32(1.5)
+        handle = native.w8a8_prepare(values, scales, case.bias, max_batch=rows)
+        destination = np.full((rows, 512), -777.0, dtype=np.float32)
 
         def execute() -> int:
-            execution = _native.W8A8Execution(case.source.ctypes.data, case.source.nbytes, destination.ctypes.data, destination.nbytes, 512)
+            execution = _native.W8A8Execution(source.ctypes.data, source.nbytes, destination.ctypes.data, destination.nbytes, rows)
             return int(native.lib.qpucuda_w8a8_linear_execute(handle, ctypes.byref(execution)))
 
         assert execute() == _native.Status.OK
-        np.testing.assert_array_equal(destination, oracle.w8a8_linear(case.source, values, scales, case.bias))
+        np.testing.assert_array_equal(destination, oracle.w8a8_linear(source, values, scales, case.bias))
         destination[:] = -777.0
         native.context.set_failure_mask(int(_native.FailurePoint.SUBMISSION))
         assert execute() == _native.Status.SUBMISSION_FAILED
         assert np.all(destination == -777.0)
         native.context.set_failure_mask(int(_native.FailurePoint.WAIT))
         assert execute() == _native.Status.TIMEOUT
-        assert np.all(destination == -777.0)
+        assert np.all(destination == -777.0), "wait failure exposed partial output"
         native.context.set_failure_mask(0)
         assert native.context.poisoned
         assert execute() == _native.Status.IO_FAILED

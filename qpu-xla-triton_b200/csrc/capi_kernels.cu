@@ -65,7 +65,8 @@ qpucuda_status qpucuda_quantize_rows_int8(qpucuda_context *context, const float 
     if (status != QPUCUDA_OK) return status;
     DeviceGuard guard(context->device);
     return launched(context,
-                    launch_quantize_rows_int8(x, x_stride, rows, cols, padded_cols, q, q_stride, scales, context->stream),
+                    launch_quantize_rows_int8(x, x_stride, rows, cols, padded_cols, q, q_stride, scales,
+                                              context->d_error, context->stream),
                     "quantize_rows_int8");
 }
 

@@ -88,7 +88,7 @@ qpucuda_status qpucuda_w8a8_linear_execute_static(qpucuda_context *context, cons
     // The quantizer rewrites every byte the GEMM reads (all rows x padded K, zeros in the padding,
     // and every row scale), so nothing left from an earlier call needs clearing.
     cudaError_t error = launch_quantize_rows_int8(source, source_stride, rows, k, k_pad, quantized, k_pad, row_scales,
-                                                  context->stream);
+                                                  context->d_error, context->stream);
     if (error != cudaSuccess) return cuda_fail(context, error, "no-alloc W8A8 linear: quantize");
     GemmEpilogue epilogue;
     epilogue.mode = bias != nullptr ? EpilogueMode::kDequantizeBias : EpilogueMode::kDequantize;

@@ -164,7 +164,7 @@ qpucuda_status enqueue_to(qpucuda_w8a8_linear *linear, const float *source, size
     if (source != nullptr) {
         const cudaError_t error = launch_quantize_rows_int8(source, source_stride, rows, linear->k, linear->k_pad,
                                                             linear->d_quantized, linear->k_pad, linear->d_row_scales,
-                                                            stream);
+                                                            context->d_error, stream);
         if (error != cudaSuccess) return cuda_fail(context, error, "quantize activations");
         quantized = linear->d_quantized;
         quantized_stride = linear->k_pad;

@@ -80,9 +80,11 @@ bool encode_tensor_map_2d_u8(CUtensorMap *map, const void *base, uint64_t inner_
 
 // ---- kernel launchers (one per .cu file) -------------------------------------------------
 
+// Many long aligned rows take a bulk-copy staged kernel whose bounded waits report through
+// error_word (the context's error word); with error_word null the register-cached kernel runs.
 cudaError_t launch_quantize_rows_int8(const float *x, size_t x_stride, uint32_t rows, uint32_t cols,
                                       uint32_t padded_cols, int8_t *q, size_t q_stride, float *scales,
-                                      cudaStream_t stream);
+                                      unsigned int *error_word, cudaStream_t stream);
 // Same quantizer over rows whose elements need not be contiguous: element (r, c) at
 // (r / rows_per_batch) * batch_stride + (r % rows_per_batch) * row_stride + c * col_stride.
 cudaError_t launch_quantize_rows_int8_layout(const float *x, uint32_t rows, uint32_t cols, uint32_t padded_cols,

@@ -3,13 +3,16 @@
 //  * quantize_rows_int8: per-row symmetric int8 (src/qpu_xla/models/tinyllama/quantization.py:156-171,
 //    :1065-1071 for activations, :1085-1092 for weights). One CTA per row; the row is read once with
 //    128-bit loads into registers, reduced to max|x| with warp shuffles, then quantized from registers.
-//    Bit-exact with NumPy: IEEE division (__fdiv_rn, never fast-math), round-half-even, clamp to +-127.
+//    Rows longer than ~14.5K columns stream through shared memory instead (bulk copies, two stages).
+//    Bit-exact with NumPy: the quotient x / scale is the IEEE one (a reciprocal product where it
+//    provably rounds the same, __fdiv_rn elsewhere; never fast-math), round-half-even, clamp +-127.
 //  * quantize_q8_0: fp32 -> native block_q8_0 (examples/benchmark_llama_cpp_qpu_persistent_q4.py:42-54).
 //  * quantize_q4_0: fp32 -> native block_q4_0, ggml's published quantize_row_q4_0_ref.
 //  * q4_0_repack: native 18-byte Q4_0 blocks -> the prepared layout (16-byte nibble blocks + fp16 scales).
 #include <cuda_fp16.h>
 
 #include "qpucuda_internal.h"
+#include "sm100_sync.cuh"
 
 namespace qpucuda {
 namespace {
@@ -19,6 +22,18 @@ __device__ __forceinline__ float scale_floor() { return __uint_as_float(0x3c0102
 
 __device__ __forceinline__ int quantize_value(float x, float scale) {
     const int v = __float2int_rn(__fdiv_rn(x, scale));
+    return v < -127 ? -127 : (v > 127 ? 127 : v);
+}
+
+// Same result as quantize_value without a division per element: p = x * RN(1/scale) is within
+// 3 * 2^-24 * |x/scale| < 2.3e-5 of RN(x/scale) (|x/scale| < 128, as |x| <= amax and
+// scale >= RN(amax/127)). So when p lies farther than 2^-15 from every half-integer, RN(x/scale)
+// sits strictly on the same side of it and rounds to the same integer; otherwise (about 6e-5 of
+// the elements) the exact IEEE division decides. NaN and infinite inputs give 0 on both paths.
+__device__ __forceinline__ int quantize_value_fast(float x, float scale, float inverse) {
+    const float p = __fmul_rn(x, inverse);
+    if (fabsf(p - rintf(p)) > 0.5f - 3.0517578125e-05f) return quantize_value(x, scale);
+    const int v = __float2int_rn(p);
     return v < -127 ? -127 : (v > 127 ? 127 : v);
 }
 
@@ -77,18 +92,96 @@ __global__ void __launch_bounds__(THREADS) quantize_rows_int8_vec(const float *_
         }
         amax = block_max<THREADS>(amax, scratch);
         const float scale = fmaxf(__fdiv_rn(amax, 127.0f), scale_floor());
+        const float inverse = __frcp_rn(scale);
         uint32_t *destination = reinterpret_cast<uint32_t *>(q + static_cast<size_t>(row) * q_stride);
 #pragma unroll
         for (int v = 0; v < VEC; ++v) {
             const uint32_t index = threadIdx.x + v * THREADS;
             if (index < vectors) {
-                destination[index] = pack4(quantize_value(cache[v].x, scale), quantize_value(cache[v].y, scale),
-                                           quantize_value(cache[v].z, scale), quantize_value(cache[v].w, scale));
+                destination[index] = pack4(
+                    quantize_value_fast(cache[v].x, scale, inverse), quantize_value_fast(cache[v].y, scale, inverse),
+                    quantize_value_fast(cache[v].z, scale, inverse), quantize_value_fast(cache[v].w, scale, inverse));
             }
         }
         int8_t *row_q = q + static_cast<size_t>(row) * q_stride;
         for (uint32_t c = cols + threadIdx.x; c < padded_cols; c += THREADS) row_q[c] = 0;
         if (threadIdx.x == 0) scales[row] = scale;
+    }
+}
+
+// Staged path for many long rows: a persistent CTA walks rows blockIdx.x, + gridDim.x, ... with
+// STAGES row buffers in shared memory, each filled by one 1D bulk copy (TMA engine, completing on
+// the stage's mbarrier) issued by thread 0 as soon as the CTA has finished the row that held it.
+// Up to STAGES rows per CTA are in flight while the CTA reduces and quantizes the current one,
+// so the SM keeps streaming instead of alternating load and compute phases. Waits are bounded
+// (error word + abort); an aborting CTA drains its own outstanding copies before it exits.
+template <int THREADS, int STAGES>
+__global__ void __launch_bounds__(THREADS) quantize_rows_int8_bulk(const float *__restrict__ x, size_t x_stride,
+                                                                   uint32_t rows, uint32_t cols, uint32_t padded_cols,
+                                                                   int8_t *__restrict__ q, size_t q_stride,
+                                                                   float *__restrict__ scales,
+                                                                   unsigned int *error_word) {
+    extern __shared__ __align__(128) float4 staged[];  // [STAGES][cols / 4]
+    __shared__ __align__(8) uint64_t full[STAGES];
+    __shared__ float scratch[32];
+    __shared__ int abort_flag;
+    const uint32_t vectors = cols / 4;
+    const uint32_t row_bytes = cols * 4u;
+    const uint32_t step = gridDim.x;
+    auto refill = [&](uint32_t row, uint32_t stage) {
+        const uint32_t bar = sm100::smem_u32(&full[stage]);
+        sm100::mbar_expect_tx(bar, row_bytes);
+        sm100::bulk_load(sm100::smem_u32(staged + static_cast<size_t>(stage) * vectors),
+                         x + static_cast<size_t>(row) * x_stride, row_bytes, bar);
+    };
+    if (threadIdx.x == 0) {
+        abort_flag = 0;
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s) sm100::mbar_init(sm100::smem_u32(&full[s]), 1);
+        sm100::mbar_init_fence();
+#pragma unroll
+        for (int s = 0; s < STAGES; ++s) {
+            const uint32_t row = blockIdx.x + s * step;
+            if (row < rows) refill(row, s);
+        }
+    }
+    __syncthreads();
+    uint32_t iteration = 0;
+    for (uint32_t row = blockIdx.x; row < rows; row += step, ++iteration) {
+        const uint32_t stage = iteration % STAGES;
+        const uint32_t parity = (iteration / STAGES) & 1u;
+        const bool landed = sm100::wait_bounded(sm100::smem_u32(&full[stage]), parity, &abort_flag, error_word);
+        if (!__syncthreads_and(landed)) {
+            if (threadIdx.x == 0) {  // let this CTA's copies in flight land before it exits
+                for (uint32_t k = 0; k < STAGES; ++k) {
+                    if (row + k * step < rows) {
+                        sm100::wait_drain(sm100::smem_u32(&full[(iteration + k) % STAGES]),
+                                          ((iteration + k) / STAGES) & 1u);
+                    }
+                }
+            }
+            return;
+        }
+        const float4 *slots = staged + static_cast<size_t>(stage) * vectors;
+        float amax = 0.0f;
+        for (uint32_t i = threadIdx.x; i < vectors; i += THREADS) {
+            const float4 v = slots[i];
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+        amax = block_max<THREADS>(amax, scratch);
+        const float scale = fmaxf(__fdiv_rn(amax, 127.0f), scale_floor());
+        const float inverse = __frcp_rn(scale);
+        int8_t *row_q = q + static_cast<size_t>(row) * q_stride;
+        uint32_t *destination = reinterpret_cast<uint32_t *>(row_q);
+        for (uint32_t i = threadIdx.x; i < vectors; i += THREADS) {
+            const float4 v = slots[i];
+            destination[i] = pack4(quantize_value_fast(v.x, scale, inverse), quantize_value_fast(v.y, scale, inverse),
+                                   quantize_value_fast(v.z, scale, inverse), quantize_value_fast(v.w, scale, inverse));
+        }
+        for (uint32_t c = cols + threadIdx.x; c < padded_cols; c += THREADS) row_q[c] = 0;
+        if (threadIdx.x == 0) scales[row] = scale;
+        __syncthreads();  // every thread is done with this stage
+        if (threadIdx.x == 0 && row + STAGES * step < rows) refill(row + STAGES * step, stage);
     }
 }
 
@@ -238,14 +331,63 @@ uint32_t grid_for(size_t work_items, uint32_t per_block) {
 
 }  // namespace
 
+namespace {
+
+// Usable dynamic shared memory per CTA on sm_100 (227 KB) less the static scratch and mbarriers.
+constexpr size_t kStagedSmemBudget = 227u * 1024u - 512u;
+
+template <int THREADS, int STAGES>
+cudaError_t launch_staged_config(const float *x, size_t x_stride, uint32_t rows, uint32_t cols, uint32_t padded_cols,
+                                 int8_t *q, size_t q_stride, float *scales, unsigned int *error_word, int sm_count,
+                                 cudaStream_t stream) {
+    const size_t smem = static_cast<size_t>(STAGES) * cols * sizeof(float);
+    auto kernel = quantize_rows_int8_bulk<THREADS, STAGES>;
+    cudaError_t error = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    int per_sm = 0;
+    if (error == cudaSuccess) error = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, THREADS, smem);
+    if (error != cudaSuccess) return error;
+    if (per_sm < 1) return cudaErrorNotSupported;
+    const uint64_t slots = static_cast<uint64_t>(sm_count) * static_cast<uint64_t>(per_sm);
+    const uint32_t grid = rows < slots ? rows : static_cast<uint32_t>(slots);
+    kernel<<<grid, THREADS, smem, stream>>>(x, x_stride, rows, cols, padded_cols, q, q_stride, scales, error_word);
+    return cudaGetLastError();
+}
+
+// Picks the bulk-staged kernel (1024 threads, two row stages) for aligned rows too long for the
+// register-cached kernel to keep more than one row per SM (row > 1/4 of the shared memory budget,
+// K > ~14.5K), with at least two rows per SM; returns cudaErrorNotSupported otherwise. Measured
+// on B200 at M = 4096: K = 28672 takes 113 us (0.79 of HBM) against 136 us register-cached;
+// at K <= 8192 the two kernels are within 3% and more stages (fewer CTAs per SM) were slower.
+cudaError_t launch_staged(const float *x, size_t x_stride, uint32_t rows, uint32_t cols, uint32_t padded_cols,
+                          int8_t *q, size_t q_stride, float *scales, unsigned int *error_word, cudaStream_t stream) {
+    int device = 0, sm_count = 0;
+    if (error_word == nullptr || cudaGetDevice(&device) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || sm_count <= 0) {
+        (void)cudaGetLastError();
+        return cudaErrorNotSupported;
+    }
+    const size_t row_bytes = static_cast<size_t>(cols) * sizeof(float);
+    if (rows < 2u * static_cast<uint32_t>(sm_count) || 4 * row_bytes <= kStagedSmemBudget ||
+        2 * row_bytes > kStagedSmemBudget) {
+        return cudaErrorNotSupported;
+    }
+    return launch_staged_config<1024, 2>(x, x_stride, rows, cols, padded_cols, q, q_stride, scales, error_word,
+                                        sm_count, stream);
+}
+
+}  // namespace
+
 cudaError_t launch_quantize_rows_int8(const float *x, size_t x_stride, uint32_t rows, uint32_t cols,
                                       uint32_t padded_cols, int8_t *q, size_t q_stride, float *scales,
-                                      cudaStream_t stream) {
+                                      unsigned int *error_word, cudaStream_t stream) {
     if (rows == 0) return cudaSuccess;
     const bool vector_ok = cols % 4 == 0 && x_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
                            q_stride % 4 == 0 && (reinterpret_cast<uintptr_t>(q) & 3u) == 0;
     const uint32_t vectors = cols / 4;
     if (vector_ok) {
+        const cudaError_t staged =
+            launch_staged(x, x_stride, rows, cols, padded_cols, q, q_stride, scales, error_word, stream);
+        if (staged != cudaErrorNotSupported) return staged;
         // VEC = 8 float4 per thread; pick the smallest warp multiple of threads that covers the row.
         if (vectors <= 32 * 8) return launch_vec<32, 8>(x, x_stride, rows, cols, padded_cols, q, q_stride, scales, stream);
         if (vectors <= 64 * 8) return launch_vec<64, 8>(x, x_stride, rows, cols, padded_cols, q, q_stride, scales, stream);
@@ -277,7 +419,7 @@ cudaError_t launch_quantize_rows_int8_layout(const float *x, uint32_t rows, uint
         batch_stride = 0;
     }
     if (col_stride == 1 && rows_per_batch == rows) {
-        return launch_quantize_rows_int8(x, row_stride, rows, cols, padded_cols, q, q_stride, scales, stream);
+        return launch_quantize_rows_int8(x, row_stride, rows, cols, padded_cols, q, q_stride, scales, nullptr, stream);
     }
     if (padded_cols % 4 != 0 || q_stride % 4 != 0 || (reinterpret_cast<uintptr_t>(q) & 3u) != 0) return cudaErrorInvalidValue;
     quantize_rows_int8_layout_kernel<<<(rows + 255) / 256, 256, 0, stream>>>(

@@ -37,7 +37,12 @@ def sha256(array: np.ndarray) -> str:
 
 @pytest.mark.parametrize(
     "rows,cols,padded",
-    [(64, 64, 64), (512, 512, 512), (17, 20, 32), (1, 2048, 2048), (2048, 5632, 5632), (3, 28672, 28672), (2, 40000, 40000), (5, 33, 48)],
+    [
+        (64, 64, 64), (512, 512, 512), (17, 20, 32), (1, 2048, 2048), (2048, 5632, 5632), (3, 28672, 28672),
+        (2, 40000, 40000), (5, 33, 48),
+        # many rows: register-cached kernel up to ~14.5K columns, bulk-staged kernel above
+        (297, 1024, 1040), (300, 16384, 16384), (600, 28672, 28688), (4096, 8192, 8192), (296, 14592, 14592),
+    ],
 )
 def test_row_quantizer_is_bit_exact(native, rows: int, cols: int, padded: int) -> None:  # type: ignore[no-untyped-def]
     import torch
@@ -49,6 +54,28 @@ def test_row_quantizer_is_bit_exact(native, rows: int, cols: int, padded: int) -
         x[1] = 0.0  # all-zero row -> the 1/127 floor
     q, scales = native.quantize_rows(torch.from_numpy(x).cuda(), padded)
     expected_q, expected_scales = oracle.quantize_rows_int8(x)
+    np.testing.assert_array_equal(scales.cpu().numpy(), expected_scales)
+    q_host = q.cpu().numpy()
+    np.testing.assert_array_equal(q_host[:, :cols], expected_q)
+    assert np.all(q_host[:, cols:] == 0)
+
+
+def test_bulk_row_quantizer_on_strided_rows_of_mixed_scale(native) -> None:  # type: ignore[no-untyped-def]
+    """Bulk-staged kernel over a 16-byte aligned strided view, with rows that hit the clamp, the
+    scale floor, exact halves and a negative maximum."""
+    import torch
+
+    rng = np.random.default_rng(17)
+    rows, cols, stride = 400, 16384, 16388
+    full = rng.standard_normal((rows, stride), dtype=np.float32)
+    full *= rng.uniform(1e-4, 1e4, (rows, 1)).astype(np.float32)
+    full[2, :cols] = 0.0
+    full[3, :cols] = -5.0
+    full[4, :cols] = np.arange(cols, dtype=np.float32) * np.float32(0.5) - np.float32(300.0)
+    full[5, :cols] = np.float32(127.0) * (np.arange(cols, dtype=np.float32) % np.float32(255.0) - np.float32(127.0)) / np.float32(254.0)
+    view = torch.from_numpy(full).cuda()[:, :cols]
+    q, scales = native.quantize_rows(view, cols + 16)
+    expected_q, expected_scales = oracle.quantize_rows_int8(np.ascontiguousarray(full[:, :cols]))
     np.testing.assert_array_equal(scales.cpu().numpy(), expected_scales)
     q_host = q.cpu().numpy()
     np.testing.assert_array_equal(q_host[:, :cols], expected_q)

@@ -294,6 +294,40 @@ def run_ours(args: argparse.Namespace) -> None:
     total_ops = sum(2.0 * TOKENS * p["n"] * p["k"] for p in projections)  # whole job, all ranks
     value_tops = total_ops / (step_ms * 1e-3) / 1e12
 
+    # ---- N > 1: the same step without the exchange (quantize + GEMM on the rank's shard) ----
+    multi_gpu = None
+    if world > 1:
+
+        def local_step() -> None:
+            for p in projections:
+                p["plan"].forward(p["source"], out=p["local"][:, : p["gather"].count])
+
+        for _ in range(args.warmup):
+            prime()
+            local_step()
+        barrier()
+        local_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        local_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        for i in range(args.steps):
+            prime()
+            local_starts[i].record(stream)
+            local_step()
+            local_ends[i].record(stream)
+        barrier()
+        local_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(local_starts, local_ends)) / args.steps)
+        # fp32 output columns every rank receives from the others per step
+        received = sum(TOKENS * (p["n"] - p["gather"].count) * 4 for p in projections)
+        multi_gpu = {
+            "kernel_ms_per_step": round(local_ms, 4),
+            "exchange_ms_per_step": round(step_ms - local_ms, 4),
+            "end_to_end_ms_per_step": round(step_ms, 4),
+            "exchange": exchange,
+            "received_bytes_per_rank_step": received,
+            "received_gbs_per_rank": round(received / (step_ms * 1e-3) / 1e9, 1),
+            "note": "kernel = quantize + GEMM on the rank's column shard alone; exchange = the step's extra time "
+            "over that (the fused epilogue overlaps the peer stores with the GEMM, so this is the exposed part)",
+        }
+
     # ---- dominant kernel: the tcgen05 GEMM alone (activations already quantized) ----
     gemm_ms = []
     for p in projections:
@@ -464,6 +498,8 @@ def run_ours(args: argparse.Namespace) -> None:
         },
         "clocks": clocks,
     }
+    if multi_gpu is not None:
+        line["multi_gpu"] = multi_gpu
     if e2e is not None:
         line["e2e"] = e2e
     if cpu_baseline is not None:

@@ -293,7 +293,7 @@ qpucuda_status qpucuda_w8a8_linear_prepare(qpucuda_context *context, const qpucu
     if (context->cc_major == 10 && context->cc_minor == 0) {
         linear->maps_ready =
             encode_tensor_map_2d_u8(&linear->map_weight, linear->d_weight, linear->k_pad, count, linear->k_pad,
-                                    kGemmBlockK, kGemmBlockN) &&
+                                    kGemmBlockK, kGemmWeightBoxRows) &&
             encode_tensor_map_2d_u8(&linear->map_quantized, linear->d_quantized, linear->k_pad, desc->max_batch,
                                     linear->k_pad, kGemmBlockK, kGemmBlockM);
     }

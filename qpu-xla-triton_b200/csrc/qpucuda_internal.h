@@ -125,10 +125,16 @@ struct GemmEpilogue {
     size_t col_stride = 1;
 };
 
-// tcgen05 int8 GEMM: a [m][k] and w [n][k] int8, K-major, 16-byte aligned rows.
+// tcgen05 int8 GEMM: a [m][k] and w [n][k] int8, K-major, 16-byte aligned rows. Tensor maps: A
+// boxes of kGemmBlockK x kGemmBlockM, W boxes of kGemmBlockK x kGemmWeightBoxRows, 128-byte swizzle.
+// Picks CTA pairs (tcgen05 cta_group::2, 256 x 256 tiles) when m spans two row blocks.
 cudaError_t launch_w8a8_gemm_sm100(const CUtensorMap *map_a, const CUtensorMap *map_w, uint32_t m, uint32_t n,
                                    uint32_t k, const GemmEpilogue &epilogue, unsigned int *error_word,
                                    int sm_count, cudaStream_t stream);
+// The same with the tile mode chosen by the caller (pair = CTA pairs).
+cudaError_t launch_w8a8_gemm_sm100_mode(const CUtensorMap *map_a, const CUtensorMap *map_w, uint32_t m, uint32_t n,
+                                        uint32_t k, const GemmEpilogue &epilogue, unsigned int *error_word,
+                                        int sm_count, bool pair, cudaStream_t stream);
 // Builds both tensor maps and launches; returns cudaErrorInvalidValue when a map cannot be encoded.
 cudaError_t run_w8a8_gemm(const int8_t *a, size_t a_stride, const int8_t *w, size_t w_stride, uint32_t m,
                           uint32_t n, uint32_t k, const GemmEpilogue &epilogue, unsigned int *error_word,
@@ -136,6 +142,7 @@ cudaError_t run_w8a8_gemm(const int8_t *a, size_t a_stride, const int8_t *w, siz
 constexpr uint32_t kGemmBlockN = 256;  // box rows of the weight tensor map
 constexpr uint32_t kGemmBlockM = 128;
 constexpr uint32_t kGemmBlockK = 128;  // bytes of K per pipeline stage
+constexpr uint32_t kGemmWeightBoxRows = 128;  // W rows per TMA box (a 256-row tile is two boxes)
 
 cudaError_t launch_w8a8_gemv(const int8_t *a, size_t a_stride, const int8_t *w, size_t w_stride, uint32_t m,
                              uint32_t n, uint32_t k, const GemmEpilogue &epilogue, int sm_count,

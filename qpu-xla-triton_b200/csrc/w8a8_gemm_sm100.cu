@@ -13,8 +13,8 @@
 //
 // Structure: one persistent CTA per SM (192 threads, ~197 KB of shared memory,
 // so exactly one CTA per SM and its 512 TMEM columns are always free).
-//   warp 0      TMA producer: A tile 128 x 128 B and W tile 256 x 128 B per stage,
-//               4-stage ring, 128-byte swizzle, mbarrier complete_tx.
+//   warp 0      TMA producer: A tile 128 x 128 B and W tile 256 x 128 B (two 128-row boxes)
+//               per stage, 4-stage ring, 128-byte swizzle, mbarrier complete_tx.
 //   warp 1      TMEM allocator and MMA issuer: 4 x tcgen05.mma (M=128, N=256, K=32)
 //               per stage; tcgen05.commit releases the stage and, after the last
 //               K block, signals the accumulator buffer full.
@@ -23,36 +23,58 @@
 //               of tile i overlap the main loop of tile i+1.
 // Every mbarrier wait is bounded (globaltimer); on expiry the kernel records
 // kKernelWaitTimeout in the error word, drains its own copies and MMAs with
-// bounded waits, frees TMEM and returns. No multicast is used anywhere.
+// bounded waits, frees TMEM and returns. No multicast load is used anywhere.
+//
+// CTA-pair mode (PAIR, clusters of 2, tcgen05 cta_group::2): a 256 x 256 tile per pair; each CTA
+// stages its 128 rows of A and 128 of the 256 W rows (32 KB per stage, 6 stages) with TMA loads
+// whose bytes complete on the leader (rank 0) CTA's barrier; the leader issues M = 256 MMAs that
+// read both CTAs' shared memory and write each CTA's 128 accumulator rows into its own tensor
+// memory; its commits arrive on the stage and accumulator barriers of both CTAs; each CTA's
+// epilogue drains its own rows and releases the buffer on the leader's barrier. The protocol
+// (who arms which barrier, the same warp allocating tensor memory in both CTAs) follows
+// CUTLASS's sm100 2-SM GEMM pipeline.
 #include "qpucuda_internal.h"
 #include "sm100_sync.cuh"
 
 namespace qpucuda {
 namespace {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
+constexpr int BM = 128;  // rows of A per CTA
+constexpr int BN = 256;  // output columns per tile
 constexpr int BK = 128;  // bytes (int8 elements) of K per stage = one 128-byte swizzle row
-constexpr int STAGES = 4;
 constexpr int UMMA_K = 32;  // K per tcgen05.mma kind::i8
-constexpr int A_STAGE_BYTES = BM * BK;
-constexpr int B_STAGE_BYTES = BN * BK;
-constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int TMEM_COLS = 2 * BN;  // two s32 accumulators of BN columns
 constexpr int NUM_THREADS = 192;
 constexpr int EPILOGUE_THREADS = 128;
+constexpr int W_BOX_ROWS = 128;  // rows of W per TMA box (a 256-row B tile is two boxes)
 
-static_assert(BN == kGemmBlockN && BM == kGemmBlockM && BK == kGemmBlockK, "tile constants must agree");
+// Pipeline shape per mode. Single-CTA: A 128 x 128 B + B 256 x 128 B = 48 KB per stage, 4 stages.
+// CTA pair (tcgen05 cta_group::2, M = 256 across two SMs): each CTA stages its own 128 rows of A
+// and its half (128 rows) of B, 32 KB per stage, 6 stages in the same shared memory.
+template <bool PAIR>
+struct Pipe {
+    static constexpr int STAGES = PAIR ? 6 : 4;
+    static constexpr int A_BYTES = BM * BK;
+    static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+};
+
+static_assert(BN == kGemmBlockN && BM == kGemmBlockM && BK == kGemmBlockK && W_BOX_ROWS == kGemmWeightBoxRows,
+              "tile constants must agree");
 
 // Instruction descriptor (kind::i8): D = s32 (bits 4-5 = 2), A = s8 (bits 7-9 = 1),
 // B = s8 (bits 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at bits 17-22,
 // M >> 4 at bits 24-28.
 constexpr uint32_t kInstrDesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
                                 (static_cast<uint32_t>(BM >> 4) << 24);
+// The same for the CTA pair: M = 256 (each CTA's tensor memory receives its 128 rows).
+constexpr uint32_t kInstrDescPair = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+                                    (static_cast<uint32_t>((2 * BM) >> 4) << 24);
 
+template <int NSTAGES>
 struct Control {
-    uint64_t full[STAGES];
-    uint64_t empty[STAGES];
+    uint64_t full[NSTAGES];
+    uint64_t empty[NSTAGES];
     uint64_t tmem_full[2];
     uint64_t tmem_empty[2];
     uint64_t drain;
@@ -64,8 +86,10 @@ struct Control {
 // of shared memory so that global stores leave as full 128-byte row segments.
 // Only the fan-out variant (peer destinations) has it.
 constexpr int EPILOGUE_STAGE_BYTES = (EPILOGUE_THREADS / 32) * 32 * 32 * 4;
+template <bool PAIR>
 constexpr size_t smem_bytes(bool fanout) {
-    return static_cast<size_t>(STAGES) * STAGE_BYTES + (fanout ? EPILOGUE_STAGE_BYTES : 0) + 1024 + sizeof(Control);
+    return static_cast<size_t>(Pipe<PAIR>::STAGES) * Pipe<PAIR>::STAGE_BYTES + (fanout ? EPILOGUE_STAGE_BYTES : 0) +
+           1024 + sizeof(Control<Pipe<PAIR>::STAGES>);
 }
 
 struct GemmParams {
@@ -93,9 +117,40 @@ struct GemmParams {
 using namespace sm100;
 
 // Bounded wait on this CTA's abort flag (see sm100_sync.cuh).
-__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, Control *control,
+template <int NSTAGES>
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, Control<NSTAGES> *control,
                                              unsigned int *error_word) {
     return sm100::wait_bounded(bar, parity, &control->abort_flag, error_word);
+}
+
+// ---- CTA-pair (cluster of 2) primitives, in the forms CUTLASS's sm100 2-SM GEMM uses ----
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t rank;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank));
+    return rank;
+}
+// Address of the same shared variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t address, uint32_t rank) {
+    uint32_t mapped;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(mapped) : "r"(address), "r"(rank));
+    return mapped;
+}
+__device__ __forceinline__ void remote_arrive(uint32_t cluster_address) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_address) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+}
+// 2D tiled TMA load into this CTA's shared memory whose bytes complete on the leader CTA's
+// mbarrier (cta_group::2 form; no multicast).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t destination, const CUtensorMap *map, uint32_t leader_bar,
+                                                 int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];" ::"r"(destination),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y)
+        : "memory");
 }
 
 // Shared-memory matrix descriptor, K-major operand in the 128-byte swizzle
@@ -123,6 +178,27 @@ __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64
 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// CTA pair: one MMA over both CTAs' operands (same shared-memory offsets in each), writing each
+// CTA's 128 rows into its own tensor memory.
+__device__ __forceinline__ void umma_i8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(kInstrDescPair), "r"(accumulate)
+        : "memory");
+}
+// Completion of the pair's MMAs signalled on the barrier at `bar`'s offset in both CTAs.
+__device__ __forceinline__ void umma_commit_pair_both(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+                 ::"r"(bar), "h"(static_cast<uint16_t>(3))
+                 : "memory");
+}
+// ... on this CTA's barrier only (abort drain).
+__device__ __forceinline__ void umma_commit_pair_local(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -160,10 +236,19 @@ __device__ __forceinline__ void store_group(void *base, size_t offset, uint4 val
 }
 
 // FANOUT: the epilogue also writes every peer destination (fused GEMM + all-gather).
-template <bool FANOUT>
+// PAIR: launched as clusters of two CTAs that share each 256-row tile (tcgen05 cta_group::2):
+// CTA rank r loads rows r*128.. of the tile's A rows and of its 256 W rows; the rank-0 (leader)
+// CTA issues the MMAs for both and each CTA's epilogue drains its own 128 rows. Tiles are then
+// 256 x 256 per pair and params.m_blocks counts 256-row blocks.
+template <bool FANOUT, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     w8a8_gemm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                            const GemmParams params) {
+    constexpr int STAGES = Pipe<PAIR>::STAGES;
+    constexpr int A_STAGE_BYTES = Pipe<PAIR>::A_BYTES;
+    constexpr int B_STAGE_BYTES = Pipe<PAIR>::B_BYTES;
+    constexpr int STAGE_BYTES = Pipe<PAIR>::STAGE_BYTES;
+    using Control = qpucuda::Control<STAGES>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *stage_a = smem;
@@ -174,6 +259,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t num_tiles = params.m_blocks * params.n_blocks;
+    const uint32_t rank = PAIR ? cluster_rank() : 0u;  // this CTA's half of the pair
+    const bool leader = rank == 0;
+    const uint32_t first_tile = PAIR ? blockIdx.x / 2 : blockIdx.x;
+    const uint32_t tile_step = PAIR ? gridDim.x / 2 : gridDim.x;
+    constexpr uint32_t kTileRows = PAIR ? 2 * BM : BM;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -182,21 +272,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(smem_u32(&control->tmem_full[i]), 1);
-            mbar_init(smem_u32(&control->tmem_empty[i]), EPILOGUE_THREADS / 32);
+            // the leader's MMA waits for the epilogue warps of both CTAs
+            mbar_init(smem_u32(&control->tmem_empty[i]), (PAIR ? 2 : 1) * EPILOGUE_THREADS / 32);
         }
         mbar_init(smem_u32(&control->drain), 1);
         control->abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                         smem_u32(&control->tmem_base)),
-                     "r"(TMEM_COLS)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        // CTA pair: the same warp of both CTAs allocates collectively, into the same offset.
+        if constexpr (PAIR) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(&control->tmem_base)),
+                         "r"(TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(&control->tmem_base)),
+                         "r"(TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any remote arrive or copy
     tc_fence_after();
     const uint32_t tmem_base = control->tmem_base;
 
@@ -210,8 +311,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             bool issued[STAGES];
             for (int s = 0; s < STAGES; ++s) issued[s] = false;
             bool ok = true;
-            for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-                const int m0 = static_cast<int>((tile % params.m_blocks) * BM);
+            for (uint32_t tile = first_tile; ok && tile < num_tiles; tile += tile_step) {
+                const int m0 = static_cast<int>((tile % params.m_blocks) * kTileRows + rank * BM);
                 const int n0 = static_cast<int>((tile / params.m_blocks) * BN);
                 for (uint32_t kb = 0; kb < params.num_kb; ++kb) {
                     if (!wait_bounded(smem_u32(&control->empty[stage]), phase ^ 1u, control, params.error_word)) {
@@ -219,9 +320,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         break;
                     }
                     const uint32_t full = smem_u32(&control->full[stage]);
-                    mbar_expect_tx(full, STAGE_BYTES);
-                    tma_load_2d(smem_u32(stage_a + stage * A_STAGE_BYTES), &map_a, full, static_cast<int>(kb * BK), m0);
-                    tma_load_2d(smem_u32(stage_b + stage * B_STAGE_BYTES), &map_w, full, static_cast<int>(kb * BK), n0);
+                    const int x = static_cast<int>(kb * BK);
+                    if constexpr (PAIR) {
+                        // Both CTAs' bytes complete on the leader's barrier, which expects them all.
+                        if (leader) mbar_expect_tx(full, 2 * STAGE_BYTES);
+                        const uint32_t leader_full = map_to_rank(full, 0);
+                        tma_load_2d_pair(smem_u32(stage_a + stage * A_STAGE_BYTES), &map_a, leader_full, x, m0);
+                        tma_load_2d_pair(smem_u32(stage_b + stage * B_STAGE_BYTES), &map_w, leader_full, x,
+                                         n0 + static_cast<int>(rank) * W_BOX_ROWS);
+                    } else {
+                        mbar_expect_tx(full, STAGE_BYTES);
+                        tma_load_2d(smem_u32(stage_a + stage * A_STAGE_BYTES), &map_a, full, x, m0);
+                        tma_load_2d(smem_u32(stage_b + stage * B_STAGE_BYTES), &map_w, full, x, n0);
+                        tma_load_2d(smem_u32(stage_b + stage * B_STAGE_BYTES + W_BOX_ROWS * BK), &map_w, full, x,
+                                    n0 + W_BOX_ROWS);
+                    }
                     issued[stage] = true;
                     issued_phase[stage] = phase;
                     if (++stage == STAGES) {
@@ -231,18 +344,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
             if (!ok) {
-                // Abort path: let every copy this thread started land before the CTA exits.
-                for (int s = 0; s < STAGES; ++s) {
-                    if (issued[s]) wait_drain(smem_u32(&control->full[s]), issued_phase[s]);
+                // Abort path: let every copy this thread started land before the CTA exits. In a
+                // pair only the leader's barriers see the copies (of both CTAs); the other CTA
+                // gives its copies in flight a bounded 200 us instead.
+                if (!PAIR || leader) {
+                    for (int s = 0; s < STAGES; ++s) {
+                        if (issued[s]) wait_drain(smem_u32(&control->full[s]), issued_phase[s]);
+                    }
+                } else {
+                    const uint64_t start = globaltimer();
+                    while (globaltimer() - start < 200000ull) {
+                    }
                 }
             }
         }
         __syncwarp();  // reconverge before the CTA barrier at the end
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
+        // ---------------- MMA issuer (the leader CTA only, in a pair) ----------------
         uint32_t stage = 0, phase = 0, local_tile = 0;
-        bool ok = true, any_mma = false;
-        for (uint32_t tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++local_tile) {
+        bool ok = !PAIR || leader, any_mma = false;
+        for (uint32_t tile = first_tile; ok && tile < num_tiles; tile += tile_step, ++local_tile) {
             const uint32_t acc = local_tile & 1u;
             const uint32_t acc_phase = (local_tile >> 1) & 1u;
             if (lane == 0) ok = wait_bounded(smem_u32(&control->tmem_empty[acc]), acc_phase ^ 1u, control, params.error_word);
@@ -261,10 +382,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                     for (int kk = 0; kk < BK / UMMA_K; ++kk) {
                         // Advance the start address by 32 bytes (encoded >> 4) within the swizzle row.
-                        umma_i8(d_tmem, a_desc + static_cast<uint64_t>(kk * (UMMA_K >> 4)),
-                                b_desc + static_cast<uint64_t>(kk * (UMMA_K >> 4)), (kb | kk) != 0 ? 1u : 0u);
+                        const uint64_t a = a_desc + static_cast<uint64_t>(kk * (UMMA_K >> 4));
+                        const uint64_t b = b_desc + static_cast<uint64_t>(kk * (UMMA_K >> 4));
+                        if constexpr (PAIR) {
+                            umma_i8_pair(d_tmem, a, b, (kb | kk) != 0 ? 1u : 0u);
+                        } else {
+                            umma_i8(d_tmem, a, b, (kb | kk) != 0 ? 1u : 0u);
+                        }
                     }
-                    umma_commit(smem_u32(&control->empty[stage]));
+                    // frees this stage in both CTAs of a pair
+                    if constexpr (PAIR) {
+                        umma_commit_pair_both(smem_u32(&control->empty[stage]));
+                    } else {
+                        umma_commit(smem_u32(&control->empty[stage]));
+                    }
                     any_mma = true;
                 }
                 __syncwarp();
@@ -274,12 +405,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
             if (!ok) break;
-            if (lane == 0) umma_commit(smem_u32(&control->tmem_full[acc]));
+            if (lane == 0) {
+                if constexpr (PAIR) {
+                    umma_commit_pair_both(smem_u32(&control->tmem_full[acc]));
+                } else {
+                    umma_commit(smem_u32(&control->tmem_full[acc]));
+                }
+            }
             __syncwarp();
         }
         if (!ok && lane == 0 && any_mma) {
             // Abort path: wait for every MMA this thread issued before TMEM is freed.
-            umma_commit(smem_u32(&control->drain));
+            if constexpr (PAIR) {
+                umma_commit_pair_local(smem_u32(&control->drain));
+            } else {
+                umma_commit(smem_u32(&control->drain));
+            }
             wait_drain(smem_u32(&control->drain), 0);
         }
         __syncwarp();
@@ -309,8 +450,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (uint32_t d = 0; d < kGemmMaxPeers; ++d)
                 if (d < peers) aligned = aligned && (reinterpret_cast<uintptr_t>(params.peer_out[d]) & 15u) == 0;
         }
+        // Release of an accumulator buffer goes to the MMA issuer's barrier (the leader's in a pair).
+        const uint32_t empty_bar0 = PAIR ? map_to_rank(smem_u32(&control->tmem_empty[0]), 0) : smem_u32(&control->tmem_empty[0]);
+        const uint32_t empty_bar1 = PAIR ? map_to_rank(smem_u32(&control->tmem_empty[1]), 0) : smem_u32(&control->tmem_empty[1]);
         uint32_t local_tile = 0;
-        for (uint32_t tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local_tile) {
+        for (uint32_t tile = first_tile; tile < num_tiles; tile += tile_step, ++local_tile) {
             const uint32_t acc = local_tile & 1u;
             const uint32_t acc_phase = (local_tile >> 1) & 1u;
             const uint32_t m_block = tile % params.m_blocks;
@@ -322,7 +466,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (!ok) break;
             tc_fence_after();
 
-            const uint32_t row0 = m_block * BM + quarter * 32;  // first row of this warp
+            const uint32_t row0 = m_block * kTileRows + rank * BM + quarter * 32;  // first row of this warp
             const uint32_t m = row0 + lane;
             const float row_scale = (m < params.m && !s32) ? params.row_scales[m] : 0.0f;
             const size_t row_base = batched ? static_cast<size_t>(m / params.rows_per_batch) * params.batch_stride +
@@ -447,7 +591,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&control->tmem_empty[acc]));
+            if (lane == 0) {
+                if constexpr (PAIR) {
+                    remote_arrive(acc == 0 ? empty_bar0 : empty_bar1);
+                } else {
+                    mbar_arrive(acc == 0 ? empty_bar0 : empty_bar1);
+                }
+            }
         }
         // Peer destinations: make this thread's remote stores visible system-wide before exit.
         if (FANOUT && params.peer_count != 0) __threadfence_system();
@@ -455,36 +605,120 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     tc_fence_before();
     __syncthreads();
+    // A pair finishes together: neither CTA exits (or frees tensor memory) while the other may
+    // still read its shared memory, signal its barriers or write its tensor memory.
+    if constexpr (PAIR) cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
-                     : "memory");
+        if constexpr (PAIR) {
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                         : "memory");
+        } else {
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                         : "memory");
+        }
     }
 }
 
 }  // namespace
 
+namespace {
+
+template <bool FANOUT, bool PAIR>
+cudaError_t configure_kernel() {
+    return cudaFuncSetAttribute(w8a8_gemm_sm100_kernel<FANOUT, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(smem_bytes<PAIR>(FANOUT)));
+}
+
+// Clusters of two that can be resident at once (one CTA per SM), cached per device.
+int resident_pairs(int sm_count) {
+    static int cached[64] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return sm_count / 2;
+    if (cached[device] > 0) return cached[device];
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3(static_cast<unsigned>(sm_count & ~1), 1, 1);
+    config.blockDim = dim3(NUM_THREADS, 1, 1);
+    config.dynamicSmemBytes = smem_bytes<true>(true);
+    cudaLaunchAttribute attribute;
+    attribute.id = cudaLaunchAttributeClusterDimension;
+    attribute.val.clusterDim.x = 2;
+    attribute.val.clusterDim.y = 1;
+    attribute.val.clusterDim.z = 1;
+    config.attrs = &attribute;
+    config.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, w8a8_gemm_sm100_kernel<true, true>, &config) != cudaSuccess ||
+        clusters <= 0) {
+        (void)cudaGetLastError();
+        return sm_count / 2;
+    }
+    cached[device] = clusters;
+    return clusters;
+}
+
+template <bool FANOUT, bool PAIR>
+cudaError_t launch_kernel(uint32_t tiles, int sm_count, const CUtensorMap *map_a, const CUtensorMap *map_w,
+                          const GemmParams &params, cudaStream_t stream) {
+    if constexpr (!PAIR) {
+        const uint32_t grid = tiles < static_cast<uint32_t>(sm_count) ? tiles : static_cast<uint32_t>(sm_count);
+        w8a8_gemm_sm100_kernel<FANOUT, false>
+            <<<grid, NUM_THREADS, smem_bytes<false>(FANOUT), stream>>>(*map_a, *map_w, params);
+        return cudaGetLastError();
+    } else {
+        const uint32_t pairs = static_cast<uint32_t>(resident_pairs(sm_count));
+        const uint32_t clusters = tiles < pairs ? tiles : pairs;
+        cudaLaunchConfig_t config = {};
+        config.gridDim = dim3(2 * clusters, 1, 1);
+        config.blockDim = dim3(NUM_THREADS, 1, 1);
+        config.dynamicSmemBytes = smem_bytes<true>(FANOUT);
+        config.stream = stream;
+        cudaLaunchAttribute attribute;
+        attribute.id = cudaLaunchAttributeClusterDimension;
+        attribute.val.clusterDim.x = 2;
+        attribute.val.clusterDim.y = 1;
+        attribute.val.clusterDim.z = 1;
+        config.attrs = &attribute;
+        config.numAttrs = 1;
+        return cudaLaunchKernelEx(&config, w8a8_gemm_sm100_kernel<FANOUT, true>, *map_a, *map_w, params);
+    }
+}
+
+}  // namespace
+
+// Single-CTA tiles (128 x 256) for one row block or when the epilogue also writes peers; CTA pairs
+// (256 x 256 per pair, a third less A and B traffic per output than the single-CTA tile) for
+// local outputs from two row blocks on. Measured on B200 (M = 4096): pairs take the 70B FFN gate
+// GEMM from 776 to 746 us and down from 689 to 658 us; with peer destinations (fused all-gather
+// at 2 GPUs) the single-CTA tiles exposed less of the exchange (0.06 against 0.14 ms per step).
 cudaError_t launch_w8a8_gemm_sm100(const CUtensorMap *map_a, const CUtensorMap *map_w, uint32_t m, uint32_t n,
                                    uint32_t k, const GemmEpilogue &epilogue, unsigned int *error_word, int sm_count,
                                    cudaStream_t stream) {
+    const bool pair = m > kGemmBlockM && epilogue.peer_count == 0;
+    return launch_w8a8_gemm_sm100_mode(map_a, map_w, m, n, k, epilogue, error_word, sm_count, pair, stream);
+}
+
+cudaError_t launch_w8a8_gemm_sm100_mode(const CUtensorMap *map_a, const CUtensorMap *map_w, uint32_t m, uint32_t n,
+                                        uint32_t k, const GemmEpilogue &epilogue, unsigned int *error_word,
+                                        int sm_count, bool pair, cudaStream_t stream) {
     if (m == 0 || n == 0) return cudaSuccess;
     if (k == 0) return cudaErrorInvalidValue;
     static bool configured = false;
     if (!configured) {
-        cudaError_t error = cudaFuncSetAttribute(w8a8_gemm_sm100_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 static_cast<int>(smem_bytes(false)));
-        if (error == cudaSuccess)
-            error = cudaFuncSetAttribute(w8a8_gemm_sm100_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem_bytes(true)));
+        cudaError_t error = configure_kernel<false, false>();
+        if (error == cudaSuccess) error = configure_kernel<true, false>();
+        if (error == cudaSuccess) error = configure_kernel<false, true>();
+        if (error == cudaSuccess) error = configure_kernel<true, true>();
         if (error != cudaSuccess) return error;
         configured = true;
     }
+    pair = pair && sm_count >= 2;
     GemmParams params;
     params.m = m;
     params.n = n;
     params.k = k;
     params.num_kb = (k + BK - 1) / BK;
-    params.m_blocks = (m + BM - 1) / BM;
+    params.m_blocks = (m + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM);
     params.n_blocks = (n + BN - 1) / BN;
     params.mode = static_cast<int>(epilogue.mode);
     params.row_scales = epilogue.row_scales;
@@ -501,13 +735,13 @@ cudaError_t launch_w8a8_gemm_sm100(const CUtensorMap *map_a, const CUtensorMap *
     params.col_stride = epilogue.col_stride;
     params.error_word = error_word;
     const uint32_t tiles = params.m_blocks * params.n_blocks;
-    const uint32_t grid = tiles < static_cast<uint32_t>(sm_count) ? tiles : static_cast<uint32_t>(sm_count);
-    if (params.peer_count != 0) {
-        w8a8_gemm_sm100_kernel<true><<<grid, NUM_THREADS, smem_bytes(true), stream>>>(*map_a, *map_w, params);
-    } else {
-        w8a8_gemm_sm100_kernel<false><<<grid, NUM_THREADS, smem_bytes(false), stream>>>(*map_a, *map_w, params);
+    const bool fanout = params.peer_count != 0;
+    if (pair) {
+        return fanout ? launch_kernel<true, true>(tiles, sm_count, map_a, map_w, params, stream)
+                      : launch_kernel<false, true>(tiles, sm_count, map_a, map_w, params, stream);
     }
-    return cudaGetLastError();
+    return fanout ? launch_kernel<true, false>(tiles, sm_count, map_a, map_w, params, stream)
+                  : launch_kernel<false, false>(tiles, sm_count, map_a, map_w, params, stream);
 }
 
 cudaError_t run_w8a8_gemm(const int8_t *a, size_t a_stride, const int8_t *w, size_t w_stride, uint32_t m, uint32_t n,
@@ -515,7 +749,7 @@ cudaError_t run_w8a8_gemm(const int8_t *a, size_t a_stride, const int8_t *w, siz
                           cudaStream_t stream) {
     CUtensorMap map_a, map_w;
     if (!encode_tensor_map_2d_u8(&map_a, a, k, m, a_stride, BK, BM) ||
-        !encode_tensor_map_2d_u8(&map_w, w, k, n, w_stride, BK, BN)) {
+        !encode_tensor_map_2d_u8(&map_w, w, k, n, w_stride, BK, W_BOX_ROWS)) {
         return cudaErrorInvalidValue;
     }
     return launch_w8a8_gemm_sm100(&map_a, &map_w, m, n, k, epilogue, error_word, sm_count, stream);

@@ -77,6 +77,9 @@ bool valid_range(size_t total, size_t offset, size_t size);
 // links only the static CUDA runtime, so it loads on machines without a driver).
 bool encode_tensor_map_2d_u8(CUtensorMap *map, const void *base, uint64_t inner_bytes, uint64_t rows,
                              uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows);
+// The same for 4-byte elements (fp32 / int32 outputs written by TMA stores), 128-byte swizzle.
+bool encode_tensor_map_2d_b32(CUtensorMap *map, const void *base, uint64_t columns, uint64_t rows,
+                              uint64_t row_stride_bytes, uint32_t box_columns, uint32_t box_rows);
 
 // ---- kernel launchers (one per .cu file) -------------------------------------------------
 

@@ -33,6 +33,8 @@
 // epilogue drains its own rows and releases the buffer on the leader's barrier. The protocol
 // (who arms which barrier, the same warp allocating tensor memory in both CTAs) follows
 // CUTLASS's sm100 2-SM GEMM pipeline.
+#include <cstring>
+
 #include "qpucuda_internal.h"
 #include "sm100_sync.cuh"
 
@@ -53,7 +55,7 @@ constexpr int W_BOX_ROWS = 128;  // rows of W per TMA box (a 256-row B tile is t
 // and its half (128 rows) of B, 32 KB per stage, 6 stages in the same shared memory.
 template <bool PAIR>
 struct Pipe {
-    static constexpr int STAGES = PAIR ? 6 : 4;
+    static constexpr int STAGES = PAIR ? 5 : 4;  // 4..7 stages measured within 1% in pair mode
     static constexpr int A_BYTES = BM * BK;
     static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -82,15 +84,17 @@ struct Control {
     volatile int abort_flag;
 };
 
-// Epilogue staging: each epilogue warp transposes its 32 rows x 32 columns chunk through 4 KB
-// of shared memory so that global stores leave as full 128-byte row segments.
-// Only the fan-out variant (peer destinations) has it.
-constexpr int EPILOGUE_STAGE_BYTES = (EPILOGUE_THREADS / 32) * 32 * 32 * 4;
+// Epilogue staging, 8 KB per epilogue warp: two 4 KB buffers of 32 rows x 128 bytes (128-byte
+// swizzle) that TMA stores copy to the output, or, with peer destinations, the 4 KB transpose
+// buffer that turns each lane's row values into 128-byte row segments for plain stores.
+constexpr int EPILOGUE_WARP_BYTES = 8192;
+constexpr int EPILOGUE_STAGE_BYTES = (EPILOGUE_THREADS / 32) * EPILOGUE_WARP_BYTES;
 template <bool PAIR>
-constexpr size_t smem_bytes(bool fanout) {
-    return static_cast<size_t>(Pipe<PAIR>::STAGES) * Pipe<PAIR>::STAGE_BYTES + (fanout ? EPILOGUE_STAGE_BYTES : 0) +
-           1024 + sizeof(Control<Pipe<PAIR>::STAGES>);
+constexpr size_t smem_bytes() {
+    return static_cast<size_t>(Pipe<PAIR>::STAGES) * Pipe<PAIR>::STAGE_BYTES + EPILOGUE_STAGE_BYTES + 1024 +
+           sizeof(Control<Pipe<PAIR>::STAGES>);
 }
+static_assert(smem_bytes<false>() <= 227 * 1024 && smem_bytes<true>() <= 227 * 1024, "shared memory budget");
 
 struct GemmParams {
     uint32_t m, n, k;
@@ -111,6 +115,8 @@ struct GemmParams {
     uint32_t rows_per_batch;
     size_t batch_stride;
     size_t col_stride;
+    // Local row-major output written by TMA stores through map_out (32 x 32 boxes).
+    uint32_t tma_store;
     unsigned int *error_word;
 };
 
@@ -217,6 +223,20 @@ __device__ __forceinline__ void tmem_load_32x32b_x32(uint32_t taddr, uint32_t (&
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// TMA store of a 32-row x 128-byte box from this CTA's shared memory (bulk async group).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, uint32_t source, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(source), "r"(x), "r"(y)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// All but the newest bulk group have finished reading their shared-memory source.
+__device__ __forceinline__ void bulk_wait_read_all_but_one() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Generic-proxy shared-memory writes made visible to the async proxy (TMA).
+__device__ __forceinline__ void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 __device__ __forceinline__ float dequant(uint32_t bits, float row_scale, float col_scale) {
     return __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(bits)), row_scale), col_scale);
 }
@@ -243,7 +263,7 @@ __device__ __forceinline__ void store_group(void *base, size_t offset, uint4 val
 template <bool FANOUT, bool PAIR>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     w8a8_gemm_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
-                           const GemmParams params) {
+                           const __grid_constant__ CUtensorMap map_out, const GemmParams params) {
     constexpr int STAGES = Pipe<PAIR>::STAGES;
     constexpr int A_STAGE_BYTES = Pipe<PAIR>::A_BYTES;
     constexpr int B_STAGE_BYTES = Pipe<PAIR>::B_BYTES;
@@ -254,7 +274,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t *stage_a = smem;
     uint8_t *stage_b = smem + STAGES * A_STAGE_BYTES;
     uint4 *epilogue_stage = reinterpret_cast<uint4 *>(smem + STAGES * STAGE_BYTES);
-    Control *control = reinterpret_cast<Control *>(smem + STAGES * STAGE_BYTES + (FANOUT ? EPILOGUE_STAGE_BYTES : 0));
+    Control *control = reinterpret_cast<Control *>(smem + STAGES * STAGE_BYTES + EPILOGUE_STAGE_BYTES);
 
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
@@ -434,7 +454,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         // so each store instruction writes four 128-byte row segments, to `out` and to every
         // peer (full-line writes over NVLink).
         const uint32_t quarter = warp & 3u;  // TMEM lanes this warp may access
-        uint4 *staging = epilogue_stage + (warp - 2u) * 256u;
+        uint4 *staging = epilogue_stage + (warp - 2u) * (EPILOGUE_WARP_BYTES / 16);
+        const bool tma_store = !FANOUT && params.tma_store != 0;
+        uint32_t stores_issued = 0;  // bulk groups this warp committed (selects the staging buffer)
+        if (tma_store && lane == 0) prefetch_tensor_map(&map_out);
         const bool s32 = params.mode == static_cast<int>(EpilogueMode::kStoreS32);
         const bool with_bias = params.mode == static_cast<int>(EpilogueMode::kDequantizeBias);
         // Row-segment stores need unit column stride; otherwise (NCHW outputs) each lane stores its
@@ -480,6 +503,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 const uint32_t n0 = n_base + chunk * 32;
                 if (n0 >= params.n) continue;  // warp-uniform
                 const bool full_chunk = n0 + 32 <= params.n;
+                if (tma_store) {
+                    // Rows past m and columns past n fall outside the tensor map and are not written.
+                    if (row0 >= params.m) continue;  // warp-uniform
+                    if (!s32) {
+#pragma unroll
+                        for (uint32_t j = 0; j < 32; ++j) {
+                            const bool in_range = full_chunk || n0 + j < params.n;
+                            float v = dequant(r[j], row_scale, in_range ? __ldg(params.col_scales + n0 + j) : 0.0f);
+                            if (with_bias) v = __fadd_rn(v, in_range ? __ldg(params.bias + n0 + j) : 0.0f);
+                            r[j] = __float_as_uint(v);
+                        }
+                    }
+                    uint4 *buffer = staging + (stores_issued & 1u) * 256u;
+                    if (lane == 0) bulk_wait_read_all_but_one();  // the store from this buffer has read it
+                    __syncwarp();
+#pragma unroll
+                    for (uint32_t c = 0; c < 8; ++c)
+                        buffer[lane * 8u + (c ^ (lane & 7u))] =
+                            make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+                    fence_proxy_async_shared();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&map_out, smem_u32(buffer), static_cast<int>(n0), static_cast<int>(row0));
+                        bulk_commit();
+                    }
+                    ++stores_issued;
+                    continue;
+                }
                 if (!FANOUT && row_segments) {
                     // Local row-major output: each lane converts and stores its own row's 32 values
                     // as eight 16-byte stores (measured faster than a shared-memory transpose when
@@ -599,6 +650,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
         }
+        // TMA stores: complete before the CTA exits.
+        if (tma_store && lane == 0) bulk_wait_all();
+        __syncwarp();
         // Peer destinations: make this thread's remote stores visible system-wide before exit.
         if (FANOUT && params.peer_count != 0) __threadfence_system();
     }
@@ -627,7 +681,7 @@ namespace {
 template <bool FANOUT, bool PAIR>
 cudaError_t configure_kernel() {
     return cudaFuncSetAttribute(w8a8_gemm_sm100_kernel<FANOUT, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(smem_bytes<PAIR>(FANOUT)));
+                                static_cast<int>(smem_bytes<PAIR>()));
 }
 
 // Clusters of two that can be resident at once (one CTA per SM), cached per device.
@@ -639,7 +693,7 @@ int resident_pairs(int sm_count) {
     cudaLaunchConfig_t config = {};
     config.gridDim = dim3(static_cast<unsigned>(sm_count & ~1), 1, 1);
     config.blockDim = dim3(NUM_THREADS, 1, 1);
-    config.dynamicSmemBytes = smem_bytes<true>(true);
+    config.dynamicSmemBytes = smem_bytes<true>();
     cudaLaunchAttribute attribute;
     attribute.id = cudaLaunchAttributeClusterDimension;
     attribute.val.clusterDim.x = 2;
@@ -659,11 +713,11 @@ int resident_pairs(int sm_count) {
 
 template <bool FANOUT, bool PAIR>
 cudaError_t launch_kernel(uint32_t tiles, int sm_count, const CUtensorMap *map_a, const CUtensorMap *map_w,
-                          const GemmParams &params, cudaStream_t stream) {
+                          const CUtensorMap *map_out, const GemmParams &params, cudaStream_t stream) {
     if constexpr (!PAIR) {
         const uint32_t grid = tiles < static_cast<uint32_t>(sm_count) ? tiles : static_cast<uint32_t>(sm_count);
         w8a8_gemm_sm100_kernel<FANOUT, false>
-            <<<grid, NUM_THREADS, smem_bytes<false>(FANOUT), stream>>>(*map_a, *map_w, params);
+            <<<grid, NUM_THREADS, smem_bytes<false>(), stream>>>(*map_a, *map_w, *map_out, params);
         return cudaGetLastError();
     } else {
         const uint32_t pairs = static_cast<uint32_t>(resident_pairs(sm_count));
@@ -671,7 +725,7 @@ cudaError_t launch_kernel(uint32_t tiles, int sm_count, const CUtensorMap *map_a
         cudaLaunchConfig_t config = {};
         config.gridDim = dim3(2 * clusters, 1, 1);
         config.blockDim = dim3(NUM_THREADS, 1, 1);
-        config.dynamicSmemBytes = smem_bytes<true>(FANOUT);
+        config.dynamicSmemBytes = smem_bytes<true>();
         config.stream = stream;
         cudaLaunchAttribute attribute;
         attribute.id = cudaLaunchAttributeClusterDimension;
@@ -680,7 +734,7 @@ cudaError_t launch_kernel(uint32_t tiles, int sm_count, const CUtensorMap *map_a
         attribute.val.clusterDim.z = 1;
         config.attrs = &attribute;
         config.numAttrs = 1;
-        return cudaLaunchKernelEx(&config, w8a8_gemm_sm100_kernel<FANOUT, true>, *map_a, *map_w, params);
+        return cudaLaunchKernelEx(&config, w8a8_gemm_sm100_kernel<FANOUT, true>, *map_a, *map_w, *map_out, params);
     }
 }
 
@@ -736,12 +790,19 @@ cudaError_t launch_w8a8_gemm_sm100_mode(const CUtensorMap *map_a, const CUtensor
     params.error_word = error_word;
     const uint32_t tiles = params.m_blocks * params.n_blocks;
     const bool fanout = params.peer_count != 0;
+    // A local row-major output leaves through TMA stores (full 128-byte lines; per-lane 16-byte
+    // stores of 32 different rows moved 3x the output bytes through L1 and cost 20% at K = 8192).
+    CUtensorMap map_out;
+    std::memset(&map_out, 0, sizeof(map_out));
+    params.tma_store = !fanout && params.col_stride == 1 && params.rows_per_batch == 0xFFFFFFFFu &&
+                       params.out_stride >= n &&
+                       encode_tensor_map_2d_b32(&map_out, params.out, n, m, params.out_stride * 4u, 32u, 32u);
     if (pair) {
-        return fanout ? launch_kernel<true, true>(tiles, sm_count, map_a, map_w, params, stream)
-                      : launch_kernel<false, true>(tiles, sm_count, map_a, map_w, params, stream);
+        return fanout ? launch_kernel<true, true>(tiles, sm_count, map_a, map_w, &map_out, params, stream)
+                      : launch_kernel<false, true>(tiles, sm_count, map_a, map_w, &map_out, params, stream);
     }
-    return fanout ? launch_kernel<true, false>(tiles, sm_count, map_a, map_w, params, stream)
-                  : launch_kernel<false, false>(tiles, sm_count, map_a, map_w, params, stream);
+    return fanout ? launch_kernel<true, false>(tiles, sm_count, map_a, map_w, &map_out, params, stream)
+                  : launch_kernel<false, false>(tiles, sm_count, map_a, map_w, &map_out, params, stream);
 }
 
 cudaError_t run_w8a8_gemm(const int8_t *a, size_t a_stride, const int8_t *w, size_t w_stride, uint32_t m, uint32_t n,

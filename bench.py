@@ -357,6 +357,30 @@ def run_ours(args: argparse.Namespace) -> None:
     achieved_tops = rank_gemm_ops / gemm_seconds / 1e12 if gemm_seconds > 0 else 0.0
     achieved_tops = -max_over_ranks(-achieved_tops)  # the slowest rank's rate
 
+    # ---- the library's int8 rate on this GPU, as the roofline's denominator ----
+    # cuBLASLt's int8 GEMM (torch._int_mm, int32 output: the same output bytes as the fp32
+    # dequantized output) on each of the rank's projection shapes, random int8 operands, same L2
+    # protocol. B200's int8 rate is nominally twice bf16; measured here it runs above twice the
+    # measured bf16 burst, so the larger of the two is the peak the GEMM is judged against.
+    library_ms = []
+    for p in projections:
+        a8 = torch.randint(-127, 128, (TOKENS, p["k"]), dtype=torch.int8, device=cuda)
+        w8 = torch.randint(-127, 128, (p["gather"].count, p["k"]), dtype=torch.int8, device=cuda)
+        for _ in range(3):
+            torch._int_mm(a8, w8.t())
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(10)]
+        for s_ev, e_ev in evs:
+            prime()
+            s_ev.record(stream)
+            torch._int_mm(a8, w8.t())
+            e_ev.record(stream)
+        torch.cuda.synchronize()
+        library_ms.append(statistics.mean(s_ev.elapsed_time(e_ev) for s_ev, e_ev in evs))
+        del a8, w8
+    torch.cuda.empty_cache()
+    library_tops = rank_gemm_ops / (sum(library_ms) * 1e-3) / 1e12
+    library_tops = max_over_ranks(library_tops)
+
     # ---- Q4_0 x Q8_0 decode matvec (M = 1), Q8_0 activations already on the device ----
     # One decode step of the FFN = gate, up and down back to back on the stream. The three
     # weight matrices (3 x 132 MB at full width) exceed L2, so each launch streams its weight
@@ -441,7 +465,8 @@ def run_ours(args: argparse.Namespace) -> None:
         cpu_baseline = cpu_reference_sample(target_seconds=args.cpu_seconds)
 
     peaks, peak_kind = measured_peaks()
-    int8_peak = 2.0 * peaks["bf16_tflops"]
+    bf16_doubled = 2.0 * peaks["bf16_tflops"]
+    int8_peak = max(bf16_doubled, library_tops)
     traffic = profile_traffic("w8a8_gemm_sm100_70b_ffn")
     q4_traffic = profile_traffic("q4_0_gemv_70b_decode")
     line = {
@@ -474,7 +499,13 @@ def run_ours(args: argparse.Namespace) -> None:
             "peak": round(int8_peak, 1),
             "unit": "TOPS",
             "frac": round(achieved_tops / int8_peak, 4),
-            "peak_source": f"2 x {peak_kind} cuBLAS bf16 burst ({peaks['bf16_tflops']} TF/s): B200 dense int8 rate is twice dense bf16",
+            "peak_source": (
+                f"the larger of cuBLASLt int8 (torch._int_mm) measured live on the same shapes ({library_tops:.1f} TOPS) "
+                f"and 2 x {peak_kind} cuBLAS bf16 burst ({bf16_doubled:.1f} TOPS)"
+            ),
+            "library_int8_tops": round(library_tops, 1),
+            "library_int8_ms_per_projection": [round(x, 4) for x in library_ms],
+            "peak_2x_bf16": round(bf16_doubled, 1),
             "traffic": traffic,
             "algorithmic_ops_per_rank_step": rank_gemm_ops,
             "gemm_ms_per_projection": [round(x, 4) for x in gemm_ms],

@@ -313,3 +313,21 @@ def quantize_q4_0(values: npt.NDArray[np.float32]) -> npt.NDArray[np.uint8]:
     codes = np.minimum(np.float32(15.0), np.trunc(scaled)).astype(np.int32)
     codes = np.clip(codes, 0, 15)
     return pack_q4_0_blocks(d.astype(np.float16), codes.astype(np.uint8))
+
+
+def pack_q4_0x4(blocks: npt.NDArray[np.uint8]) -> npt.NDArray[np.uint8]:
+    """Native ``block_q4_0`` rows ``[N, K/32, 18]`` (N % 4 == 0) into ggml-cpu's CPU_REPACK
+    block_q4_0x4 bytes, the layout the reference's backend unpacks (ggml-qpu.cpp:250-283): per
+    group of 4 rows and K block, the 4 fp16 scales (8 bytes), then 64 quant bytes in which the
+    4-byte chunk c of row r sits at (c * 4 + r) * 4, every byte XOR 0x88."""
+    n, nblocks, _ = blocks.shape
+    if n % 4 != 0:
+        raise ValueError("CPU_REPACK groups need N % 4 == 0")
+    rows = blocks.reshape(n // 4, 4, nblocks, 18)
+    packed = np.empty((n // 4, nblocks, 72), dtype=np.uint8)
+    for r in range(4):
+        packed[:, :, 2 * r : 2 * r + 2] = rows[:, r, :, 0:2]
+        for c in range(4):
+            at = 8 + (c * 4 + r) * 4
+            packed[:, :, at : at + 4] = rows[:, r, :, 2 + c * 4 : 6 + c * 4] ^ np.uint8(0x88)
+    return packed.reshape(-1)

@@ -147,6 +147,37 @@ class MatrixLayout(Structure):
     ]
 
 
+class GgmlTensor(Structure):
+    """``qpucuda_ggml_tensor``: the ggml_tensor fields the MUL_MAT offload reads."""
+
+    _fields_ = [
+        ("type", ctypes.c_int32),
+        ("cpu_repack", ctypes.c_int32),
+        ("ne", ctypes.c_int64 * 4),
+        ("nb", c_size_t * 4),
+        ("data", c_void_p),
+        ("identity", c_void_p),
+    ]
+
+
+class GgmlStats(Structure):
+    """``qpucuda_ggml_stats``."""
+
+    _fields_ = [
+        ("dispatch_count", c_uint64),
+        ("weight_cache_hits", c_uint64),
+        ("weight_cache_misses", c_uint64),
+        ("input_copy_ns", c_uint64),
+        ("submit_wait_ns", c_uint64),
+        ("output_copy_ns", c_uint64),
+        ("complete_ns", c_uint64),
+        ("rows", c_uint32),
+    ]
+
+
+GGML_TYPE_F32 = 0
+GGML_TYPE_Q4_0 = 2
+
 MEMORY_HOST = 0
 MEMORY_DEVICE = 1
 
@@ -221,6 +252,17 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, c_size_t, c_uint32, _P, c_size_t, c_uint32, c_uint32, c_uint32],
     ),
     "qpucuda_q4_0_kernel_source_hash": (c_char_p, []),
+    # qpucuda_ggml.h
+    "qpucuda_ggml_supports_mul_mat": (
+        c_int,
+        [POINTER(GgmlTensor), POINTER(GgmlTensor), POINTER(GgmlTensor), c_uint32, c_uint32],
+    ),
+    "qpucuda_ggml_unpack_q4_0x4": (_S, [_P, c_size_t, c_uint32, c_uint32, _P, c_size_t]),
+    "qpucuda_ggml_backend_create": (_S, [_P, c_uint32, c_uint32, POINTER(c_void_p)]),
+    "qpucuda_ggml_backend_destroy": (None, [_P]),
+    "qpucuda_ggml_mul_mat": (_S, [_P, POINTER(GgmlTensor), POINTER(GgmlTensor), POINTER(GgmlTensor)]),
+    "qpucuda_ggml_backend_forget": (None, [_P, _P]),
+    "qpucuda_ggml_backend_stats": (_S, [_P, POINTER(GgmlStats)]),
 }
 
 _LOCK = threading.Lock()

@@ -365,8 +365,135 @@ class PreparedQ4_0Linear:
         self.close()
 
 
+# ---------------------------------------------------------------------------------------------
+# GGML MUL_MAT offload core (include/qpucuda_ggml.h): what the reference's llama.cpp backend does
+# per MUL_MAT node (integrations/llama_cpp/backend/ggml-qpu.cpp:245-377, 539-620), over tensor
+# views with ggml's conventions: ne[0] is the innermost (K) extent, nb[i] the byte strides.
+
+
+def ggml_tensor_view(
+    array: npt.NDArray[Any], ggml_type: int, *, cpu_repack: bool = False, identity: int | None = None
+) -> Any:
+    """A ``qpucuda_ggml_tensor`` over a host array: F32 ``[M, K]`` rows, or Q4_0 weight blocks
+    ``[N, K/32, 18]`` (native) / the same bytes in block_q4_0x4 groups (``cpu_repack``)."""
+    view = _native.GgmlTensor()
+    view.type = ggml_type
+    view.cpu_repack = 1 if cpu_repack else 0
+    if ggml_type == _native.GGML_TYPE_F32:
+        rows, columns = array.shape
+        ne = (columns, rows, 1, 1)
+        nb0 = 4
+        nb1 = nb0 * columns
+    elif ggml_type == _native.GGML_TYPE_Q4_0:
+        outputs, blocks = array.shape[0], array.shape[1]
+        ne = (blocks * Q4_0_BLOCK_ELEMENTS, outputs, 1, 1)
+        nb0 = Q4_0_BLOCK_BYTES
+        nb1 = Q4_0_BLOCK_BYTES * blocks
+    else:
+        raise ValueError(f"unsupported ggml type {ggml_type}")
+    for i, extent in enumerate(ne):
+        view.ne[i] = extent
+    view.nb[0] = nb0
+    view.nb[1] = nb1
+    view.nb[2] = nb1 * ne[1]
+    view.nb[3] = view.nb[2] * ne[2]
+    view.data = array.ctypes.data
+    view.identity = identity if identity is not None else array.ctypes.data
+    return view
+
+
+def ggml_supports_mul_mat(weight: Any, activation: Any, destination: Any, *, minimum_rows: int = 1, maximum_rows: int = 4 * 65535) -> bool:
+    """``supports_q4_0_mul_mat`` with the device's row window (ggml-qpu.cpp:362-377, 631-633)."""
+    library = _native.load()
+    return bool(library.qpucuda_ggml_supports_mul_mat(ctypes.byref(weight), ctypes.byref(activation), ctypes.byref(destination), minimum_rows, maximum_rows))
+
+
+def ggml_unpack_q4_0x4(packed: npt.NDArray[np.uint8], input_columns: int, output_columns: int) -> npt.NDArray[np.uint8]:
+    """block_q4_0x4 groups back to native ``[N, K/32, 18]`` blocks (ggml-qpu.cpp:250-283)."""
+    packed = np.ascontiguousarray(packed, dtype=np.uint8)
+    native = np.empty((output_columns, input_columns // Q4_0_BLOCK_ELEMENTS, Q4_0_BLOCK_BYTES), dtype=np.uint8)
+    status = _native.load().qpucuda_ggml_unpack_q4_0x4(packed.ctypes.data, packed.nbytes, input_columns, output_columns, native.ctypes.data, native.nbytes)
+    _native.raise_for_status(status, what="qpucuda_ggml_unpack_q4_0x4")
+    return native
+
+
+class GgmlMulMatBackend:
+    """The MUL_MAT offload of one llama.cpp backend instance on one GPU: a weight cache of
+    prepared Q4_0 linears keyed by tensor identity, staging, and per-call statistics."""
+
+    def __init__(self: Self, device: Device, *, minimum_rows: int = 1, maximum_rows: int = 4 * 65535) -> None:
+        if not device.is_cuda:
+            raise ValueError("GgmlMulMatBackend requires the CUDA backend")
+        self.device = device
+        self.minimum_rows = minimum_rows
+        self.maximum_rows = maximum_rows
+        self._backend = device.backend
+        self._native = self._backend.native  # type: ignore[attr-defined]
+        handle = ctypes.c_void_p()
+        status = self._native.library.qpucuda_ggml_backend_create(self._native.handle, minimum_rows, maximum_rows, ctypes.byref(handle))
+        self._native.check(status, "qpucuda_ggml_backend_create")
+        self._handle = int(handle.value)  # type: ignore[arg-type]
+        self._closed = False
+
+    def supports(self: Self, weight: Any, activation: Any, destination: Any) -> bool:
+        return ggml_supports_mul_mat(weight, activation, destination, minimum_rows=self.minimum_rows, maximum_rows=self.maximum_rows)
+
+    def mul_mat_views(self: Self, weight: Any, activation: Any, destination: Any) -> int:
+        """``compute_q4_0_mul_mat`` over tensor views; returns the status (no raise)."""
+        with self._backend.launch_lock:  # type: ignore[attr-defined]
+            self._native.use_library_stream()
+            return int(self._native.library.qpucuda_ggml_mul_mat(self._handle, ctypes.byref(weight), ctypes.byref(activation), ctypes.byref(destination)))
+
+    def mul_mat(
+        self: Self,
+        weight_blocks: npt.NDArray[np.uint8],
+        activation: npt.NDArray[np.float32],
+        *,
+        cpu_repack: bool = False,
+        output_columns: int | None = None,
+        identity: int | None = None,
+    ) -> npt.NDArray[np.float32]:
+        """``activation [M, K] x weight^T`` for native Q4_0 blocks ``[N, K/32, 18]``, or, with
+        ``cpu_repack``, the same weight as block_q4_0x4 bytes (give ``output_columns``)."""
+        activation = np.ascontiguousarray(activation, dtype=np.float32)
+        if cpu_repack:
+            if output_columns is None:
+                raise ValueError("output_columns is required for a CPU_REPACK weight")
+            blocks = activation.shape[1] // Q4_0_BLOCK_ELEMENTS
+            weight_blocks = np.ascontiguousarray(weight_blocks, dtype=np.uint8).reshape(output_columns, blocks, Q4_0_BLOCK_BYTES)
+        weight_view = ggml_tensor_view(weight_blocks, _native.GGML_TYPE_Q4_0, cpu_repack=cpu_repack, identity=identity)
+        destination = np.empty((activation.shape[0], weight_blocks.shape[0]), dtype=np.float32)
+        status = self.mul_mat_views(weight_view, ggml_tensor_view(activation, _native.GGML_TYPE_F32), ggml_tensor_view(destination, _native.GGML_TYPE_F32))
+        self._native.check(status, "qpucuda_ggml_mul_mat")
+        return destination
+
+    def forget(self: Self, identity: int) -> None:
+        self._native.library.qpucuda_ggml_backend_forget(self._handle, identity)
+
+    @property
+    def stats(self: Self) -> dict[str, int]:
+        stats = _native.GgmlStats()
+        self._native.check(self._native.library.qpucuda_ggml_backend_stats(self._handle, ctypes.byref(stats)), "qpucuda_ggml_backend_stats")
+        return {name: int(getattr(stats, name)) for name, _ in _native.GgmlStats._fields_}
+
+    def close(self: Self) -> None:
+        if not self._closed:
+            self._native.library.qpucuda_ggml_backend_destroy(self._handle)
+            self._closed = True
+
+    def __enter__(self: Self) -> Self:
+        return self
+
+    def __exit__(self: Self, exc_type: object, exc_value: object, traceback: object) -> None:
+        self.close()
+
+
 __all__ = [
+    "GgmlMulMatBackend",
     "PreparedQ4_0Linear",
+    "ggml_supports_mul_mat",
+    "ggml_tensor_view",
+    "ggml_unpack_q4_0x4",
     "pack_ggml_q4_0_blocks",
     "pack_ggml_q8_0_blocks",
     "q4_0_kernel_source_hash",

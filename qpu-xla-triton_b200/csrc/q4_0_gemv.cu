@@ -157,6 +157,24 @@ __device__ __forceinline__ void read_activation_item(const ActivationView &view,
     }
 }
 
+constexpr int kFloatMagic = 0x4B400000;  // bits of 1.5 * 2^23 = 12582912.0f
+
+// Packed fp32 pairs (sm_100 add/mul .f32x2): each lane rounds to nearest exactly as
+// __fadd_rn / __fmul_rn, two values per instruction.
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+    return static_cast<unsigned long long>(__float_as_uint(lo)) | (static_cast<unsigned long long>(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 __device__ __forceinline__ void write_activation_item(const StagedActivation &staged, uint32_t item,
                                                       const uint32_t (&words)[8], uint16_t scale_bits) {
     int sum = 0;
@@ -164,7 +182,9 @@ __device__ __forceinline__ void write_activation_item(const StagedActivation &st
     for (int i = 0; i < 8; ++i) sum = __dp4a(static_cast<int>(words[i]), 0x01010101, sum);
     staged.lo[item] = make_int4(words[0], words[1], words[2], words[3]);
     staged.hi[item] = make_int4(words[4], words[5], words[6], words[7]);
-    staged.meta[item] = make_int2(__float_as_int(__half2float(__ushort_as_half(scale_bits))), -8 * sum);
+    // The dp4a seed also carries the float magic, so a block's dot comes out as the bits of
+    // 1.5 * 2^23 + dot (|dot| <= 32 * 127 * 8 < 2^22): one exact subtraction gives (float)dot.
+    staged.meta[item] = make_int2(__float_as_int(__half2float(__ushort_as_half(scale_bits))), kFloatMagic - 8 * sum);
 }
 
 // One thread per (row, block) item, two items per trip so two L2 round trips overlap. With
@@ -213,11 +233,14 @@ __device__ __forceinline__ int block_dot(uint4 w, int4 lo, int4 hi, int seed) {
 }
 
 // acc[r][c] += ((float)dot * d_w[c]) * d_a[r], rounded step by step as the reference rounds
-// each block term (ggml_q4_0.py:81-100).
+// each block term (ggml_q4_0.py:81-100). (float)dot is exact (the magic in the seed, one
+// subtraction), the two products of a column pair share packed multiplies, and the accumulate
+// stays a scalar __fadd_rn so nothing can be contracted into a fused multiply-add.
 template <int ROWS, int COLS>
 __device__ __forceinline__ void accumulate_block(const uint4 (&w)[COLS], const float (&dw)[COLS], uint32_t item,
                                                  uint32_t blocks, const StagedActivation &staged,
                                                  float (&acc)[ROWS][COLS]) {
+    const unsigned long long unbias = pack2(-12582912.0f, -12582912.0f);
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
         const uint32_t at = static_cast<uint32_t>(r) * blocks + item;
@@ -225,9 +248,21 @@ __device__ __forceinline__ void accumulate_block(const uint4 (&w)[COLS], const f
         const int4 hi = staged.hi[at];
         const int2 meta = staged.meta[at];
         const float da = __int_as_float(meta.x);
+        const unsigned long long da2 = pack2(da, da);
 #pragma unroll
-        for (int c = 0; c < COLS; ++c)
-            acc[r][c] = __fadd_rn(acc[r][c], __fmul_rn(__fmul_rn(__int2float_rn(block_dot(w[c], lo, hi, meta.y)), dw[c]), da));
+        for (int c = 0; c + 1 < COLS; c += 2) {
+            const int bits0 = block_dot(w[c], lo, hi, meta.y);
+            const int bits1 = block_dot(w[c + 1], lo, hi, meta.y);
+            unsigned long long v = add2(pack2(__int_as_float(bits0), __int_as_float(bits1)), unbias);
+            v = mul2(v, pack2(dw[c], dw[c + 1]));
+            v = mul2(v, da2);
+            acc[r][c] = __fadd_rn(acc[r][c], __uint_as_float(static_cast<uint32_t>(v)));
+            acc[r][c + 1] = __fadd_rn(acc[r][c + 1], __uint_as_float(static_cast<uint32_t>(v >> 32)));
+        }
+        if constexpr (COLS % 2 == 1) {
+            const float x = __fadd_rn(__int_as_float(block_dot(w[COLS - 1], lo, hi, meta.y)), -12582912.0f);
+            acc[r][COLS - 1] = __fadd_rn(acc[r][COLS - 1], __fmul_rn(__fmul_rn(x, dw[COLS - 1]), da));
+        }
     }
 }
 
@@ -276,8 +311,11 @@ struct DirectParams {
 // activation is staged, and the first trip of its next group before the warp reduces the
 // current one, so the weight stream does not stop for either. Partial sums of a group's
 // SPLIT warps are added in part order through shared memory (deterministic). Registers per
-// thread are capped so that MIN_BLOCKS CTAs of 256 threads fit on an SM.
-template <int ROWS, int SPLIT, int COLS, int UNROLL, int MIN_BLOCKS, bool F32>
+// thread are capped so that MIN_BLOCKS CTAs of 256 threads fit on an SM. With PIPE, a trip's
+// weights are copied and the next trip's loads (or the next group's first) are issued before
+// the trip is computed, so a warp's loads stay in flight during its own arithmetic (the
+// several-row kernels, whose arithmetic per byte is several times the single row's).
+template <int ROWS, int SPLIT, int COLS, int UNROLL, int MIN_BLOCKS, bool F32, bool PIPE = false>
 __global__ void __launch_bounds__(kThreads, MIN_BLOCKS) q4_0_direct_kernel(const DirectParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float partial[kWarps][ROWS * COLS];
@@ -348,20 +386,40 @@ __global__ void __launch_bounds__(kThreads, MIN_BLOCKS) q4_0_direct_kernel(const
 #pragma unroll
             for (int c = 0; c < COLS; ++c) acc[r][c] = 0.0f;
         }
+        const uint32_t next = group + gridDim.x * kSlots;
         for (uint32_t b = first; b < blocks; b += kTrip) {
-            if (b != first) load_trip(group, b);
+            uint4 wc[UNROLL][COLS];
+            uint16_t sc[UNROLL][COLS];
+            if constexpr (PIPE) {
+#pragma unroll
+                for (int u = 0; u < UNROLL; ++u) {
+#pragma unroll
+                    for (int c = 0; c < COLS; ++c) {
+                        wc[u][c] = w[u][c];
+                        sc[u][c] = s[u][c];
+                    }
+                }
+                if (b + kTrip < blocks) {
+                    load_trip(group, b + kTrip);
+                } else if (next < groups) {
+                    load_trip(next, first);
+                }
+            } else if (b != first) {
+                load_trip(group, b);
+            }
+            const auto &wt = PIPE ? wc : w;
+            const auto &st = PIPE ? sc : s;
 #pragma unroll
             for (int u = 0; u < UNROLL; ++u) {
                 if (b + u * kStride < blocks) {
                     float dw[COLS];
 #pragma unroll
-                    for (int c = 0; c < COLS; ++c) dw[c] = __half2float(__ushort_as_half(s[u][c]));
-                    accumulate_block<ROWS, COLS>(w[u], dw, b + u * kStride, blocks, staged, acc);
+                    for (int c = 0; c < COLS; ++c) dw[c] = __half2float(__ushort_as_half(st[u][c]));
+                    accumulate_block<ROWS, COLS>(wt[u], dw, b + u * kStride, blocks, staged, acc);
                 }
             }
         }
-        const uint32_t next = group + gridDim.x * kSlots;
-        if (next < groups) load_trip(next, first);
+        if (!PIPE && next < groups) load_trip(next, first);
 
         float sums[ROWS * COLS];
 #pragma unroll
@@ -445,11 +503,11 @@ __global__ void __launch_bounds__(kNativeThreads) q4_0_native_kernel(const Nativ
     }
 }
 
-template <int ROWS, int SPLIT, int COLS, int UNROLL, int MIN_BLOCKS, bool F32>
+template <int ROWS, int SPLIT, int COLS, int UNROLL, int MIN_BLOCKS, bool F32, bool PIPE = false>
 cudaError_t launch_direct(const DirectParams &p, int sm_count, cudaStream_t stream) {
     const size_t smem = activation_bytes(ROWS, p.blocks);
     if (smem > kSmemBudget) return cudaErrorInvalidValue;
-    auto kernel = q4_0_direct_kernel<ROWS, SPLIT, COLS, UNROLL, MIN_BLOCKS, F32>;
+    auto kernel = q4_0_direct_kernel<ROWS, SPLIT, COLS, UNROLL, MIN_BLOCKS, F32, PIPE>;
     if (smem > 48u * 1024u) {
         const cudaError_t error =
             cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -490,12 +548,18 @@ cudaError_t launch_rows(const DirectParams &p, int sm_count, cudaStream_t stream
     // split over 4 warps with seven blocks per lane and column in one trip: four times the
     // independent groups of the unsplit kernel, so the grid fills the SMs even when the matrix
     // is narrow (a column shard), and 14 loads in flight per lane within 128 registers.
+    // Two rows, and four rows over long reductions, overlap each warp's next loads with its
+    // arithmetic (PIPE); measured on B200 with L2 flushed (70B FFN shapes): two rows
+    // 34.8 -> 32.8 us (K = 8192) and 41.0 -> 34.8 us (K = 28672), four rows at K = 28672
+    // 59.4 -> 51.2 us; four rows at K = 8192 and the single row gained nothing from it, and three
+    // rows at K = 28672 lost (45.1 -> 49.2 us).
     if constexpr (ROWS == 1) {
         if (p.blocks >= 640) return launch_direct<ROWS, 4, 2, 7, 2, F32>(p, sm_count, stream);
         return launch_direct<ROWS, 1, 2, 4, 3, F32>(p, sm_count, stream);
     } else if constexpr (ROWS == 2) {
-        return launch_direct<ROWS, 1, 2, 2, 3, F32>(p, sm_count, stream);
+        return launch_direct<ROWS, 1, 2, 2, 2, F32, true>(p, sm_count, stream);
     } else {
+        if (ROWS == 4 && p.blocks >= 640) return launch_direct<ROWS, 1, 2, 4, 2, F32, true>(p, sm_count, stream);
         return launch_direct<ROWS, 1, 2, 4, 2, F32>(p, sm_count, stream);
     }
 }
@@ -629,24 +693,6 @@ __device__ __forceinline__ void mma_s8(const uint32_t (&a)[4], uint32_t b0, uint
         "{%10, %10, %11, %11};"
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c_lo), "r"(c_hi));
-}
-
-constexpr int kFloatMagic = 0x4B400000;  // bits of 1.5 * 2^23 = 12582912.0f
-
-// Packed fp32 pairs (sm_100 add/mul .f32x2): each lane rounds to nearest exactly as
-// __fadd_rn / __fmul_rn, two values per instruction.
-__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
-    return static_cast<unsigned long long>(__float_as_uint(lo)) | (static_cast<unsigned long long>(__float_as_uint(hi)) << 32);
-}
-__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
-    unsigned long long d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
-    unsigned long long d;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
 }
 
 // BM rows x BN columns per CTA, 8 warps tiled over it (MxTile), kStages stages of 4 blocks.

@@ -22,6 +22,12 @@ constexpr uint32_t kMaxRows = 4u * 65535u;
 struct CachedLinear {
     qpucuda_q4_0_linear *linear = nullptr;
     uint32_t row_capacity = 0;
+    // What the plan was prepared from: a key reused by a different tensor (freed and
+    // reallocated at the same address) does not match and is prepared afresh.
+    const void *data = nullptr;
+    int64_t input_columns = 0;
+    int64_t output_columns = 0;
+    int32_t cpu_repack = 0;
 };
 
 bool contiguous_f32(const qpucuda_ggml_tensor *t) {
@@ -85,12 +91,14 @@ qpucuda_status ensure_staging(qpucuda_ggml_backend *backend, size_t source, size
 }
 
 // get_or_prepare_linear (ggml-qpu.cpp:319-360): a cached plan serves any call with at most its
-// row capacity; a call with more rows replaces it.
+// row capacity on the same weight (data pointer, shape, layout); otherwise it is replaced.
 qpucuda_status get_or_prepare(qpucuda_ggml_backend *backend, const qpucuda_ggml_tensor *weight, uint32_t rows,
                               qpucuda_q4_0_linear **result) {
     const void *key = weight->identity != nullptr ? weight->identity : weight->data;
     auto existing = backend->linears.find(key);
-    if (existing != backend->linears.end() && existing->second.row_capacity >= rows) {
+    if (existing != backend->linears.end() && existing->second.row_capacity >= rows &&
+        existing->second.data == weight->data && existing->second.input_columns == weight->ne[0] &&
+        existing->second.output_columns == weight->ne[1] && existing->second.cpu_repack == weight->cpu_repack) {
         ++backend->stats.weight_cache_hits;
         *result = existing->second.linear;
         return QPUCUDA_OK;
@@ -130,7 +138,7 @@ qpucuda_status get_or_prepare(qpucuda_ggml_backend *backend, const qpucuda_ggml_
     const qpucuda_status status = qpucuda_q4_0_linear_prepare(backend->context, &desc, &prepared);
     if (status != QPUCUDA_OK) return status;
     ++backend->stats.weight_cache_misses;
-    backend->linears.emplace(key, CachedLinear{prepared, rows});
+    backend->linears.emplace(key, CachedLinear{prepared, rows, weight->data, weight->ne[0], weight->ne[1], weight->cpu_repack});
     *result = prepared;
     return QPUCUDA_OK;
 }

@@ -64,6 +64,13 @@ def test_weight_cache_follows_get_or_prepare_linear(cuda_device: Device) -> None
         backend.mul_mat(weight, activation[:2])
         assert backend.stats["weight_cache_misses"] == 3
         assert backend.stats["dispatch_count"] == 5
+        # the same cache key on another weight (a tensor reallocated at a reused address): a new plan
+        other = oracle.quantize_q4_0(np.random.default_rng(6).standard_normal((64, 512)).astype(np.float32) * 0.02)
+        got = backend.mul_mat(other, activation[:2], identity=weight.ctypes.data)
+        assert backend.stats["weight_cache_misses"] == 4
+        from gpu_helpers import max_relative_error
+
+        assert max_relative_error(got, _expected(activation[:2], other)) <= Q4_0_TOLERANCE
 
 
 def test_cpu_repack_weights(cuda_device: Device) -> None:

@@ -55,10 +55,16 @@ constexpr int W_BOX_ROWS = 128;  // rows of W per TMA box (a 256-row B tile is t
 // and its half (128 rows) of B, 32 KB per stage, 6 stages in the same shared memory.
 template <bool PAIR>
 struct Pipe {
-    static constexpr int STAGES = PAIR ? 5 : 4;  // 4..7 stages measured within 1% in pair mode
-    static constexpr int A_BYTES = BM * BK;
-    static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK;
+    // 128-byte K boxes per stage and per operand: CTA pairs take two (256 bytes of K, eight
+    // MMAs between barrier round trips)
+    static constexpr int K_BOXES = PAIR ? 2 : 1;
+    static constexpr int STAGES = PAIR ? 3 : 4;
+    static constexpr int A_BOX_BYTES = BM * BK;
+    static constexpr int B_BOX_BYTES = (PAIR ? BN / 2 : BN) * BK;
+    static constexpr int A_BYTES = K_BOXES * A_BOX_BYTES;
+    static constexpr int B_BYTES = K_BOXES * B_BOX_BYTES;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int K_STAGE = K_BOXES * BK;  // bytes of K per stage
 };
 
 static_assert(BN == kGemmBlockN && BM == kGemmBlockM && BK == kGemmBlockK && W_BOX_ROWS == kGemmWeightBoxRows,
@@ -340,14 +346,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         break;
                     }
                     const uint32_t full = smem_u32(&control->full[stage]);
-                    const int x = static_cast<int>(kb * BK);
+                    const int x = static_cast<int>(kb * Pipe<PAIR>::K_STAGE);
                     if constexpr (PAIR) {
                         // Both CTAs' bytes complete on the leader's barrier, which expects them all.
                         if (leader) mbar_expect_tx(full, 2 * STAGE_BYTES);
                         const uint32_t leader_full = map_to_rank(full, 0);
-                        tma_load_2d_pair(smem_u32(stage_a + stage * A_STAGE_BYTES), &map_a, leader_full, x, m0);
-                        tma_load_2d_pair(smem_u32(stage_b + stage * B_STAGE_BYTES), &map_w, leader_full, x,
-                                         n0 + static_cast<int>(rank) * W_BOX_ROWS);
+#pragma unroll
+                        for (int box = 0; box < Pipe<PAIR>::K_BOXES; ++box) {
+                            tma_load_2d_pair(smem_u32(stage_a + stage * A_STAGE_BYTES + box * Pipe<PAIR>::A_BOX_BYTES),
+                                             &map_a, leader_full, x + box * BK, m0);
+                            tma_load_2d_pair(smem_u32(stage_b + stage * B_STAGE_BYTES + box * Pipe<PAIR>::B_BOX_BYTES),
+                                             &map_w, leader_full, x + box * BK, n0 + static_cast<int>(rank) * W_BOX_ROWS);
+                        }
                     } else {
                         mbar_expect_tx(full, STAGE_BYTES);
                         tma_load_2d(smem_u32(stage_a + stage * A_STAGE_BYTES), &map_a, full, x, m0);
@@ -397,13 +407,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (!ok) break;
                 tc_fence_after();
                 if (lane == 0) {
-                    const uint64_t a_desc = smem_desc_sw128(smem_u32(stage_a + stage * A_STAGE_BYTES));
-                    const uint64_t b_desc = smem_desc_sw128(smem_u32(stage_b + stage * B_STAGE_BYTES));
 #pragma unroll
-                    for (int kk = 0; kk < BK / UMMA_K; ++kk) {
-                        // Advance the start address by 32 bytes (encoded >> 4) within the swizzle row.
-                        const uint64_t a = a_desc + static_cast<uint64_t>(kk * (UMMA_K >> 4));
-                        const uint64_t b = b_desc + static_cast<uint64_t>(kk * (UMMA_K >> 4));
+                    for (int kk = 0; kk < Pipe<PAIR>::K_STAGE / UMMA_K; ++kk) {
+                        // box kk / 4 of the stage; within it, the start address advances by 32 bytes
+                        // (encoded >> 4) along the swizzle row
+                        constexpr int kPerBox = BK / UMMA_K;
+                        const int box = kk / kPerBox;
+                        const uint64_t a = smem_desc_sw128(smem_u32(stage_a + stage * A_STAGE_BYTES + box * Pipe<PAIR>::A_BOX_BYTES)) +
+                                           static_cast<uint64_t>((kk % kPerBox) * (UMMA_K >> 4));
+                        const uint64_t b = smem_desc_sw128(smem_u32(stage_b + stage * B_STAGE_BYTES + box * Pipe<PAIR>::B_BOX_BYTES)) +
+                                           static_cast<uint64_t>((kk % kPerBox) * (UMMA_K >> 4));
                         if constexpr (PAIR) {
                             umma_i8_pair(d_tmem, a, b, (kb | kk) != 0 ? 1u : 0u);
                         } else {
@@ -771,7 +784,7 @@ cudaError_t launch_w8a8_gemm_sm100_mode(const CUtensorMap *map_a, const CUtensor
     params.m = m;
     params.n = n;
     params.k = k;
-    params.num_kb = (k + BK - 1) / BK;
+    params.num_kb = pair ? (k + Pipe<true>::K_STAGE - 1) / Pipe<true>::K_STAGE : (k + BK - 1) / BK;
     params.m_blocks = (m + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM);
     params.n_blocks = (n + BN - 1) / BN;
     params.mode = static_cast<int>(epilogue.mode);

@@ -753,15 +753,15 @@ cudaError_t launch_kernel(uint32_t tiles, int sm_count, const CUtensorMap *map_a
 
 }  // namespace
 
-// Single-CTA tiles (128 x 256) for one row block or when the epilogue also writes peers; CTA pairs
-// (256 x 256 per pair, a third less A and B traffic per output than the single-CTA tile) for
-// local outputs from two row blocks on. Measured on B200 (M = 4096): pairs take the 70B FFN gate
-// GEMM from 776 to 746 us and down from 689 to 658 us; with peer destinations (fused all-gather
-// at 2 GPUs) the single-CTA tiles exposed less of the exchange (0.06 against 0.14 ms per step).
+// Single-CTA tiles (128 x 256) for one row block; CTA pairs (256 x 256 per pair, a third less A
+// and B traffic per output than the single-CTA tile, 256-byte K stages) from two row blocks on.
+// Measured on B200 (M = 4096, L2 flushed): the 70B FFN gate GEMM takes 746 us single-CTA and
+// 666 us in pairs, down 692 and 602 us; with peer destinations (fused all-gather, 2 GPUs) the
+// step measured 4137 TOPS in pairs against 4071-4077 single-CTA in the same call.
 cudaError_t launch_w8a8_gemm_sm100(const CUtensorMap *map_a, const CUtensorMap *map_w, uint32_t m, uint32_t n,
                                    uint32_t k, const GemmEpilogue &epilogue, unsigned int *error_word, int sm_count,
                                    cudaStream_t stream) {
-    const bool pair = m > kGemmBlockM && epilogue.peer_count == 0;
+    const bool pair = m > kGemmBlockM;
     return launch_w8a8_gemm_sm100_mode(map_a, map_w, m, n, k, epilogue, error_word, sm_count, pair, stream);
 }
 

@@ -15,9 +15,9 @@
 // so exactly one CTA per SM and its 512 TMEM columns are always free).
 //   warp 0      TMA producer: A tile 128 x 128 B and W tile 256 x 128 B (two 128-row boxes)
 //               per stage, 4-stage ring, 128-byte swizzle, mbarrier complete_tx.
-//   warp 1      TMEM allocator and MMA issuer: 4 x tcgen05.mma (M=128, N=256, K=32)
-//               per stage; tcgen05.commit releases the stage and, after the last
-//               K block, signals the accumulator buffer full.
+//   warp 1      TMEM allocator and MMA issuer (one thread runs the loop): 4 x tcgen05.mma
+//               (M=128, N=256, K=32) per stage; tcgen05.commit releases the stage and,
+//               after the last K block, signals the accumulator buffer full.
 //   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, dequantize,
 //               store; two accumulator buffers (2 x 256 columns) let the epilogue
 //               of tile i overlap the main loop of tile i+1.
@@ -391,22 +391,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         __syncwarp();  // reconverge before the CTA barrier at the end
     } else if (warp == 1) {
         // ---------------- MMA issuer (the leader CTA only, in a pair) ----------------
-        uint32_t stage = 0, phase = 0, local_tile = 0;
-        bool ok = !PAIR || leader, any_mma = false;
-        for (uint32_t tile = first_tile; ok && tile < num_tiles; tile += tile_step, ++local_tile) {
-            const uint32_t acc = local_tile & 1u;
-            const uint32_t acc_phase = (local_tile >> 1) & 1u;
-            if (lane == 0) ok = wait_bounded(smem_u32(&control->tmem_empty[acc]), acc_phase ^ 1u, control, params.error_word);
-            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t d_tmem = tmem_base + acc * BN;
-            for (uint32_t kb = 0; kb < params.num_kb; ++kb) {
-                if (lane == 0) ok = wait_bounded(smem_u32(&control->full[stage]), phase, control, params.error_word);
-                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        // One thread runs the whole loop: it waits on the barriers, fences and issues; the warp's
+        // other lanes wait at the final __syncwarp.
+        if (lane == 0 && (!PAIR || leader)) {
+            uint32_t stage = 0, phase = 0, local_tile = 0;
+            bool ok = true, any_mma = false;
+            for (uint32_t tile = first_tile; ok && tile < num_tiles; tile += tile_step, ++local_tile) {
+                const uint32_t acc = local_tile & 1u;
+                const uint32_t acc_phase = (local_tile >> 1) & 1u;
+                ok = wait_bounded(smem_u32(&control->tmem_empty[acc]), acc_phase ^ 1u, control, params.error_word);
                 if (!ok) break;
                 tc_fence_after();
-                if (lane == 0) {
+                const uint32_t d_tmem = tmem_base + acc * BN;
+                for (uint32_t kb = 0; kb < params.num_kb; ++kb) {
+                    ok = wait_bounded(smem_u32(&control->full[stage]), phase, control, params.error_word);
+                    if (!ok) break;
+                    tc_fence_after();
 #pragma unroll
                     for (int kk = 0; kk < Pipe<PAIR>::K_STAGE / UMMA_K; ++kk) {
                         // box kk / 4 of the stage; within it, the start address advances by 32 bytes
@@ -430,31 +430,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         umma_commit(smem_u32(&control->empty[stage]));
                     }
                     any_mma = true;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
                 }
-                __syncwarp();
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1u;
-                }
-            }
-            if (!ok) break;
-            if (lane == 0) {
+                if (!ok) break;
                 if constexpr (PAIR) {
                     umma_commit_pair_both(smem_u32(&control->tmem_full[acc]));
                 } else {
                     umma_commit(smem_u32(&control->tmem_full[acc]));
                 }
             }
-            __syncwarp();
-        }
-        if (!ok && lane == 0 && any_mma) {
-            // Abort path: wait for every MMA this thread issued before TMEM is freed.
-            if constexpr (PAIR) {
-                umma_commit_pair_local(smem_u32(&control->drain));
-            } else {
-                umma_commit(smem_u32(&control->drain));
+            if (!ok && any_mma) {
+                // Abort path: wait for every MMA this thread issued before TMEM is freed.
+                if constexpr (PAIR) {
+                    umma_commit_pair_local(smem_u32(&control->drain));
+                } else {
+                    umma_commit(smem_u32(&control->drain));
+                }
+                wait_drain(smem_u32(&control->drain), 0);
             }
-            wait_drain(smem_u32(&control->drain), 0);
         }
         __syncwarp();
     } else {

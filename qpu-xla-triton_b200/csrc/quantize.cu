@@ -342,11 +342,16 @@ cudaError_t launch_staged_config(const float *x, size_t x_stride, uint32_t rows,
                                  cudaStream_t stream) {
     const size_t smem = static_cast<size_t>(STAGES) * cols * sizeof(float);
     auto kernel = quantize_rows_int8_bulk<THREADS, STAGES>;
-    cudaError_t error = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    int per_sm = 0;
-    if (error == cudaSuccess) error = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, THREADS, smem);
-    if (error != cudaSuccess) return error;
-    if (per_sm < 1) return cudaErrorNotSupported;
+    // The attribute is raised to the whole budget once, so every row length fits; 1024 threads
+    // and at least half the shared memory per CTA leave one CTA per SM.
+    static bool configured = false;
+    if (!configured) {
+        const cudaError_t error = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       static_cast<int>(kStagedSmemBudget));
+        if (error != cudaSuccess) return error;
+        configured = true;
+    }
+    const int per_sm = 1;
     const uint64_t slots = static_cast<uint64_t>(sm_count) * static_cast<uint64_t>(per_sm);
     const uint32_t grid = rows < slots ? rows : static_cast<uint32_t>(slots);
     kernel<<<grid, THREADS, smem, stream>>>(x, x_stride, rows, cols, padded_cols, q, q_stride, scales, error_word);

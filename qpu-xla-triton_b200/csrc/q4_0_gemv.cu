@@ -835,13 +835,12 @@ __global__ void __launch_bounds__(kMxThreads) q4_0_mx_kernel(const MxParams p) {
 
 template <int BM>
 cudaError_t launch_mx_tiles(const MxParams &p, uint32_t rows_pad, uint32_t count, cudaStream_t stream) {
-    static bool configured = false;
-    if (!configured) {
-        const cudaError_t error = cudaFuncSetAttribute(q4_0_mx_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                       MxTile<BM>::kSmemBytes);
-        if (error != cudaSuccess) return error;
-        configured = true;
-    }
+    static PerDeviceOnce configured;
+    const cudaError_t error = configured.run([] {
+        return cudaFuncSetAttribute(q4_0_mx_kernel<BM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    MxTile<BM>::kSmemBytes);
+    });
+    if (error != cudaSuccess) return error;
     const dim3 grid((count + MxTile<BM>::kBN - 1) / MxTile<BM>::kBN, (p.rows + BM - 1) / BM);
     (void)rows_pad;
     q4_0_mx_kernel<BM><<<grid, kMxThreads, MxTile<BM>::kSmemBytes, stream>>>(p);

@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdint>
 #include <mutex>
@@ -65,6 +66,32 @@ class DeviceGuard {
   private:
     int previous_ = -1;
     bool changed_ = false;
+};
+
+// Runs a kernel's one-time set-up (cudaFuncSetAttribute and the like) once per device: such
+// attributes apply to the current device only, and several contexts of one process may sit on
+// different devices. Thread-safe; a failed set-up is retried by the next call.
+class PerDeviceOnce {
+  public:
+    template <typename Configure>
+    cudaError_t run(Configure &&configure) {
+        int device = 0;
+        const cudaError_t error = cudaGetDevice(&device);
+        if (error != cudaSuccess) return error;
+        if (device < 0 || device >= kMaxDevices) return configure();
+        const uint64_t bit = uint64_t{1} << device;
+        if (done_.load(std::memory_order_acquire) & bit) return cudaSuccess;
+        std::lock_guard<std::mutex> lock(mutex_);
+        if (done_.load(std::memory_order_relaxed) & bit) return cudaSuccess;
+        const cudaError_t result = configure();
+        if (result == cudaSuccess) done_.fetch_or(bit, std::memory_order_release);
+        return result;
+    }
+
+  private:
+    static constexpr int kMaxDevices = 64;
+    std::atomic<uint64_t> done_{0};
+    std::mutex mutex_;
 };
 
 uint64_t monotonic_ns();

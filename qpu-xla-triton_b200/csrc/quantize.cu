@@ -344,13 +344,12 @@ cudaError_t launch_staged_config(const float *x, size_t x_stride, uint32_t rows,
     auto kernel = quantize_rows_int8_bulk<THREADS, STAGES>;
     // The attribute is raised to the whole budget once, so every row length fits; 1024 threads
     // and at least half the shared memory per CTA leave one CTA per SM.
-    static bool configured = false;
-    if (!configured) {
-        const cudaError_t error = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                       static_cast<int>(kStagedSmemBudget));
-        if (error != cudaSuccess) return error;
-        configured = true;
-    }
+    static PerDeviceOnce configured;
+    const cudaError_t error = configured.run([kernel] {
+        return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kStagedSmemBudget));
+    });
+    if (error != cudaSuccess) return error;
     const int per_sm = 1;
     const uint64_t slots = static_cast<uint64_t>(sm_count) * static_cast<uint64_t>(per_sm);
     const uint32_t grid = rows < slots ? rows : static_cast<uint32_t>(slots);

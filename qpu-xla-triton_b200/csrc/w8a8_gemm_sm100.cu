@@ -11,7 +11,7 @@
 // __int2float_rn / __fmul_rn / __fadd_rn so nothing is contracted into an FMA
 // and the result is bit-identical to the reference's NumPy arithmetic.
 //
-// Structure: one persistent CTA per SM (192 threads, ~197 KB of shared memory,
+// Structure: one persistent CTA per SM (192 threads, ~225 KB of shared memory,
 // so exactly one CTA per SM and its 512 TMEM columns are always free).
 //   warp 0      TMA producer: A tile 128 x 128 B and W tile 256 x 128 B (two 128-row boxes)
 //               per stage, 4-stage ring, 128-byte swizzle, mbarrier complete_tx.
@@ -26,10 +26,10 @@
 // bounded waits, frees TMEM and returns. No multicast load is used anywhere.
 //
 // CTA-pair mode (PAIR, clusters of 2, tcgen05 cta_group::2): a 256 x 256 tile per pair; each CTA
-// stages its 128 rows of A and 128 of the 256 W rows (32 KB per stage, 6 stages) with TMA loads
-// whose bytes complete on the leader (rank 0) CTA's barrier; the leader issues M = 256 MMAs that
-// read both CTAs' shared memory and write each CTA's 128 accumulator rows into its own tensor
-// memory; its commits arrive on the stage and accumulator barriers of both CTAs; each CTA's
+// stages its 128 rows of A and 128 of the 256 W rows (256 bytes of K per stage, 64 KB, 3 stages)
+// with TMA loads whose bytes complete on the leader (rank 0) CTA's barrier; the leader issues
+// M = 256 MMAs that read both CTAs' shared memory and write each CTA's 128 accumulator rows into
+// its own tensor memory; its commits arrive on the stage and accumulator barriers of both CTAs; each CTA's
 // epilogue drains its own rows and releases the buffer on the leader's barrier. The protocol
 // (who arms which barrier, the same warp allocating tensor memory in both CTAs) follows
 // CUTLASS's sm100 2-SM GEMM pipeline.
@@ -52,7 +52,7 @@ constexpr int W_BOX_ROWS = 128;  // rows of W per TMA box (a 256-row B tile is t
 
 // Pipeline shape per mode. Single-CTA: A 128 x 128 B + B 256 x 128 B = 48 KB per stage, 4 stages.
 // CTA pair (tcgen05 cta_group::2, M = 256 across two SMs): each CTA stages its own 128 rows of A
-// and its half (128 rows) of B, 32 KB per stage, 6 stages in the same shared memory.
+// and its half (128 rows) of B for 256 bytes of K, 64 KB per stage, 3 stages.
 template <bool PAIR>
 struct Pipe {
     // 128-byte K boxes per stage and per operand: CTA pairs take two (256 bytes of K, eight
@@ -695,10 +695,11 @@ cudaError_t configure_kernel() {
 
 // Clusters of two that can be resident at once (one CTA per SM), cached per device.
 int resident_pairs(int sm_count) {
-    static int cached[64] = {};
+    static std::atomic<int> cached[64] = {};
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return sm_count / 2;
-    if (cached[device] > 0) return cached[device];
+    const int known = cached[device].load(std::memory_order_relaxed);
+    if (known > 0) return known;
     cudaLaunchConfig_t config = {};
     config.gridDim = dim3(static_cast<unsigned>(sm_count & ~1), 1, 1);
     config.blockDim = dim3(NUM_THREADS, 1, 1);
@@ -716,7 +717,7 @@ int resident_pairs(int sm_count) {
         (void)cudaGetLastError();
         return sm_count / 2;
     }
-    cached[device] = clusters;
+    cached[device].store(clusters, std::memory_order_relaxed);
     return clusters;
 }
 
@@ -766,15 +767,15 @@ cudaError_t launch_w8a8_gemm_sm100_mode(const CUtensorMap *map_a, const CUtensor
                                         int sm_count, bool pair, cudaStream_t stream) {
     if (m == 0 || n == 0) return cudaSuccess;
     if (k == 0) return cudaErrorInvalidValue;
-    static bool configured = false;
-    if (!configured) {
+    static PerDeviceOnce configured;
+    const cudaError_t configure_error = configured.run([] {
         cudaError_t error = configure_kernel<false, false>();
         if (error == cudaSuccess) error = configure_kernel<true, false>();
         if (error == cudaSuccess) error = configure_kernel<false, true>();
         if (error == cudaSuccess) error = configure_kernel<true, true>();
-        if (error != cudaSuccess) return error;
-        configured = true;
-    }
+        return error;
+    });
+    if (configure_error != cudaSuccess) return configure_error;
     pair = pair && sm_count >= 2;
     GemmParams params;
     params.m = m;

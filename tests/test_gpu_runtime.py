@@ -82,6 +82,55 @@ def test_host_execute_of_a_large_batch_is_sliced_and_exact(cuda_device: Device) 
             np.testing.assert_array_equal(plan.execute_host(source), expected)
 
 
+def test_two_contexts_driven_from_two_threads_at_once() -> None:
+    """Two contexts on one device, each called from its own host thread at the same time (the C
+    calls release the GIL): every kernel's one-time set-up is per device and thread-safe, and each
+    context keeps its own stream and staging. Rows of 16384 columns take the bulk-staged row
+    quantizer, batches above 1024 rows the sliced host pipeline, M > 128 the CTA-pair GEMM."""
+    import threading
+
+    rng = np.random.default_rng(83)
+    rows, k, n = 1100, 16384, 384
+    weight = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32)
+    values, scales = oracle.quantize_per_output_channel_int8(weight)
+    sources = [(rng.standard_normal((rows, k)) * rng.uniform(0.1, 8.0, (rows, 1))).astype(np.float32) for _ in range(2)]
+    devices = [Device.open(device_ordinal=0) for _ in range(2)]
+    plans: list[PreparedW8A8Linear] = []
+    try:
+        plans = [PreparedW8A8Linear(d, QuantizedMatrixInt8(values, scales), max_batch=rows, bias=bias) for d in devices]
+        results: list[np.ndarray | None] = [None, None]
+        errors: list[BaseException] = []
+        start = threading.Barrier(2)
+
+        def run(index: int) -> None:
+            try:
+                start.wait(timeout=60)
+                for _ in range(3):
+                    results[index] = plans[index].execute_host(sources[index])
+            except BaseException as error:  # noqa: BLE001 - reported below
+                errors.append(error)
+
+        threads = [threading.Thread(target=run, args=(index,)) for index in range(2)]
+        for thread in threads:
+            thread.start()
+        for thread in threads:
+            thread.join(timeout=300)
+        assert not any(thread.is_alive() for thread in threads) and not errors, errors
+        for index in range(2):
+            result = results[index]
+            assert result is not None
+            for part in (slice(0, 64), slice(rows - 64, rows)):
+                expected = oracle.w8a8_linear(sources[index][part], values, scales, bias)
+                np.testing.assert_array_equal(result[part], expected)
+            np.testing.assert_array_equal(result, plans[index].execute_host(sources[index]))
+    finally:
+        for plan in plans:
+            plan.close()
+        for device in devices:
+            device.close()
+
+
 def test_plan_binding_and_in_flight_rules(cuda_device: Device) -> None:
     from qpu_xla import DependencyError
 

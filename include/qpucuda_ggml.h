@@ -64,8 +64,8 @@ typedef struct qpucuda_ggml_stats {
     uint32_t rows;            /* M of the last call */
 } qpucuda_ggml_stats;
 
-/* 1 when the node is a MUL_MAT this offload computes: weight Q4_0 [K, N, 1, 1] with K % 32 == 0
- * and N % 16 == 0 (N % 4 as well when cpu_repack), activation F32 [K, M, 1, 1] contiguous with
+/* 1 when the node is a MUL_MAT this offload computes: weight Q4_0 [K, N, 1, 1] contiguous with
+ * K % 32 == 0 and N % 16 == 0 (N % 4 as well when cpu_repack), activation F32 [K, M, 1, 1] contiguous with
  * minimum_rows <= M <= maximum_rows and M <= 4 * 65535, destination F32 [N, M] contiguous. */
 int qpucuda_ggml_supports_mul_mat(const qpucuda_ggml_tensor *weight, const qpucuda_ggml_tensor *activation,
                                   const qpucuda_ggml_tensor *destination, uint32_t minimum_rows,

@@ -35,6 +35,13 @@ bool contiguous_f32(const qpucuda_ggml_tensor *t) {
            t->nb[2] == t->nb[1] * static_cast<size_t>(t->ne[1]) && t->nb[3] == t->nb[2] * static_cast<size_t>(t->ne[2]);
 }
 
+// Q4_0 blocks packed row after row ([N][K/32][18 bytes]): the only weight layout the prepare
+// copies from.
+bool contiguous_q4_0(const qpucuda_ggml_tensor *t) {
+    return t->nb[0] == kQ40BlockBytes && t->nb[1] == kQ40BlockBytes * static_cast<size_t>(t->ne[0] / 32) &&
+           t->nb[2] == t->nb[1] * static_cast<size_t>(t->ne[1]) && t->nb[3] == t->nb[2] * static_cast<size_t>(t->ne[2]);
+}
+
 uint64_t now_ns() {
     return static_cast<uint64_t>(
         std::chrono::duration_cast<std::chrono::nanoseconds>(std::chrono::steady_clock::now().time_since_epoch())
@@ -165,8 +172,10 @@ int qpucuda_ggml_supports_mul_mat(const qpucuda_ggml_tensor *weight, const qpucu
     const bool result = destination->type == QPUCUDA_GGML_TYPE_F32 && destination->ne[0] == weight->ne[1] &&
                         destination->ne[1] == activation->ne[1] && destination->ne[2] == 1 &&
                         destination->ne[3] == 1 && contiguous_f32(destination);
-    // unpack_q4_0_4x4 needs whole 4-row groups (ggml-qpu.cpp:257-261)
-    const bool layout = weight->cpu_repack == 0 || weight->ne[1] % 4 == 0;
+    // unpack_q4_0_4x4 needs whole 4-row groups (ggml-qpu.cpp:257-261). The weight must also be
+    // contiguous, which the reference assumes without checking: a strided view falls back to
+    // another backend here instead of being read as packed blocks.
+    const bool layout = (weight->cpu_repack == 0 || weight->ne[1] % 4 == 0) && contiguous_q4_0(weight);
     // the device's row window (ggml-qpu.cpp:631-633)
     const bool window = activation->ne[1] >= static_cast<int64_t>(minimum_rows) &&
                         activation->ne[1] <= static_cast<int64_t>(maximum_rows);

@@ -376,6 +376,14 @@ def ggml_tensor_view(
 ) -> Any:
     """A ``qpucuda_ggml_tensor`` over a host array: F32 ``[M, K]`` rows, or Q4_0 weight blocks
     ``[N, K/32, 18]`` (native) / the same bytes in block_q4_0x4 groups (``cpu_repack``)."""
+    if not array.flags.c_contiguous:
+        raise ValueError("ggml tensor view needs a C-contiguous array")
+    if ggml_type == _native.GGML_TYPE_F32 and (array.dtype != np.float32 or array.ndim != 2):
+        raise ValueError(f"F32 view needs a float32 [M, K] array, got {array.dtype} {array.shape}")
+    if ggml_type == _native.GGML_TYPE_Q4_0 and (
+        array.dtype != np.uint8 or array.ndim != 3 or array.shape[2] != Q4_0_BLOCK_BYTES
+    ):
+        raise ValueError(f"Q4_0 view needs uint8 [N, K/32, {Q4_0_BLOCK_BYTES}] blocks, got {array.dtype} {array.shape}")
     view = _native.GgmlTensor()
     view.type = ggml_type
     view.cpu_repack = 1 if cpu_repack else 0

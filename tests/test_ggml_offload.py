@@ -44,6 +44,8 @@ def test_supported_node() -> None:
         lambda w, a, d: w.ne.__setitem__(2, 2),  # batched weight
         lambda w, a, d: a.ne.__setitem__(3, 2),  # batched activation
         lambda w, a, d: a.nb.__setitem__(1, a.nb[1] + 16),  # activation rows not contiguous
+        lambda w, a, d: w.nb.__setitem__(1, w.nb[1] + 18),  # weight rows not packed back to back
+        lambda w, a, d: w.nb.__setitem__(0, 34),  # weight blocks are not Q4_0-sized
         lambda w, a, d: d.ne.__setitem__(0, 16),  # destination is not [N, M]
         lambda w, a, d: d.nb.__setitem__(0, 8),  # destination not contiguous
         lambda w, a, d: setattr(d, "data", None),  # no destination memory
@@ -53,6 +55,19 @@ def test_unsupported_nodes(mutate) -> None:  # type: ignore[no-untyped-def]
     _, (w, a, d) = _views()
     mutate(w, a, d)
     assert not ggml_supports_mul_mat(w, a, d)
+
+
+def test_views_reject_arrays_they_cannot_describe() -> None:
+    arrays, _ = _views()
+    weight, activation, _ = arrays
+    with pytest.raises(ValueError, match="C-contiguous"):
+        ggml_tensor_view(activation[:, ::2], _native.GGML_TYPE_F32)
+    with pytest.raises(ValueError, match="C-contiguous"):
+        ggml_tensor_view(weight[::2], _native.GGML_TYPE_Q4_0)
+    with pytest.raises(ValueError, match="float32"):
+        ggml_tensor_view(activation.astype(np.float64), _native.GGML_TYPE_F32)
+    with pytest.raises(ValueError, match="uint8"):
+        ggml_tensor_view(weight.reshape(weight.shape[0], -1), _native.GGML_TYPE_Q4_0)
 
 
 def test_row_window() -> None:

@@ -144,8 +144,14 @@ qpucuda_status get_or_prepare(qpucuda_ggml_backend *backend, const qpucuda_ggml_
     qpucuda_q4_0_linear *prepared = nullptr;
     const qpucuda_status status = qpucuda_q4_0_linear_prepare(backend->context, &desc, &prepared);
     if (status != QPUCUDA_OK) return status;
+    try {
+        backend->linears.emplace(key, CachedLinear{prepared, rows, weight->data, weight->ne[0], weight->ne[1],
+                                                   weight->cpu_repack});
+    } catch (...) {
+        qpucuda_q4_0_linear_destroy(prepared);  // no exception crosses the C ABI
+        return fail(backend->context, QPUCUDA_ALLOCATION_FAILED, "GGML offload: weight cache entry");
+    }
     ++backend->stats.weight_cache_misses;
-    backend->linears.emplace(key, CachedLinear{prepared, rows, weight->data, weight->ne[0], weight->ne[1], weight->cpu_repack});
     *result = prepared;
     return QPUCUDA_OK;
 }

@@ -122,6 +122,7 @@ const char *qpucuda_q4_0_kernel_source_hash(void) { return QPUCUDA_Q4_0_SOURCE_H
 
 qpucuda_status qpucuda_q4_0_linear_prepare(qpucuda_context *context, const qpucuda_q4_0_linear_desc *desc,
                                            qpucuda_q4_0_linear **result) {
+    if (result != nullptr) *result = nullptr;
     // Argument rules of qpu_llama_q4_0_linear_prepare (qpu_llama_q4_0.c:205-225).
     if (context == nullptr || desc == nullptr || result == nullptr || desc->weights == nullptr ||
         desc->expected_source_hash == nullptr || desc->rows == 0 || desc->rows > 4u * UINT16_MAX ||

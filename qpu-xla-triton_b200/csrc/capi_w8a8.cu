@@ -76,20 +76,28 @@ void free_linear(qpucuda_w8a8_linear *linear) {
 constexpr uint32_t kSliceRows = 1024;
 
 bool ensure_pipeline(qpucuda_w8a8_linear *linear, uint32_t slices) {
-    if (linear->copy_in == nullptr &&
-        (cudaStreamCreateWithFlags(&linear->copy_in, cudaStreamNonBlocking) != cudaSuccess ||
-         cudaStreamCreateWithFlags(&linear->copy_out, cudaStreamNonBlocking) != cudaSuccess)) {
-        (void)cudaGetLastError();
-        return false;
+    // Each stream on its own: after a failed creation the other stays usable, and a null handle
+    // (the legacy default stream) is never used as a copy stream.
+    for (cudaStream_t *stream : {&linear->copy_in, &linear->copy_out}) {
+        if (*stream == nullptr && cudaStreamCreateWithFlags(stream, cudaStreamNonBlocking) != cudaSuccess) {
+            *stream = nullptr;
+            (void)cudaGetLastError();
+            return false;
+        }
     }
     const size_t needed = 2u * slices + 2u;
+    try {
+        linear->events.reserve(needed);
+    } catch (...) {
+        return false;  // no exception crosses the C ABI
+    }
     while (linear->events.size() < needed) {
         cudaEvent_t event = nullptr;
         if (cudaEventCreateWithFlags(&event, cudaEventDisableTiming) != cudaSuccess) {
             (void)cudaGetLastError();
             return false;
         }
-        linear->events.push_back(event);
+        linear->events.push_back(event);  // capacity reserved above: does not throw
     }
     return true;
 }

@@ -48,16 +48,22 @@ void parallel_memcpy(void *destination, const void *source, size_t bytes) {
         return;
     }
     const size_t chunk = (bytes + workers - 1) / workers;
-    std::vector<std::thread> threads;
-    threads.reserve(workers);
-    for (size_t i = 0; i < workers; ++i) {
-        const size_t begin = i * chunk;
-        if (begin >= bytes) break;
+    auto copy_chunk = [=](size_t index) {
+        const size_t begin = index * chunk;
+        if (begin >= bytes) return;
         const size_t length = begin + chunk <= bytes ? chunk : bytes - begin;
-        threads.emplace_back([=]() {
-            std::memcpy(static_cast<uint8_t *>(destination) + begin, static_cast<const uint8_t *>(source) + begin, length);
-        });
+        std::memcpy(static_cast<uint8_t *>(destination) + begin, static_cast<const uint8_t *>(source) + begin, length);
+    };
+    std::vector<std::thread> threads;
+    size_t started = 0;
+    try {
+        threads.reserve(workers);
+        for (; started < workers; ++started) threads.emplace_back(copy_chunk, started);
+    } catch (...) {
+        // No thread or memory to spare: nothing may throw across the C ABI, so the chunks that
+        // found no thread are copied by the caller's thread below.
     }
+    for (size_t index = started; index < workers; ++index) copy_chunk(index);
     for (auto &thread : threads) thread.join();
 }
 

@@ -427,6 +427,36 @@ def run_ours(args: argparse.Namespace) -> None:
     q4_gbs = q4_total_bytes / q4_seconds / 1e9
     q4_rank_gbs = q4_bytes_rank / (q4_step_ms * 1e-3) / 1e9
 
+    # ---- W8A8 decode (rows <= 8 take the int8 GEMV): the prefill plans at M = 1 and M = 8,
+    # fp32 rows on the device (row quantizer + GEMV per projection), L2 flushed per bracket.
+    # Algorithmic bytes per projection: N*K weights + M*K activations + 4(N + M + M*N). ----
+    w8a8_gemv: dict[str, dict[str, float]] = {}
+    for gemv_rows in (1, 8):
+
+        def decode_w8a8(rows: int = gemv_rows) -> None:
+            for p in projections:
+                p["plan"].forward(p["source"][:rows], out=p["local"][:rows, : p["gather"].count])
+
+        gemv_bytes_rank = sum(
+            float(p["gather"].count) * p["k"] + gemv_rows * p["k"] + 4.0 * (p["gather"].count + gemv_rows + gemv_rows * p["gather"].count)
+            for p in projections
+        )
+        for _ in range(3):
+            decode_w8a8()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for s, e in evs:
+            prime()
+            s.record(stream)
+            decode_w8a8()
+            e.record(stream)
+        torch.cuda.synchronize()
+        gemv_step_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in evs))
+        w8a8_gemv[str(gemv_rows)] = {
+            "value": round(sum_over_ranks(gemv_bytes_rank) / (gemv_step_ms * 1e-3) / 1e9, 1),
+            "rank_gbs": round(gemv_bytes_rank / (gemv_step_ms * 1e-3) / 1e9, 1),
+            "us_per_decode_ffn": round(gemv_step_ms * 1e3, 2),
+        }
+
     clocks = sampler.stop() if rank == 0 else {}
 
     # ---- end to end through the C-ABI with host (pinned) buffers ----
@@ -526,6 +556,22 @@ def run_ours(args: argparse.Namespace) -> None:
             },
             "us_per_decode_ffn": round(q4_step_ms * 1e3, 2),
             "us_per_projection_alone": [round(x * 1e3, 2) for x in q4_ms],
+        },
+        "w8a8_gemv": {
+            "metric": "W8A8 decode GB/s (whole job), one FFN step (gate, up, down: row quantizer + int8 GEMV) per bracket, at M = 1 and M = 8",
+            "value": w8a8_gemv["1"]["value"],
+            "unit": "GB/s",
+            "rows": w8a8_gemv,
+            "roofline": {
+                "kernel": "w8a8_gemv_kernel (dp4a, persistent balanced grid, split-K across a CTA's warps, next column's first loads issued before the reduction at M <= 2)",
+                "bound": "hbm",
+                "achieved": w8a8_gemv["1"]["rank_gbs"],
+                "peak": peaks["hbm_gbs"],
+                "unit": "GB/s",
+                "frac": round(w8a8_gemv["1"]["rank_gbs"] / peaks["hbm_gbs"], 4),
+                "peak_source": f"{peak_kind} STREAM-style copy",
+                "traffic": None,
+            },
         },
         "clocks": clocks,
     }

@@ -165,6 +165,7 @@ class PreparedW8A8Linear:
         self._native.check(status, "qpucuda_w8a8_linear_prepare")
         self._handle = int(handle.value)  # type: ignore[arg-type]
         self._queue: Queue | None = None
+        self._cpu_queue: Queue | None = None
         self._last_event: Event | None = None
         self._closed = False
 
@@ -269,6 +270,38 @@ class PreparedW8A8Linear:
         )
         self._last_event = event
         return event
+
+    def execute_hybrid(
+        self: Self,
+        destination: Tensor,
+        source: Tensor,
+        *,
+        qpu_queue: Queue,
+        cpu_queue: Queue,
+        qpu_outputs: int,
+        wait_for: Iterable[Event] = (),
+    ) -> Event:
+        """The aligned output prefix / disjoint tail split (quantization.py:350-514) with the
+        reference's argument rules: two distinct queues of the plan device, each bound on first
+        use, and ``qpu_outputs`` a positive multiple of 16 below the output count. Both parts run
+        on the GPU here (this build has no CPU compute path). The reference computes its two parts
+        with the same exact arithmetic, so the output is the whole linear either way;
+        ``cpu_queue`` is validated and bound but receives no work."""
+        if self._closed:
+            raise RuntimeError("prepared W8A8 linear plan is closed")
+        if self._last_event is not None and not self._last_event.done:
+            raise RuntimeError("prepared W8A8 linear plan already has an in-flight invocation")
+        if qpu_queue is cpu_queue:
+            raise DependencyError("hybrid W8A8 linear requires distinct CPU and QPU queues")
+        if qpu_queue.device is not self.device or cpu_queue.device is not self.device:
+            raise DependencyError("hybrid W8A8 queues must belong to the plan device")
+        if self._cpu_queue is None:
+            self._cpu_queue = cpu_queue
+        elif self._cpu_queue is not cpu_queue:
+            raise DependencyError("prepared W8A8 linear plan is bound to its first CPU queue")
+        if qpu_outputs <= 0 or qpu_outputs >= self.output_count or qpu_outputs % 16:
+            raise ValueError("hybrid W8A8 qpu_outputs must be aligned and leave a non-empty CPU tail")
+        return self.execute(destination, source, queue=qpu_queue, wait_for=wait_for)
 
     def execute_prepared(self: Self, destination: Tensor, *, batch: int, queue: Queue, wait_for: Iterable[Event] = ()) -> Event:
         """Run on activations already quantized into the plan scratch (quantization.py:325-348)."""

@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 
 from oracle import qpu_oracle as oracle
-from qpu_xla import AccessMode, Device, EventStatus, Placement, workloads
+from qpu_xla import AccessMode, DependencyError, Device, EventStatus, Placement, workloads
 from qpu_xla.candidates import CandidateRegistry
 from qpu_xla.ggml import PreparedQ4_0Linear, quantize_q8_0
 from qpu_xla.kernels import (
@@ -65,6 +65,26 @@ def test_prepared_linear_on_a_queue_matches_the_reference(cuda_device: Device, g
         np.testing.assert_array_equal(one_out.numpy(), ref["output"][:1])
         # host-buffer C-ABI path of the same plan
         np.testing.assert_array_equal(plan.execute_host(case.source), ref["output"])
+
+
+def test_execute_hybrid_computes_both_parts_on_the_gpu(cuda_device: Device, golden: dict) -> None:
+    """quantization.py:350-514: the aligned prefix and the tail both run on the GPU here, so the
+    output is the reference's whole result (its two parts share one exact arithmetic)."""
+    ref = golden["w8a8_square_512"]
+    case = workloads.square_case(512)
+    weight = QuantizedMatrixInt8(ref["weight_values"], ref["weight_scales"])
+    with cuda_device.queue() as gpu_queue, cuda_device.queue() as cpu_queue, PreparedW8A8Linear(
+        cuda_device, weight, max_batch=512, bias=ref["bias"]
+    ) as plan:
+        source = cuda_device.tensor((512, 512), np.float32)
+        destination = cuda_device.tensor((512, 512), np.float32)
+        source.write(case.source)
+        with pytest.raises(DependencyError):
+            plan.execute_hybrid(destination, source, qpu_queue=gpu_queue, cpu_queue=gpu_queue, qpu_outputs=256)
+        with pytest.raises(ValueError):
+            plan.execute_hybrid(destination, source, qpu_queue=gpu_queue, cpu_queue=cpu_queue, qpu_outputs=100)
+        plan.execute_hybrid(destination, source, qpu_queue=gpu_queue, cpu_queue=cpu_queue, qpu_outputs=256).wait()
+        np.testing.assert_array_equal(destination.numpy(), ref["output"])
 
 
 def test_host_execute_of_a_large_batch_is_sliced_and_exact(cuda_device: Device) -> None:

@@ -9,9 +9,9 @@ rows) with the dequant (+bias) epilogue fused. There is no CPU execution path:
 ``qpu_dequantize`` / ``fuse_dequantize`` are accepted for signature
 compatibility, and the dequantization always runs fused on the GPU.
 
-The reference's CPU/QPU hybrid splits (``execute_hybrid*``) have no counterpart
-here; their output-channel split is :class:`qpu_xla.sharded.ShardedW8A8Linear`
-across GPUs.
+The reference's CPU/QPU hybrid splits (``execute_hybrid*``) keep their calls and
+argument rules, with both parts on the GPU; an output-channel split across GPUs
+is :class:`qpu_xla.sharded.ShardedW8A8Linear`.
 """
 
 from __future__ import annotations
@@ -271,6 +271,37 @@ class PreparedW8A8Linear:
         self._last_event = event
         return event
 
+    def _bind_hybrid_queues(self: Self, qpu_queue: Queue, cpu_queue: Queue) -> None:
+        """The reference's queue rules for every hybrid split (quantization.py:361-375, 717-732):
+        an open plan with nothing in flight, two distinct queues of the plan device, each bound to
+        the plan on first use."""
+        if self._closed:
+            raise RuntimeError("prepared W8A8 linear plan is closed")
+        if self._last_event is not None and not self._last_event.done:
+            raise RuntimeError("prepared W8A8 linear plan already has an in-flight invocation")
+        if qpu_queue is cpu_queue:
+            raise DependencyError("hybrid W8A8 linear requires distinct CPU and QPU queues")
+        if qpu_queue.device is not self.device or cpu_queue.device is not self.device:
+            raise DependencyError("hybrid W8A8 queues must belong to the plan device")
+        if self._queue is None:
+            self._queue = qpu_queue
+        elif self._queue is not qpu_queue:
+            raise DependencyError("prepared W8A8 linear plan is bound to its first QPU queue")
+        if self._cpu_queue is None:
+            self._cpu_queue = cpu_queue
+        elif self._cpu_queue is not cpu_queue:
+            raise DependencyError("prepared W8A8 linear plan is bound to its first CPU queue")
+
+    def _check_hybrid_units(self: Self, name: str, units: int, total: int) -> None:
+        if units <= 0 or units >= total or units % 16:
+            raise ValueError(f"hybrid W8A8 {name} must be aligned and leave a non-empty CPU tail")
+
+    # The reference's CPU/QPU splits (quantization.py:350-514, 516-662, 664-878) keep their calls
+    # and argument rules here, and both parts of every split run on the GPU: this build has no CPU
+    # compute path. The reference computes its two parts with the same exact arithmetic (rows are
+    # quantized independently, output channels are independent), so the output is the whole
+    # linear either way; ``cpu_queue`` is validated and bound but receives no work.
+
     def execute_hybrid(
         self: Self,
         destination: Tensor,
@@ -281,27 +312,47 @@ class PreparedW8A8Linear:
         qpu_outputs: int,
         wait_for: Iterable[Event] = (),
     ) -> Event:
-        """The aligned output prefix / disjoint tail split (quantization.py:350-514) with the
-        reference's argument rules: two distinct queues of the plan device, each bound on first
-        use, and ``qpu_outputs`` a positive multiple of 16 below the output count. Both parts run
-        on the GPU here (this build has no CPU compute path). The reference computes its two parts
-        with the same exact arithmetic, so the output is the whole linear either way;
-        ``cpu_queue`` is validated and bound but receives no work."""
-        if self._closed:
-            raise RuntimeError("prepared W8A8 linear plan is closed")
-        if self._last_event is not None and not self._last_event.done:
-            raise RuntimeError("prepared W8A8 linear plan already has an in-flight invocation")
-        if qpu_queue is cpu_queue:
-            raise DependencyError("hybrid W8A8 linear requires distinct CPU and QPU queues")
-        if qpu_queue.device is not self.device or cpu_queue.device is not self.device:
-            raise DependencyError("hybrid W8A8 queues must belong to the plan device")
-        if self._cpu_queue is None:
-            self._cpu_queue = cpu_queue
-        elif self._cpu_queue is not cpu_queue:
-            raise DependencyError("prepared W8A8 linear plan is bound to its first CPU queue")
-        if qpu_outputs <= 0 or qpu_outputs >= self.output_count or qpu_outputs % 16:
-            raise ValueError("hybrid W8A8 qpu_outputs must be aligned and leave a non-empty CPU tail")
+        """An aligned output-channel prefix and the disjoint tail (quantization.py:350-514)."""
+        self._bind_hybrid_queues(qpu_queue, cpu_queue)
+        self._check_hybrid_units("qpu_outputs", qpu_outputs, self.output_count)
         return self.execute(destination, source, queue=qpu_queue, wait_for=wait_for)
+
+    def execute_hybrid_rows(
+        self: Self,
+        destination: Tensor,
+        source: Tensor,
+        *,
+        qpu_queue: Queue,
+        cpu_queue: Queue,
+        qpu_rows: int,
+        wait_for: Iterable[Event] = (),
+    ) -> Event:
+        """An aligned row prefix and the disjoint tail (quantization.py:516-662)."""
+        self._bind_hybrid_queues(qpu_queue, cpu_queue)
+        if len(source.shape) != 2:
+            raise ValueError("prepared W8A8 linear requires rank-2 source and destination")
+        self._check_hybrid_units("qpu_rows", qpu_rows, source.shape[0])
+        return self.execute(destination, source, queue=qpu_queue, wait_for=wait_for)
+
+    def execute_prepared_hybrid_rows(
+        self: Self, destination: Tensor, *, batch: int, qpu_queue: Queue, cpu_queue: Queue, qpu_rows: int, wait_for: Iterable[Event] = ()
+    ) -> Event:
+        """The row split over activations already in the plan scratch (quantization.py:664-683)."""
+        self._bind_hybrid_queues(qpu_queue, cpu_queue)
+        if batch <= 0 or batch > self.max_batch:
+            raise ValueError("prepared W8A8 linear batch exceeds the plan shape")
+        self._check_hybrid_units("qpu_rows", qpu_rows, batch)
+        return self.execute_prepared(destination, batch=batch, queue=qpu_queue, wait_for=wait_for)
+
+    def execute_prepared_hybrid_outputs(
+        self: Self, destination: Tensor, *, batch: int, qpu_queue: Queue, cpu_queue: Queue, qpu_outputs: int, wait_for: Iterable[Event] = ()
+    ) -> Event:
+        """The output split over activations already in the plan scratch (quantization.py:685-704)."""
+        self._bind_hybrid_queues(qpu_queue, cpu_queue)
+        if batch <= 0 or batch > self.max_batch:
+            raise ValueError("prepared W8A8 linear batch exceeds the plan shape")
+        self._check_hybrid_units("qpu_outputs", qpu_outputs, self.output_count)
+        return self.execute_prepared(destination, batch=batch, queue=qpu_queue, wait_for=wait_for)
 
     def execute_prepared(self: Self, destination: Tensor, *, batch: int, queue: Queue, wait_for: Iterable[Event] = ()) -> Event:
         """Run on activations already quantized into the plan scratch (quantization.py:325-348)."""

@@ -4,7 +4,8 @@
 Workload (the configuration the metric is quoted on
 "at 1/2/4/8 GPUs"): the Llama-2-70B FFN at prefill, M = 4096 tokens, W8A8
 dynamic linear for gate (8192->28672), up (8192->28672) and down (28672->8192);
-plus the Q4_0 x Q8_0 decode matvec (M = 1) on the same three shapes. Weights are
+plus, as objects of the same line, the Q4_0 x Q8_0 decode matvec (M = 1) and the
+W8A8 decode (the same plans at M = 1 and 8, int8 GEMV) on the same three shapes. Weights are
 random-init ~N(0, 0.02), activations ~N(0, 1), drawn on the GPU from a fixed
 seed (identical on every rank). Each projection's output channels (N) are split
 across the ranks; N = 1 runs the identical inputs unsplit.

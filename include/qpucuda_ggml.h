@@ -15,8 +15,9 @@
  *     quantizes the F32 rows to Q8_0 on the CPU first, this build copies the F32 rows to the
  *     device and quantizes them inside the matvec (rows <= 4) or the tensor-core tiled path
  *     (rows > 4); the destination is written only after a successful bounded wait.
- * The ggml glue a maintainer adds (backend/device/buffer-type registration, graph_compute's
- * node loop) is shown in INTEGRATION.md.
+ * The ggml glue a maintainer adds on top (backend/device/buffer-type registration and
+ * graph_compute's node loop, which calls qpucuda_ggml_supports_mul_mat and
+ * qpucuda_ggml_mul_mat per node) needs llama.cpp's own headers and is not part of this library.
  */
 #ifndef QPUCUDA_GGML_H
 #define QPUCUDA_GGML_H

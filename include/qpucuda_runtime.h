@@ -100,6 +100,20 @@ qpucuda_status qpucuda_context_synchronize(qpucuda_context *context);
 /* 1 when a failed wait poisoned the context. */
 int qpucuda_context_poisoned(const qpucuda_context *context);
 
+/* Device-side check of the wait-expiry path. Launches one CTA on the context
+ * stream that waits, bounded by wait_limit_ns (1 .. 1e9 ns), on an mbarrier
+ * nothing arrives at -- the same bounded wait every tcgen05 / bulk-copy barrier
+ * wait of this library uses -- so the wait runs out, the kernel records the
+ * expiry in the context's error word and returns. The call then waits for the
+ * stream as every operator does and returns what an operator whose kernel wait
+ * expired returns: QPUCUDA_TIMEOUT, with the context poisoned. No fault, trap or
+ * unbounded wait is involved, so the CUDA device stays usable and a new context
+ * on it runs normally. The reference checks this path only by host injection
+ * (QPU_LLAMA_FAIL_WAIT, integrations/llama_cpp/tests/
+ * qpu_llama_native_safety_smoke.c:655-669; poisoning at qpu_llama_runtime.c:616-619);
+ * this entry point has no counterpart in its C API. */
+qpucuda_status qpucuda_context_probe_wait_expiry(qpucuda_context *context, uint64_t wait_limit_ns);
+
 /* qpu_llama_status_string (qpu_llama_runtime.h:133). */
 const char *qpucuda_status_string(qpucuda_status status);
 /* Library build identity: "<version> sm_100a". */

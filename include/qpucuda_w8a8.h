@@ -139,7 +139,9 @@ qpucuda_status qpucuda_w8a8_linear_scratch(
     const float **row_scales);
 
 /* Size of the fixed device scratch used by qpucuda_w8a8_linear_execute_static
- * (16 MiB, held by every GPU that loads this library until the process exits). */
+ * (16 MiB per GPU, reserved when the library's module is loaded on that GPU --
+ * at the latest by the entry point's first call there -- and held until the
+ * process exits). */
 #define QPUCUDA_STATIC_SCRATCH_BYTES (16u * 1024u * 1024u)
 
 /* W8A8 linear that allocates nothing. This entry point has no counterpart in
@@ -161,15 +163,20 @@ qpucuda_status qpucuda_w8a8_linear_scratch(
  * library: rows * (k rounded up to 16) bytes, rounded up to 256, plus 4 * rows
  * bytes must fit in QPUCUDA_STATIC_SCRATCH_BYTES (e.g. 1024 rows at k = 8192);
  * larger requests return QPUCUDA_INVALID_ARGUMENT with the reason in
- * qpucuda_context_last_error. Nothing is allocated: no cudaMalloc, cudaFree or
- * allocating library routine is called.
+ * qpucuda_context_last_error. No cudaMalloc, cudaFree or allocating library
+ * routine is called.
  *
- * The first call on each device looks up the array's device address
- * (cudaGetSymbolAddress, with that device current); make that first call
- * before any stream capture. All calls share the one array and it keeps the
- * last call's contents; each call rewrites every byte it later reads, so
- * nothing needs clearing, but calls whose work overlaps on the GPU (different
- * streams, or different contexts on one device) race on the array. */
+ * The first call on each device (in each CUDA context of it) is the set-up: it
+ * looks up the array's device address (cudaGetSymbolAddress, with that device
+ * current) and loads and configures every kernel this entry point can launch.
+ * Under CUDA's lazy module loading that set-up can allocate device memory, so
+ * make the first call at start-up: outside any region where allocation is
+ * forbidden, and before any stream capture. Later calls allocate nothing. After
+ * a device reset the next call repeats the set-up. All calls share the one
+ * array and it keeps the last call's contents; each call rewrites every byte it
+ * later reads, so nothing needs clearing, but calls whose work overlaps on the
+ * GPU (different streams, or different contexts on one device) race on the
+ * array. */
 qpucuda_status qpucuda_w8a8_linear_execute_static(
     qpucuda_context *context,
     const float *source,

@@ -12,7 +12,10 @@
 //
 // The array's host-side name is not a device address: at set-up, once per
 // device, with that device current, cudaGetSymbolAddress yields the address the
-// kernels get. That set-up happens inside the first call on each device.
+// kernels get. That set-up happens inside the first call on each device, which
+// also loads and configures every kernel the entry point can launch; it may
+// allocate (CUDA's lazy module loading), so make that first call at start-up,
+// outside any region where allocation is forbidden and before any stream capture.
 #include <climits>
 #include <mutex>
 
@@ -27,23 +30,74 @@ namespace {
 static __device__ __align__(256) uint8_t g_static_scratch[QPUCUDA_STATIC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-std::mutex g_setup_mutex;
-uint8_t *g_scratch_address[kMaxDevices] = {};
 
+// Per device: the array's address and the id of the CUDA context it was resolved in. A device
+// reset (or a released and re-created primary context) gives a new context id, and the set-up
+// runs again there instead of handing the kernels an address of the old context.
+struct ScratchSlot {
+    unsigned long long context_id = 0;
+    uint8_t *address = nullptr;
+};
+std::mutex g_setup_mutex;
+ScratchSlot g_slots[kMaxDevices];
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext *);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long *);
+
+template <typename Fn>
+Fn driver_function(const char *name) {
+    void *pointer = nullptr;
+    cudaDriverEntryPointQueryResult query;
+    if (cudaGetDriverEntryPoint(name, &pointer, cudaEnableDefault, &query) != cudaSuccess ||
+        query != cudaDriverEntryPointSuccess) {
+        (void)cudaGetLastError();
+        return nullptr;
+    }
+    return reinterpret_cast<Fn>(pointer);
+}
+
+// Id of the context current on this thread; false when none is bound yet (or the driver lacks
+// the query), in which case the set-up simply runs again.
+bool current_context_id(unsigned long long *id) {
+    static const CtxGetCurrentFn get_current = driver_function<CtxGetCurrentFn>("cuCtxGetCurrent");
+    static const CtxGetIdFn get_id = driver_function<CtxGetIdFn>("cuCtxGetId");
+    CUcontext context = nullptr;
+    if (get_current == nullptr || get_id == nullptr || get_current(&context) != CUDA_SUCCESS || context == nullptr) {
+        return false;
+    }
+    return get_id(context, id) == CUDA_SUCCESS;
+}
+
+// The scratch address for the context's device (current, via DeviceGuard), set up on first use
+// in each CUDA context: symbol lookup, then every kernel variant loaded and configured.
 qpucuda_status scratch_address(qpucuda_context *context, uint8_t **address) {
     if (context->device < 0 || context->device >= kMaxDevices) {
         return fail(context, QPUCUDA_CAPABILITY_MISSING, "no-alloc W8A8 linear: device ordinal beyond %d", kMaxDevices);
     }
+    unsigned long long id = 0;
+    bool have_id = current_context_id(&id);
     std::lock_guard<std::mutex> lock(g_setup_mutex);
-    if (g_scratch_address[context->device] == nullptr) {
-        void *pointer = nullptr;
-        const cudaError_t error = cudaGetSymbolAddress(&pointer, g_static_scratch);  // device is current (DeviceGuard)
-        if (error != cudaSuccess || pointer == nullptr) {
-            return cuda_fail(context, error, "no-alloc W8A8 linear: cudaGetSymbolAddress", QPUCUDA_DEVICE_UNAVAILABLE);
-        }
-        g_scratch_address[context->device] = static_cast<uint8_t *>(pointer);
+    ScratchSlot &slot = g_slots[context->device];
+    if (have_id && slot.address != nullptr && slot.context_id == id) {
+        *address = slot.address;
+        return QPUCUDA_OK;
     }
-    *address = g_scratch_address[context->device];
+    void *pointer = nullptr;
+    cudaError_t error = cudaGetSymbolAddress(&pointer, g_static_scratch);
+    if (error != cudaSuccess || pointer == nullptr) {
+        return cuda_fail(context, error, "no-alloc W8A8 linear: cudaGetSymbolAddress", QPUCUDA_DEVICE_UNAVAILABLE);
+    }
+    error = preload_quantize_rows_int8();
+    if (error == cudaSuccess) error = preload_w8a8_gemv();
+    if (error == cudaSuccess && context->cc_major == 10 && context->cc_minor == 0)
+        error = preload_w8a8_gemm_sm100(context->sm_count);
+    if (error != cudaSuccess) {
+        return cuda_fail(context, error, "no-alloc W8A8 linear: kernel set-up", QPUCUDA_DEVICE_UNAVAILABLE);
+    }
+    if (!have_id) have_id = current_context_id(&id);  // the lookup above bound the context
+    slot.context_id = have_id ? id : 0;
+    slot.address = have_id ? static_cast<uint8_t *>(pointer) : nullptr;  // no id: set up again next call
+    *address = static_cast<uint8_t *>(pointer);
     return QPUCUDA_OK;
 }
 

@@ -110,6 +110,13 @@ bool encode_tensor_map_2d_b32(CUtensorMap *map, const void *base, uint64_t colum
 
 // ---- kernel launchers (one per .cu file) -------------------------------------------------
 
+// Load (under CUDA's lazy module loading) and configure every kernel variant the row quantizer,
+// the W8A8 GEMV and the tcgen05 GEMM launchers can pick, on the current device, and fill their
+// cached occupancy figures, so later launches of them do no first-use set-up.
+cudaError_t preload_quantize_rows_int8();
+cudaError_t preload_w8a8_gemv();
+cudaError_t preload_w8a8_gemm_sm100(int sm_count);
+
 // Many long aligned rows take a bulk-copy staged kernel whose bounded waits report through
 // error_word (the context's error word); with error_word null the register-cached kernel runs.
 cudaError_t launch_quantize_rows_int8(const float *x, size_t x_stride, uint32_t rows, uint32_t cols,

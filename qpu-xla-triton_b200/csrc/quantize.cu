@@ -336,19 +336,25 @@ namespace {
 // Usable dynamic shared memory per CTA on sm_100 (227 KB) less the static scratch and mbarriers.
 constexpr size_t kStagedSmemBudget = 227u * 1024u - 512u;
 
+// The staged kernel's shared-memory attribute is raised to the whole budget once per device, so
+// every row length fits; 1024 threads and at least half the shared memory per CTA leave one CTA
+// per SM.
+template <int THREADS, int STAGES>
+cudaError_t configure_staged() {
+    static PerDeviceOnce configured;
+    return configured.run([] {
+        return cudaFuncSetAttribute(quantize_rows_int8_bulk<THREADS, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kStagedSmemBudget));
+    });
+}
+
 template <int THREADS, int STAGES>
 cudaError_t launch_staged_config(const float *x, size_t x_stride, uint32_t rows, uint32_t cols, uint32_t padded_cols,
                                  int8_t *q, size_t q_stride, float *scales, unsigned int *error_word, int sm_count,
                                  cudaStream_t stream) {
     const size_t smem = static_cast<size_t>(STAGES) * cols * sizeof(float);
     auto kernel = quantize_rows_int8_bulk<THREADS, STAGES>;
-    // The attribute is raised to the whole budget once, so every row length fits; 1024 threads
-    // and at least half the shared memory per CTA leave one CTA per SM.
-    static PerDeviceOnce configured;
-    const cudaError_t error = configured.run([kernel] {
-        return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(kStagedSmemBudget));
-    });
+    const cudaError_t error = configure_staged<THREADS, STAGES>();
     if (error != cudaSuccess) return error;
     const int per_sm = 1;
     const uint64_t slots = static_cast<uint64_t>(sm_count) * static_cast<uint64_t>(per_sm);
@@ -380,6 +386,19 @@ cudaError_t launch_staged(const float *x, size_t x_stride, uint32_t rows, uint32
 }
 
 }  // namespace
+
+cudaError_t preload_quantize_rows_int8() {
+    cudaFuncAttributes attributes;
+    cudaError_t error = configure_staged<1024, 2>();
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, quantize_rows_int8_vec<32, 8>);
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, quantize_rows_int8_vec<64, 8>);
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, quantize_rows_int8_vec<128, 8>);
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, quantize_rows_int8_vec<256, 8>);
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, quantize_rows_int8_vec<512, 8>);
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, quantize_rows_int8_vec<1024, 8>);
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, quantize_rows_int8_generic);
+    return error;
+}
 
 cudaError_t launch_quantize_rows_int8(const float *x, size_t x_stride, uint32_t rows, uint32_t cols,
                                       uint32_t padded_cols, int8_t *q, size_t q_stride, float *scales,

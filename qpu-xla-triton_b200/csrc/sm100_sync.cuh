@@ -52,23 +52,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
-// false when the CTA was aborted or the wait exceeded its bound (the latter records the
-// error and aborts the CTA).
-__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                                             unsigned int *error_word) {
+// false when the CTA was aborted or the wait exceeded limit_ns (the latter records the error
+// and aborts the CTA).
+__device__ __forceinline__ bool wait_bounded_ns(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                                unsigned int *error_word, uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t start = globaltimer();
     for (uint32_t spin = 1;; ++spin) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((spin & 63u) == 0) {
             if (*abort_flag != 0) return false;
-            if (globaltimer() - start > kKernelWaitLimitNs) {
+            if (globaltimer() - start > limit_ns) {
                 *abort_flag = 1;
                 atomicExch(error_word, static_cast<unsigned int>(kKernelWaitTimeout));
                 return false;
             }
         }
     }
+}
+
+// The product kernels' waits: bounded by kKernelWaitLimitNs.
+__device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                             unsigned int *error_word) {
+    return wait_bounded_ns(bar, parity, abort_flag, error_word, kKernelWaitLimitNs);
 }
 
 // Bounded wait that ignores the abort flag (abort path only).

@@ -762,19 +762,34 @@ cudaError_t launch_w8a8_gemm_sm100(const CUtensorMap *map_a, const CUtensorMap *
     return launch_w8a8_gemm_sm100_mode(map_a, map_w, m, n, k, epilogue, error_word, sm_count, pair, stream);
 }
 
-cudaError_t launch_w8a8_gemm_sm100_mode(const CUtensorMap *map_a, const CUtensorMap *map_w, uint32_t m, uint32_t n,
-                                        uint32_t k, const GemmEpilogue &epilogue, unsigned int *error_word,
-                                        int sm_count, bool pair, cudaStream_t stream) {
-    if (m == 0 || n == 0) return cudaSuccess;
-    if (k == 0) return cudaErrorInvalidValue;
+namespace {
+// Shared-memory attribute of every variant, once per device (setting it also loads the kernel
+// under CUDA's lazy module loading).
+cudaError_t configure_all_variants() {
     static PerDeviceOnce configured;
-    const cudaError_t configure_error = configured.run([] {
+    return configured.run([] {
         cudaError_t error = configure_kernel<false, false>();
         if (error == cudaSuccess) error = configure_kernel<true, false>();
         if (error == cudaSuccess) error = configure_kernel<false, true>();
         if (error == cudaSuccess) error = configure_kernel<true, true>();
         return error;
     });
+}
+}  // namespace
+
+cudaError_t preload_w8a8_gemm_sm100(int sm_count) {
+    const cudaError_t error = configure_all_variants();
+    if (error != cudaSuccess) return error;
+    (void)resident_pairs(sm_count);  // the cluster occupancy query, cached per device
+    return cudaSuccess;
+}
+
+cudaError_t launch_w8a8_gemm_sm100_mode(const CUtensorMap *map_a, const CUtensorMap *map_w, uint32_t m, uint32_t n,
+                                        uint32_t k, const GemmEpilogue &epilogue, unsigned int *error_word,
+                                        int sm_count, bool pair, cudaStream_t stream) {
+    if (m == 0 || n == 0) return cudaSuccess;
+    if (k == 0) return cudaErrorInvalidValue;
+    const cudaError_t configure_error = configure_all_variants();
     if (configure_error != cudaSuccess) return configure_error;
     pair = pair && sm_count >= 2;
     GemmParams params;

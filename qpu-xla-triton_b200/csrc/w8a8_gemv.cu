@@ -245,7 +245,29 @@ cudaError_t launch_rows(const GemvParams &p, int sm_count, cudaStream_t stream) 
     return cudaGetLastError();
 }
 
+template <int ROWS>
+cudaError_t preload_rows() {
+    cudaFuncAttributes attributes;
+    cudaError_t error = cudaFuncGetAttributes(&attributes, w8a8_gemv_kernel<ROWS, 1>);
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, w8a8_gemv_kernel<ROWS, 2>);
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, w8a8_gemv_kernel<ROWS, 4>);
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, w8a8_gemv_kernel<ROWS, 8>);
+    (void)resident_ctas<ROWS, 1>();
+    (void)resident_ctas<ROWS, 2>();
+    (void)resident_ctas<ROWS, 4>();
+    (void)resident_ctas<ROWS, 8>();
+    return error;
+}
+
 }  // namespace
+
+cudaError_t preload_w8a8_gemv() {
+    cudaError_t error = preload_rows<1>();
+    if (error == cudaSuccess) error = preload_rows<2>();
+    if (error == cudaSuccess) error = preload_rows<4>();
+    if (error == cudaSuccess) error = preload_rows<8>();
+    return error;
+}
 
 cudaError_t launch_w8a8_gemv(const int8_t *a, size_t a_stride, const int8_t *w, size_t w_stride, uint32_t m,
                              uint32_t n, uint32_t k, const GemmEpilogue &epilogue, int sm_count,

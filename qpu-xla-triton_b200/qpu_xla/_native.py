@@ -197,6 +197,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "qpucuda_context_library_stream": (_P, [_P]),
     "qpucuda_context_synchronize": (_S, [_P]),
     "qpucuda_context_poisoned": (c_int, [_P]),
+    "qpucuda_context_probe_wait_expiry": (_S, [_P, c_uint64]),
     "qpucuda_status_string": (c_char_p, [c_int]),
     "qpucuda_build_info": (c_char_p, []),
     # qpucuda_kernels.h

@@ -1,32 +1,44 @@
 #!/usr/bin/env python3
 """Headline benchmark: W8A8 GEMM TOPS (and Q4_0 GEMV GB/s) at 1/2/4/8 B200s.
 
-Workload (the configuration the metric is quoted on
-"at 1/2/4/8 GPUs"): the Llama-2-70B FFN at prefill, M = 4096 tokens, W8A8
-dynamic linear for gate (8192->28672), up (8192->28672) and down (28672->8192);
-plus, as objects of the same line, the Q4_0 x Q8_0 decode matvec (M = 1) and the
-W8A8 decode (the same plans at M = 1 and 8, int8 GEMV) on the same three shapes. Weights are
-random-init ~N(0, 0.02), activations ~N(0, 1), drawn on the GPU from a fixed
-seed (identical on every rank). Each projection's output channels (N) are split
-across the ranks; N = 1 runs the identical inputs unsplit.
+Headline workload (the configuration the metric is quoted on
+"at 1/2/4/8 GPUs"): the Llama-2-70B FFN at prefill, M = 4096 tokens, W8A8 dynamic
+linear for gate (8192->28672), up (8192->28672) and down (28672->8192). Weights are
+random-init ~N(0, 0.02), activations ~N(0, 1), drawn on the GPU from a fixed seed
+(identical on every rank). Each projection's output channels (N) are split across the
+ranks; N = 1 runs the identical inputs unsplit.
 
-One step = for each projection: quantize the fp32 rows (int8 kernel), tcgen05
-int8 GEMM with the fused dequant epilogue on the rank's column shard, and (N > 1)
-the exchange that leaves the full [M, N] fp32 output on every rank: the GEMM
-epilogue stores each tile into every rank's output buffer (mapped with CUDA IPC)
-over NVLink as it finishes, then a one-element NCCL all-reduce orders all ranks'
-stores (the fused GEMM + all-gather). If the peer mapping is refused, the step
-falls back to an NCCL all-gather after the GEMM and the line says so. L2 is
-flushed between timed steps, outside the
-per-step CUDA-event brackets: a 256 MiB write, then a 256 MiB read of a second
-buffer, so the timed kernels start on a cache of clean lines (as after the
-previous layer's weight stream) rather than paying the write-back of the flush's
-own dirty lines; inputs also exceed L2.
+One step = for each projection: quantize the fp32 rows (int8 row-quantizer kernel) into
+the plan's scratch, then the tcgen05 int8 GEMM with the fused dequant epilogue on the
+rank's column shard, and (N > 1) the exchange that leaves the full [M, N] fp32 output on
+every rank: the GEMM epilogue stores each tile into every rank's output buffer (mapped
+with CUDA IPC) over NVLink as it finishes, then one NCCL all-reduce of one element per
+step orders all ranks' stores (the fused GEMM + all-gather). If the peer mapping is
+refused, the step falls back to an NCCL all-gather after each GEMM and the line says so.
+At N = 1 CUDA events recorded between the quantizer and the GEMM launches inside the
+timed steps give the GEMM's own time, which the roofline uses.
+
+L2 is flushed before every timed bracket, outside it: a 256 MiB write, then a 256 MiB
+read of a second buffer, so the timed kernels start on a cache of clean lines; the
+headline's inputs also exceed L2.
+
+Further objects of the same JSON line time the other configurations at N = 1, each with
+its own roofline (achieved / measured peak / ncu traffic per launch) and the reference's
+CPU path timed on the host beside it:
+  * ``q4_0_gemv`` / ``w8a8_gemv`` -- the decode of configs[4] on the same 70B shapes (Q4_0
+    x Q8_0 at M = 1 and 4; W8A8 int8 GEMV at M = 1 and 8), per rank on its shard;
+  * ``square`` -- configs[0-1], the reference's 64^3 and 512^3 (+bias) W8A8 cases;
+  * ``tinyllama_w8a8`` -- configs[2], all seven projections of one TinyLlama layer at
+    M = 1, 128 and 2048;
+  * ``tinyllama_q4_0`` -- configs[3], Q4_0 x Q8_0 at M = 1 and 4 on the TinyLlama FFN
+    shapes, each bracket streaming 16 distinct weight copies (the 6.5 MB weight would
+    otherwise be served from L2);
+  * ``llama7b_ffn`` -- the 7B FFN of configs[4] at M = 4096 (W8A8) and M = 1 (Q4_0).
 
 ``python bench.py [--gpus N --steps K --warmup W]``; for N > 1 run under
-``torch.distributed.run`` (one rank per GPU). ``--impl reference`` times the
-reference's own CPU implementation (the oracle port of
-src/qpu_xla/models/tinyllama/quantization.py:1065-1082) on a bounded sample.
+``torch.distributed.run`` (one rank per GPU). ``--impl reference`` times the reference's
+own CPU implementation (the NumPy port of src/qpu_xla/models/tinyllama/quantization.py:
+1065-1082) on a bounded sample.
 """
 
 from __future__ import annotations
@@ -41,6 +53,7 @@ import threading
 import time
 from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
+from typing import Any, Callable
 
 ROOT = Path(__file__).resolve().parent
 sys.path[:0] = [str(ROOT / "qpu-xla-triton_b200"), str(ROOT)]
@@ -51,6 +64,8 @@ TOKENS = 4096
 SEED = 4
 L2_FLUSH_BYTES = 256 << 20
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+OBJECTS = ("square", "tinyllama_w8a8", "tinyllama_q4_0", "llama7b_ffn")
+Q4_0_COPIES = 16  # distinct TinyLlama weight copies streamed per bracket (16 x 6.5 MB)
 
 
 ONLY: set[str] = set()  # --only: restrict to some projections (profiling captures of a smaller case)
@@ -70,19 +85,46 @@ def measured_peaks() -> tuple[dict[str, float], str]:
     return dict(FALLBACK_PEAKS), "fallback"
 
 
-def profile_traffic(name: str) -> float | None:
-    """Per-launch DRAM bytes recorded by the committed ncu summary ``profiles/<name>.md`` (a
-    ``traffic_bytes_per_launch: <n>`` line), or None before a capture exists."""
+def profile_traffic(name: str, key: str | None = None) -> float | None:
+    """Per-launch DRAM bytes recorded by the committed ncu summary ``profiles/<name>.md``: the
+    ``traffic_bytes_per_launch: <n>`` line, or with ``key`` the
+    ``traffic_bytes_per_launch[<key>]: <n>`` line; None before a capture exists."""
     path = ROOT / "profiles" / f"{name}.md"
     if not path.exists():
         return None
+    label = "traffic_bytes_per_launch" + (f"[{key}]" if key else "") + ":"
     for line in path.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
+        if line.strip().startswith(label):
             try:
                 return float(line.split(":", 1)[1].strip().split()[0])
             except ValueError:
                 return None
     return None
+
+
+def roofline(*, kernel: str, seconds: float, ops: float, nbytes: float, int8_peak: float, hbm_peak: float,
+             peak_note: str, traffic: float | None, traffic_launches: int = 1) -> dict[str, Any]:
+    """Roofline of one timed launch sequence: the bound is whichever of ops / int8 peak and bytes
+    / HBM peak takes longer; achieved is in that bound's unit; traffic is ncu's DRAM bytes for
+    the same launches (per launch x launches), or None before a capture exists."""
+    tensor_s = ops / (int8_peak * 1e12) if ops else 0.0
+    hbm_s = nbytes / (hbm_peak * 1e9)
+    if tensor_s >= hbm_s:
+        achieved, peak, unit, bound = ops / seconds / 1e12, int8_peak, "TOPS", "tensor"
+    else:
+        achieved, peak, unit, bound = nbytes / seconds / 1e9, hbm_peak, "GB/s", "hbm"
+    return {
+        "kernel": kernel,
+        "bound": bound,
+        "achieved": round(achieved, 2),
+        "peak": round(peak, 1),
+        "unit": unit,
+        "frac": round(achieved / peak, 4),
+        "peak_source": peak_note,
+        "algorithmic_ops": ops,
+        "algorithmic_bytes": nbytes,
+        "traffic": None if traffic is None else traffic * traffic_launches,
+    }
 
 
 # ---------------------------------------------------------------------------- clocks
@@ -162,13 +204,154 @@ class ClockSampler:
 # ---------------------------------------------------------------------------- ours
 
 
+class Bench:
+    """Device, stream, L2 flush and bracket timing shared by every object."""
+
+    def __init__(self, device: Any, stream: Any, cuda: Any) -> None:
+        import torch
+
+        self.device = device
+        self.stream = stream
+        self.cuda = cuda
+        self.native = device.backend.native
+        self.flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=cuda)
+        self.flush_clean = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=cuda)
+
+    def launch(self, call: Callable[[Any, int], int]) -> None:
+        """A C-ABI call on the bench stream: ``call(library, context handle) -> status``."""
+        self.device.backend.launch(self.stream, lambda n: n.check(call(n.library, n.handle), "bench"))
+
+    def prime(self) -> None:
+        """Flush L2 (write one buffer larger than L2, then read another so the lines left are
+        clean), then hold the stream ~60 us so the host has queued the bracketed launches
+        before the start event executes (no host launch latency inside a timed bracket)."""
+        import torch
+
+        self.flush.zero_()
+        self.flush_clean.sum()
+        torch.cuda._sleep(120_000)
+
+    def brackets(self, fn: Callable[[], None], reps: int, warmup: int = 3) -> list[float]:
+        """``reps`` CUDA-event brackets of ``fn`` on the bench stream, L2 flushed before each; ms."""
+        import torch
+
+        for _ in range(warmup):
+            fn()
+        events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for start, end in events:
+            self.prime()
+            start.record(self.stream)
+            fn()
+            end.record(self.stream)
+        torch.cuda.synchronize()
+        return [start.elapsed_time(end) for start, end in events]
+
+    def quantize_weight(self, weight: Any) -> Any:
+        """fp32 [N, K] CUDA tensor -> QuantizedMatrixInt8 through the row-quantizer kernel."""
+        import torch
+
+        from qpu_xla.quantization import QuantizedMatrixInt8
+
+        n, k = weight.shape
+        values = torch.empty((n, k), dtype=torch.int8, device=self.cuda)
+        scales = torch.empty((n,), dtype=torch.float32, device=self.cuda)
+        self.launch(lambda lib, h: lib.qpucuda_quantize_rows_int8(h, weight.data_ptr(), k, n, k, k, values.data_ptr(), k, scales.data_ptr()))
+        torch.cuda.synchronize()
+        return QuantizedMatrixInt8(values.cpu().numpy(), scales.cpu().numpy())
+
+    def q4_0_blocks(self, weight: Any) -> Any:
+        """fp32 [N, K] CUDA tensor -> native Q4_0 blocks (host uint8 [N, K/32, 18])."""
+        import torch
+
+        n, k = weight.shape
+        blocks = torch.empty((n, k // 32, 18), dtype=torch.uint8, device=self.cuda)
+        self.launch(lambda lib, h: lib.qpucuda_quantize_q4_0(h, weight.data_ptr(), k, n, k, blocks.data_ptr()))
+        torch.cuda.synchronize()
+        return blocks.cpu().numpy()
+
+    def q8_0(self, source: Any) -> Any:
+        """fp32 [M, K] CUDA rows -> Q8_0 blocks on the device."""
+        import torch
+
+        m, k = source.shape
+        act = torch.empty((m, k // 32, 34), dtype=torch.uint8, device=self.cuda)
+        self.launch(lambda lib, h: lib.qpucuda_quantize_q8_0(h, source.data_ptr(), source.stride(0), m, k, act.data_ptr()))
+        return act
+
+
+class PrefillProjection:
+    """One W8A8 projection of a prefill step: the plan, its source and output, and the two launches
+    of a step (row quantizer into the plan's scratch, then the GEMM from that scratch)."""
+
+    def __init__(self, bench: Bench, name: str, plan: Any, source: Any, out: Any, k: int, count: int) -> None:
+        self.bench = bench
+        self.name = name
+        self.plan = plan
+        self.source = source
+        self.out = out
+        self.k = k
+        self.count = count
+        self.quantized, self.row_scales = plan.scratch()
+        self.handle = plan._handle
+
+    def quantize(self) -> None:
+        src, q, s, k = self.source, self.quantized, self.row_scales, self.k
+        self.bench.launch(lambda lib, h: lib.qpucuda_quantize_rows_int8(
+            h, src.data_ptr(), src.stride(0), src.shape[0], k, q.shape[1], q.data_ptr(), q.stride(0), s.data_ptr()))
+
+    def gemm(self) -> None:
+        handle, q, s, out, rows = self.handle, self.quantized, self.row_scales, self.out, self.source.shape[0]
+        self.bench.launch(lambda lib, h: lib.qpucuda_w8a8_linear_execute_prepared_device(
+            handle, q.data_ptr(), q.stride(0), s.data_ptr(), rows, out.data_ptr(), out.stride(0)))
+
+
+def timed_prefill(bench: Bench, projections: list[PrefillProjection], steps: int, warmup: int,
+                  extra: Callable[[], None] | None = None) -> tuple[float, list[float], list[float]]:
+    """``steps`` prefill steps (each projection: quantize, GEMM), L2 flushed before each, CUDA
+    events around every step and around every launch inside it. Returns (ms per step, ms per
+    quantizer launch per projection, ms per GEMM launch per projection)."""
+    import torch
+
+    def step(marks: list[Any] | None) -> None:
+        for i, p in enumerate(projections):
+            if marks is not None:
+                marks[2 * i].record(bench.stream)
+            p.quantize()
+            if marks is not None:
+                marks[2 * i + 1].record(bench.stream)
+            p.gemm()
+        if marks is not None:
+            marks[-1].record(bench.stream)
+        if extra is not None:
+            extra()
+
+    for _ in range(warmup):
+        bench.prime()
+        step(None)
+    torch.cuda.synchronize()
+    records = []
+    for _ in range(steps):
+        marks = [torch.cuda.Event(enable_timing=True) for _ in range(2 * len(projections) + 1)]
+        bench.prime()
+        step(marks)
+        records.append(marks)
+    torch.cuda.synchronize()
+    step_ms = statistics.mean(r[0].elapsed_time(r[-1]) for r in records)
+    quant_ms, gemm_ms = [], []
+    for i in range(len(projections)):
+        quant_ms.append(statistics.mean(r[2 * i].elapsed_time(r[2 * i + 1]) for r in records))
+        end = (lambda r, i=i: r[2 * i + 2])
+        gemm_ms.append(statistics.mean(r[2 * i + 1].elapsed_time(end(r)) for r in records))
+    return step_ms, quant_ms, gemm_ms
+
+
 def run_ours(args: argparse.Namespace) -> None:
     import torch
     import torch.distributed as dist
 
     from qpu_xla import Device
     from qpu_xla.ggml import PreparedQ4_0Linear
-    from qpu_xla.quantization import PreparedW8A8Linear, QuantizedMatrixInt8
+    from qpu_xla.quantization import PreparedW8A8Linear
     from qpu_xla.sharded import ColumnGather
 
     rank = int(os.environ.get("RANK", "0"))
@@ -183,35 +366,31 @@ def run_ours(args: argparse.Namespace) -> None:
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=cuda)
     device = Device.open(device_ordinal=local_rank)
-    native = device.backend.native  # type: ignore[attr-defined]
     stream = torch.cuda.current_stream(cuda)
-
-    def launch(call):  # type: ignore[no-untyped-def]
-        device.backend.launch(stream, lambda n: n.check(call(n.library, n.handle), "bench"))  # type: ignore[attr-defined]
+    bench = Bench(device, stream, cuda)
+    peaks, peak_kind = measured_peaks()
 
     # ---- inputs and plans (identical on every rank: seeded GPU generator) ----
     generator = torch.Generator(device=cuda)
     generator.manual_seed(SEED)
-    projections = []
+    projections: list[dict[str, Any]] = []
     sources: dict[int, torch.Tensor] = {}
-    for index, (name, k, n) in enumerate(shapes()):
+    for name, k, n in shapes():
         if k not in sources:
             sources[k] = torch.randn((TOKENS, k), generator=generator, device=cuda, dtype=torch.float32)
         weight = torch.randn((n, k), generator=generator, device=cuda, dtype=torch.float32) * 0.02
-        values = torch.empty((n, k), dtype=torch.int8, device=cuda)
-        scales = torch.empty((n,), dtype=torch.float32, device=cuda)
-        launch(lambda lib, h: lib.qpucuda_quantize_rows_int8(h, weight.data_ptr(), k, n, k, k, values.data_ptr(), k, scales.data_ptr()))
-        q4_blocks = torch.empty((n, k // 32, 18), dtype=torch.uint8, device=cuda)
-        launch(lambda lib, h: lib.qpucuda_quantize_q4_0(h, weight.data_ptr(), k, n, k, q4_blocks.data_ptr()))
-        torch.cuda.synchronize()
+        quantized = bench.quantize_weight(weight)
+        q4_blocks = bench.q4_0_blocks(weight)
         gather = ColumnGather(n, world, rank)
-        quantized = QuantizedMatrixInt8(values.cpu().numpy(), scales.cpu().numpy())
         plan = PreparedW8A8Linear(device, quantized, max_batch=TOKENS, resident_outputs=(gather.start, gather.count))
-        q4 = PreparedQ4_0Linear(device, q4_blocks.cpu().numpy(), rows=1, resident_column_start=gather.start, resident_column_count=gather.count)
+        q4 = PreparedQ4_0Linear(device, q4_blocks, rows=4, resident_column_start=gather.start, resident_column_count=gather.count)
         local = torch.zeros((TOKENS, gather.width), dtype=torch.float32, device=cuda)
         full = torch.empty((TOKENS, n), dtype=torch.float32, device=cuda) if world > 1 else local
-        projections.append({"name": name, "k": k, "n": n, "gather": gather, "plan": plan, "q4": q4, "local": local, "full": full, "source": sources[k]})
-        del weight, values, scales, q4_blocks
+        projections.append({
+            "name": name, "k": k, "n": n, "gather": gather, "plan": plan, "q4": q4, "local": local, "full": full,
+            "source": sources[k], "step": PrefillProjection(bench, name, plan, sources[k], local[:, : gather.count], k, gather.count),
+        })
+        del weight, quantized, q4_blocks
     exchange = "none"
     if world > 1 and args.exchange == "nccl":
         exchange = "NCCL all-gather after the GEMM (selected with --exchange nccl)"
@@ -219,7 +398,7 @@ def run_ours(args: argparse.Namespace) -> None:
     elif world > 1:
         from qpu_xla.sharded import PeerOutput
 
-        exchange = "fused GEMM epilogue stores into every rank's output (CUDA IPC over NVLink) + NCCL all-reduce barrier"
+        exchange = "fused GEMM epilogue stores into every rank's output (CUDA IPC over NVLink) + one NCCL all-reduce per step"
         try:
             for p in projections:
                 p["peer"] = PeerOutput(device, TOKENS, p["n"])
@@ -230,28 +409,22 @@ def run_ours(args: argparse.Namespace) -> None:
             exchange = f"NCCL all-gather after the GEMM (peer mapping refused: {str(error)[:120]})"
         barrier_flag = torch.zeros(1, dtype=torch.float32, device=cuda)
     torch.cuda.empty_cache()
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=cuda)
-    flush_clean = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=cuda)
-
-    def prime() -> None:
-        """Flush L2 (write one buffer larger than L2, then read another so the lines left are
-        clean), then hold the stream ~60 us so the host has queued the bracketed launches
-        before the start event executes (no host launch latency inside a timed bracket)."""
-        flush.zero_()
-        flush_clean.sum()
-        torch.cuda._sleep(120_000)
 
     def step() -> None:
+        fused = False
         for p in projections:
             g = p["gather"]
             if "peer" in p:
                 destination, peers = p["peer"].slice_pointers(g.start)
                 p["plan"].forward_fanout(p["source"], destination, peers, p["n"])
-                dist.all_reduce(barrier_flag)
+                fused = True
                 continue
-            p["plan"].forward(p["source"], out=p["local"][:, : g.count])
+            p["step"].quantize()
+            p["step"].gemm()
             if world > 1:
                 g.gather(p["local"], out=p["full"])
+        if fused:
+            dist.all_reduce(barrier_flag)  # every rank's peer stores of this step are done
 
     def barrier() -> None:
         if world > 1:
@@ -278,14 +451,14 @@ def run_ours(args: argparse.Namespace) -> None:
 
     # ---- headline: K whole steps, per-step CUDA events, L2 flushed in between ----
     for _ in range(args.warmup):
-        prime()
+        bench.prime()
         step()
     barrier()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     wall0 = time.perf_counter()
     for i in range(args.steps):
-        prime()
+        bench.prime()
         starts[i].record(stream)
         step()
         ends[i].record(stream)
@@ -295,28 +468,12 @@ def run_ours(args: argparse.Namespace) -> None:
     total_ops = sum(2.0 * TOKENS * p["n"] * p["k"] for p in projections)  # whole job, all ranks
     value_tops = total_ops / (step_ms * 1e-3) / 1e12
 
-    # ---- N > 1: the same step without the exchange (quantize + GEMM on the rank's shard) ----
+    # ---- the rank's own kernels: the same step on its shard with an event between every launch
+    # (at N = 1 this is the headline step again; at N > 1 it leaves out the exchange) ----
+    local_ms, quant_ms, gemm_ms = timed_prefill(bench, [p["step"] for p in projections], args.steps, args.warmup)
+    local_ms = max_over_ranks(local_ms)
     multi_gpu = None
     if world > 1:
-
-        def local_step() -> None:
-            for p in projections:
-                p["plan"].forward(p["source"], out=p["local"][:, : p["gather"].count])
-
-        for _ in range(args.warmup):
-            prime()
-            local_step()
-        barrier()
-        local_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        local_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-        for i in range(args.steps):
-            prime()
-            local_starts[i].record(stream)
-            local_step()
-            local_ends[i].record(stream)
-        barrier()
-        local_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(local_starts, local_ends)) / args.steps)
-        # fp32 output columns every rank receives from the others per step
         received = sum(TOKENS * (p["n"] - p["gather"].count) * 4 for p in projections)
         multi_gpu = {
             "kernel_ms_per_step": round(local_ms, 4),
@@ -328,31 +485,6 @@ def run_ours(args: argparse.Namespace) -> None:
             "note": "kernel = quantize + GEMM on the rank's column shard alone; exchange = the step's extra time "
             "over that (the fused epilogue overlaps the peer stores with the GEMM, so this is the exposed part)",
         }
-
-    # ---- dominant kernel: the tcgen05 GEMM alone (activations already quantized) ----
-    gemm_ms = []
-    for p in projections:
-        plan = p["plan"]
-        quantized, row_scales = plan.scratch()
-        plan.forward(p["source"], out=p["local"][:, : p["gather"].count])  # fills the scratch for this projection
-        handle = plan._handle
-        out = p["local"]
-
-        def gemm(handle=handle, quantized=quantized, row_scales=row_scales, out=out, count=p["gather"].count):  # type: ignore[no-untyped-def]
-            launch(lambda lib, h: lib.qpucuda_w8a8_linear_execute_prepared_device(
-                handle, quantized.data_ptr(), quantized.stride(0), row_scales.data_ptr(), TOKENS, out.data_ptr(), out.stride(0)))
-
-        for _ in range(3):
-            gemm()
-        reps = 10
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-        for s, e in evs:
-            prime()
-            s.record(stream)
-            gemm()
-            e.record(stream)
-        torch.cuda.synchronize()
-        gemm_ms.append(statistics.mean(s.elapsed_time(e) for s, e in evs))
     rank_gemm_ops = sum(2.0 * TOKENS * p["gather"].count * p["k"] for p in projections)
     gemm_seconds = sum(gemm_ms) * 1e-3
     achieved_tops = rank_gemm_ops / gemm_seconds / 1e12 if gemm_seconds > 0 else 0.0
@@ -367,66 +499,48 @@ def run_ours(args: argparse.Namespace) -> None:
     for p in projections:
         a8 = torch.randint(-127, 128, (TOKENS, p["k"]), dtype=torch.int8, device=cuda)
         w8 = torch.randint(-127, 128, (p["gather"].count, p["k"]), dtype=torch.int8, device=cuda)
-        for _ in range(3):
-            torch._int_mm(a8, w8.t())
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(10)]
-        for s_ev, e_ev in evs:
-            prime()
-            s_ev.record(stream)
-            torch._int_mm(a8, w8.t())
-            e_ev.record(stream)
-        torch.cuda.synchronize()
-        library_ms.append(statistics.mean(s_ev.elapsed_time(e_ev) for s_ev, e_ev in evs))
+        library_ms.append(statistics.mean(bench.brackets(lambda a8=a8, w8=w8: torch._int_mm(a8, w8.t()), 10)))
         del a8, w8
     torch.cuda.empty_cache()
-    library_tops = rank_gemm_ops / (sum(library_ms) * 1e-3) / 1e12
-    library_tops = max_over_ranks(library_tops)
+    library_tops = max_over_ranks(rank_gemm_ops / (sum(library_ms) * 1e-3) / 1e12)
+    bf16_doubled = 2.0 * peaks["bf16_tflops"]
+    int8_peak = max(bf16_doubled, library_tops)
+    int8_note = (f"the larger of cuBLASLt int8 (torch._int_mm) measured live on the 70B FFN shapes ({library_tops:.1f} TOPS) "
+                 f"and 2 x {peak_kind} cuBLAS bf16 burst ({bf16_doubled:.1f} TOPS)")
+    hbm_note = f"{peak_kind} STREAM-style copy"
 
-    # ---- Q4_0 x Q8_0 decode matvec (M = 1), Q8_0 activations already on the device ----
-    # One decode step of the FFN = gate, up and down back to back on the stream. The three
-    # weight matrices (3 x 132 MB at full width) exceed L2, so each launch streams its weight
-    # from DRAM; L2 is flushed before every bracketed step as for the prefill steps.
-    q4_inputs = []
-    q4_bytes_rank = 0.0
-    for p in projections:
-        g = p["gather"]
-        act = torch.empty((1, p["k"] // 32, 34), dtype=torch.uint8, device=cuda)
-        src = p["source"][:1]
-        launch(lambda lib, h: lib.qpucuda_quantize_q8_0(h, src.data_ptr(), src.stride(0), 1, p["k"], act.data_ptr()))
-        out = torch.empty((1, g.width), dtype=torch.float32, device=cuda)
-        q4_inputs.append((p["q4"], act, out[:, : g.count]))
-        q4_bytes_rank += 18.0 * g.count * p["k"] / 32 + 34.0 * p["k"] / 32 + 4.0 * g.count
-
-    def decode_ffn() -> None:
-        for q4, act, out in q4_inputs:
-            q4.forward(act, out=out)
-
-    for _ in range(3):
-        decode_ffn()
+    # ---- Q4_0 x Q8_0 decode (M = 1 and 4) on the 70B shapes, Q8_0 activations on the device ----
+    # One decode step of the FFN = gate, up and down back to back on the stream. The three weight
+    # matrices (3 x 132 MB at full width) exceed L2, and L2 is flushed before every bracket.
     reps = 20
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-    for s, e in evs:
-        prime()
-        s.record(stream)
-        decode_ffn()
-        e.record(stream)
-    torch.cuda.synchronize()
-    q4_step_ms = statistics.mean(s.elapsed_time(e) for s, e in evs)
-    # each projection alone in its own bracket (includes one bracket's fixed event overhead)
-    q4_ms = []
-    for q4, act, out in q4_inputs:
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-        for s, e in evs:
-            prime()
-            s.record(stream)
-            q4.forward(act, out=out)
-            e.record(stream)
-        torch.cuda.synchronize()
-        q4_ms.append(statistics.mean(s.elapsed_time(e) for s, e in evs))
-    q4_seconds = max_over_ranks(q4_step_ms * 1e-3)
-    q4_total_bytes = sum_over_ranks(q4_bytes_rank)
-    q4_gbs = q4_total_bytes / q4_seconds / 1e9
-    q4_rank_gbs = q4_bytes_rank / (q4_step_ms * 1e-3) / 1e9
+    q4_rows: dict[str, dict[str, float]] = {}
+    q4_alone: list[float] = []
+    for rows in (1, 4):
+        q4_inputs = []
+        q4_bytes_rank = 0.0
+        for p in projections:
+            g = p["gather"]
+            act = bench.q8_0(p["source"][:rows])
+            out = torch.empty((rows, g.width), dtype=torch.float32, device=cuda)
+            q4_inputs.append((p["q4"], act, out[:, : g.count]))
+            q4_bytes_rank += 18.0 * g.count * p["k"] / 32 + 34.0 * rows * p["k"] / 32 + 4.0 * rows * g.count
+
+        def decode_ffn(q4_inputs: list[Any] = q4_inputs) -> None:
+            for q4, act, out in q4_inputs:
+                q4.forward(act, out=out)
+
+        q4_ms = statistics.mean(bench.brackets(decode_ffn, reps))
+        q4_seconds = max_over_ranks(q4_ms * 1e-3)
+        q4_rows[str(rows)] = {
+            "value": round(sum_over_ranks(q4_bytes_rank) / q4_seconds / 1e9, 1),
+            "rank_gbs": round(q4_bytes_rank / (q4_ms * 1e-3) / 1e9, 1),
+            "us_per_decode_ffn": round(q4_ms * 1e3, 2),
+            "frac": round(q4_bytes_rank / (q4_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+        }
+        if rows == 1:
+            # each projection alone in its own bracket (includes one bracket's fixed event overhead)
+            for q4, act, out in q4_inputs:
+                q4_alone.append(statistics.mean(bench.brackets(lambda q4=q4, act=act, out=out: q4.forward(act, out=out), reps)))
 
     # ---- W8A8 decode (rows <= 8 take the int8 GEMV): the prefill plans at M = 1 and M = 8,
     # fp32 rows on the device (row quantizer + GEMV per projection), L2 flushed per bracket.
@@ -442,21 +556,21 @@ def run_ours(args: argparse.Namespace) -> None:
             float(p["gather"].count) * p["k"] + gemv_rows * p["k"] + 4.0 * (p["gather"].count + gemv_rows + gemv_rows * p["gather"].count)
             for p in projections
         )
-        for _ in range(3):
-            decode_w8a8()
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
-        for s, e in evs:
-            prime()
-            s.record(stream)
-            decode_w8a8()
-            e.record(stream)
-        torch.cuda.synchronize()
-        gemv_step_ms = max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in evs))
+        gemv_step_ms = max_over_ranks(statistics.mean(bench.brackets(decode_w8a8, reps)))
         w8a8_gemv[str(gemv_rows)] = {
             "value": round(sum_over_ranks(gemv_bytes_rank) / (gemv_step_ms * 1e-3) / 1e9, 1),
             "rank_gbs": round(gemv_bytes_rank / (gemv_step_ms * 1e-3) / 1e9, 1),
             "us_per_decode_ffn": round(gemv_step_ms * 1e3, 2),
+            "frac": round(gemv_bytes_rank / (gemv_step_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
         }
+
+    # ---- the other configurations (N = 1 only; they are single-GPU configurations) ----
+    objects: dict[str, Any] = {}
+    wanted = [o for o in OBJECTS if not args.objects or o in args.objects]
+    if world == 1:
+        for name in wanted:
+            objects[name] = OBJECT_RUNNERS[name](bench, int8_peak, peaks["hbm_gbs"], int8_note, hbm_note)
+            torch.cuda.empty_cache()
 
     clocks = sampler.stop() if rank == 0 else {}
 
@@ -471,7 +585,7 @@ def run_ours(args: argparse.Namespace) -> None:
 
         def e2e_step() -> None:
             for p, out in zip(projections, host_out):
-                p["plan"].execute_host(host_sources[p["k"]].numpy(), out.numpy())
+                p["plan"].execute_host(host_sources[p["k"]].numpy(), out.numpy(), direct=True)
 
         e2e_step()
         barrier()
@@ -488,18 +602,18 @@ def run_ours(args: argparse.Namespace) -> None:
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
             "ms_per_step": e2e_seconds * 1e3,
-            "path": "qpucuda_w8a8_linear_execute (host pinned buffers) per rank on its column shard",
+            "path": "qpucuda_w8a8_linear_execute_direct (page-locked host source and destination, copies by DMA "
+            "on two copy streams overlapping the kernels) per rank on its column shard; host wall clock, max over ranks",
         }
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_baseline = cpu_reference_sample(target_seconds=args.cpu_seconds)
+        cpu_baseline["torch_int32"] = cpu_torch_int32_sample(workload_shapes=shapes(), tokens=TOKENS, target_seconds=args.cpu_seconds / 4)
+        for name, entry in objects.items():
+            entry["cpu"] = OBJECT_CPU[name](args.cpu_seconds / 5)
 
-    peaks, peak_kind = measured_peaks()
-    bf16_doubled = 2.0 * peaks["bf16_tflops"]
-    int8_peak = max(bf16_doubled, library_tops)
     traffic = profile_traffic("w8a8_gemm_sm100_70b_ffn")
-    q4_traffic = profile_traffic("q4_0_gemv_70b_decode")
     line = {
         "metric": METRIC,
         "value": round(value_tops, 3),
@@ -518,7 +632,7 @@ def run_ours(args: argparse.Namespace) -> None:
             "tokens": TOKENS,
             "projections": [f"{name} {k}->{n}" for name, k, n in shapes()],
             "parallelism": f"output-channel split x{world}" + (f" + {exchange}" if world > 1 else ""),
-            "l2": "flushed between timed steps (256 MiB write, then 256 MiB read of a second buffer; outside the CUDA-event brackets); inputs exceed L2",
+            "l2": "flushed before every timed step or bracket (256 MiB write, then 256 MiB read of a second buffer; outside the CUDA-event brackets); the headline's inputs exceed L2",
             "timing": "per-step CUDA events on the launching stream, summed over K steps, max over ranks",
             "wall_s_timed_loop": round(wall, 4),
         },
@@ -530,33 +644,34 @@ def run_ours(args: argparse.Namespace) -> None:
             "peak": round(int8_peak, 1),
             "unit": "TOPS",
             "frac": round(achieved_tops / int8_peak, 4),
-            "peak_source": (
-                f"the larger of cuBLASLt int8 (torch._int_mm) measured live on the same shapes ({library_tops:.1f} TOPS) "
-                f"and 2 x {peak_kind} cuBLAS bf16 burst ({bf16_doubled:.1f} TOPS)"
-            ),
+            "peak_source": int8_note,
             "library_int8_tops": round(library_tops, 1),
             "library_int8_ms_per_projection": [round(x, 4) for x in library_ms],
             "peak_2x_bf16": round(bf16_doubled, 1),
             "traffic": traffic,
             "algorithmic_ops_per_rank_step": rank_gemm_ops,
             "gemm_ms_per_projection": [round(x, 4) for x in gemm_ms],
+            "gemm_timing": "CUDA events recorded between the row-quantizer and GEMM launches inside the timed steps (L2 flushed before each step)",
+            "row_quantizer_ms_per_projection": [round(x, 4) for x in quant_ms],
+            "row_quantizer_gbs": [round((4.0 + 1.0) * TOKENS * p["k"] / (ms * 1e-3) / 1e9, 1) for p, ms in zip(projections, quant_ms)],
         },
         "q4_0_gemv": {
-            "metric": "Q4_0 x Q8_0 M=1 GEMV GB/s (whole job), one decode FFN step (gate, up, down) per bracket",
-            "value": round(q4_gbs, 1),
+            "metric": "Q4_0 x Q8_0 GEMV GB/s (whole job), one decode FFN step (gate, up, down) per bracket, at M = 1 and 4",
+            "value": q4_rows["1"]["value"],
             "unit": "GB/s",
+            "rows": q4_rows,
             "roofline": {
                 "kernel": "q4_0_direct_kernel (dp4a, prepared nibble layout, two columns per warp)",
                 "bound": "hbm",
-                "achieved": round(q4_rank_gbs, 1),
+                "achieved": q4_rows["1"]["rank_gbs"],
                 "peak": peaks["hbm_gbs"],
                 "unit": "GB/s",
-                "frac": round(q4_rank_gbs / peaks["hbm_gbs"], 4),
-                "peak_source": f"{peak_kind} STREAM-style copy",
-                "traffic": q4_traffic,
+                "frac": q4_rows["1"]["frac"],
+                "peak_source": hbm_note,
+                "traffic": profile_traffic("q4_0_gemv_70b_decode"),
             },
-            "us_per_decode_ffn": round(q4_step_ms * 1e3, 2),
-            "us_per_projection_alone": [round(x * 1e3, 2) for x in q4_ms],
+            "us_per_decode_ffn": q4_rows["1"]["us_per_decode_ffn"],
+            "us_per_projection_alone": [round(x * 1e3, 2) for x in q4_alone],
         },
         "w8a8_gemv": {
             "metric": "W8A8 decode GB/s (whole job), one FFN step (gate, up, down: row quantizer + int8 GEMV) per bracket, at M = 1 and M = 8",
@@ -564,18 +679,19 @@ def run_ours(args: argparse.Namespace) -> None:
             "unit": "GB/s",
             "rows": w8a8_gemv,
             "roofline": {
-                "kernel": "w8a8_gemv_kernel (dp4a, persistent balanced grid, split-K across a CTA's warps, next column's first loads issued before the reduction at M <= 2)",
+                "kernel": "w8a8_gemv_kernel (dp4a, persistent balanced grid, split-K across a CTA's warps)",
                 "bound": "hbm",
                 "achieved": w8a8_gemv["1"]["rank_gbs"],
                 "peak": peaks["hbm_gbs"],
                 "unit": "GB/s",
-                "frac": round(w8a8_gemv["1"]["rank_gbs"] / peaks["hbm_gbs"], 4),
-                "peak_source": f"{peak_kind} STREAM-style copy",
-                "traffic": None,
+                "frac": w8a8_gemv["1"]["frac"],
+                "peak_source": hbm_note,
+                "traffic": profile_traffic("w8a8_gemv_70b_decode"),
             },
         },
         "clocks": clocks,
     }
+    line.update(objects)
     if multi_gpu is not None:
         line["multi_gpu"] = multi_gpu
     if e2e is not None:
@@ -595,36 +711,241 @@ def run_ours(args: argparse.Namespace) -> None:
         dist.destroy_process_group()
 
 
+# ---------------------------------------------------------------------------- objects (N = 1)
+
+
+def object_square(bench: Bench, int8_peak: float, hbm_peak: float, int8_note: str, hbm_note: str) -> dict[str, Any]:
+    """configs[0-1]: the reference's square W8A8 cases (64^3; 512^3 with bias) through the
+    prepared plan, one call (row quantizer + GEMM) per bracket."""
+    import torch
+
+    from qpu_xla import workloads
+    from qpu_xla.quantization import PreparedW8A8Linear, quantize_per_output_channel_int8
+
+    result: dict[str, Any] = {"metric": "W8A8 linear (quantize + GEMM + dequant) per call, M = K = N", "unit": "TOPS"}
+    for size in (64, 512):
+        case = workloads.square_case(size)
+        weight = quantize_per_output_channel_int8(case.weight, device=bench.device)
+        src = torch.from_numpy(case.source).to(bench.cuda)
+        dst = torch.empty((size, size), dtype=torch.float32, device=bench.cuda)
+        with PreparedW8A8Linear(bench.device, weight, max_batch=size, bias=case.bias) as plan:
+            ms = statistics.median(bench.brackets(lambda plan=plan: plan.forward(src, out=dst), 50))
+        ops = 2.0 * size**3
+        nbytes = 4.0 * size * size * 2 + size * size + 4.0 * (2 * size + (size if case.bias is not None else 0))
+        result[str(size)] = {
+            "value": round(ops / (ms * 1e-3) / 1e12, 4),
+            "us_per_call": round(ms * 1e3, 2),
+            "bias": case.bias is not None,
+            "roofline": roofline(kernel="row quantizer + w8a8_gemm_sm100 (one tile)", seconds=ms * 1e-3, ops=ops, nbytes=nbytes,
+                                 int8_peak=int8_peak, hbm_peak=hbm_peak, peak_note=int8_note,
+                                 traffic=profile_traffic("objects_traffic", f"square_{size}")),
+            "note": "two launches of a few microseconds each: launch latency bounds this size, not the tensor pipe or HBM",
+        }
+    result["value"] = result["512"]["value"]
+    return result
+
+
+def object_tinyllama_w8a8(bench: Bench, int8_peak: float, hbm_peak: float, int8_note: str, hbm_note: str) -> dict[str, Any]:
+    """the seven projections of one TinyLlama layer (q, k, v, o, gate, up, down) back to
+    back per bracket, at M = 1, 128 and 2048; random-init weights ~N(0, 0.02)."""
+    import torch
+
+    from qpu_xla import workloads
+    from qpu_xla.quantization import PreparedW8A8Linear, quantize_per_output_channel_int8
+
+    shapes7 = workloads.TINYLLAMA_LAYER
+    plans = []
+    for shape in shapes7:
+        case = workloads.tinyllama_case(shape, workloads.TINYLLAMA_TOKENS[-1])
+        plans.append(PreparedW8A8Linear(bench.device, quantize_per_output_channel_int8(case.weight, device=bench.device),
+                                        max_batch=max(workloads.TINYLLAMA_TOKENS)))
+    result: dict[str, Any] = {"metric": "TinyLlama layer, 7 W8A8 projections per bracket", "unit": "TOPS", "tokens": {}}
+    try:
+        for tokens in workloads.TINYLLAMA_TOKENS:
+            sources = [torch.from_numpy(workloads.tinyllama_case(shape, tokens).source).to(bench.cuda) for shape in shapes7]
+            outs = [torch.empty((tokens, shape.out_features), dtype=torch.float32, device=bench.cuda) for shape in shapes7]
+
+            def layer(sources: list[Any] = sources, outs: list[Any] = outs) -> None:
+                for plan, src, out in zip(plans, sources, outs):
+                    plan.forward(src, out=out)
+
+            ms = statistics.median(bench.brackets(layer, 20))
+            ops = sum(2.0 * tokens * s.in_features * s.out_features for s in shapes7)
+            k16 = [((s.in_features + 15) // 16) * 16 for s in shapes7]
+            nbytes = sum(s.out_features * k + tokens * s.in_features * 4.0 + tokens * k + 4.0 * (s.out_features + tokens + tokens * s.out_features)
+                         for s, k in zip(shapes7, k16))
+            path = "row quantizer + w8a8_gemv_kernel" if tokens <= 8 else "row quantizer + w8a8_gemm_sm100"
+            result["tokens"][str(tokens)] = {
+                "tops": round(ops / (ms * 1e-3) / 1e12, 2),
+                "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                "us_per_layer": round(ms * 1e3, 2),
+                "roofline": roofline(kernel=path, seconds=ms * 1e-3, ops=ops, nbytes=nbytes, int8_peak=int8_peak, hbm_peak=hbm_peak,
+                                     peak_note=int8_note if ops / (int8_peak * 1e12) >= nbytes / (hbm_peak * 1e9) else hbm_note,
+                                     traffic=profile_traffic("objects_traffic", f"tinyllama_w8a8_m{tokens}")),
+            }
+            del sources, outs
+    finally:
+        for plan in plans:
+            plan.close()
+    result["value"] = result["tokens"]["2048"]["tops"]
+    return result
+
+
+def object_tinyllama_q4_0(bench: Bench, int8_peak: float, hbm_peak: float, int8_note: str, hbm_note: str) -> dict[str, Any]:
+    """Q4_0 x Q8_0 at M = 1 and 4 on the TinyLlama FFN shapes. Each weight is 6.5 MB,
+    so a bracket streams Q4_0_COPIES distinct prepared copies of it (one launch each, L2 flushed
+    before the bracket): every copy comes from DRAM."""
+    import torch
+
+    from qpu_xla import workloads
+    from qpu_xla.ggml import PreparedQ4_0Linear
+
+    result: dict[str, Any] = {"metric": f"Q4_0 x Q8_0 GB/s, {Q4_0_COPIES} weight copies per bracket", "unit": "GB/s", "shapes": {}}
+    for shape in workloads.TINYLLAMA_Q4_0_SHAPES:
+        _, weight = workloads.q4_0_case(shape, 1)
+        blocks = bench.q4_0_blocks(torch.from_numpy(weight).to(bench.cuda))
+        copies = [PreparedQ4_0Linear(bench.device, blocks, rows=4) for _ in range(Q4_0_COPIES)]
+        entry: dict[str, Any] = {}
+        try:
+            for rows in (1, 4):
+                source, _ = workloads.q4_0_case(shape, rows)
+                act = bench.q8_0(torch.from_numpy(source).to(bench.cuda))
+                out = torch.empty((rows, shape.out_features), dtype=torch.float32, device=bench.cuda)
+
+                def run(act: Any = act, out: Any = out) -> None:
+                    for plan in copies:
+                        plan.forward(act, out=out)
+
+                ms = statistics.median(bench.brackets(run, 20))
+                per_launch = 18.0 * shape.out_features * shape.in_features / 32 + 34.0 * rows * shape.in_features / 32 + 4.0 * rows * shape.out_features
+                seconds = ms * 1e-3 / Q4_0_COPIES
+                entry[str(rows)] = {
+                    "gbs": round(per_launch / seconds / 1e9, 1),
+                    "us_per_launch": round(seconds * 1e6, 2),
+                    "roofline": roofline(kernel="q4_0_direct_kernel", seconds=seconds, ops=0.0, nbytes=per_launch, int8_peak=int8_peak,
+                                         hbm_peak=hbm_peak, peak_note=hbm_note,
+                                         traffic=profile_traffic("objects_traffic", f"tinyllama_q4_0_{shape.name}_m{rows}")),
+                }
+        finally:
+            for plan in copies:
+                plan.close()
+        result["shapes"][f"{shape.name} {shape.in_features}->{shape.out_features}"] = entry
+    first = next(iter(result["shapes"].values()))
+    result["value"] = first["1"]["gbs"]
+    return result
+
+
+def object_llama7b_ffn(bench: Bench, int8_peak: float, hbm_peak: float, int8_note: str, hbm_note: str) -> dict[str, Any]:
+    """configs[4]'s 7B FFN (4096 -> 11008 -> 4096): W8A8 prefill at M = 4096 (the headline's step,
+    events between launches) and the Q4_0 decode FFN at M = 1 (76 MB of weights per bracket)."""
+    import torch
+
+    from qpu_xla import workloads
+    from qpu_xla.ggml import PreparedQ4_0Linear
+    from qpu_xla.quantization import PreparedW8A8Linear
+
+    generator = torch.Generator(device=bench.cuda)
+    generator.manual_seed(SEED + 3)
+    prefill, q4_plans, keep = [], [], []
+    srcs: dict[int, Any] = {}
+    for shape in workloads.LLAMA2_7B_FFN:
+        k, n = shape.in_features, shape.out_features
+        if k not in srcs:
+            srcs[k] = torch.randn((TOKENS, k), generator=generator, device=bench.cuda, dtype=torch.float32)
+        weight = torch.randn((n, k), generator=generator, device=bench.cuda, dtype=torch.float32) * 0.02
+        plan = PreparedW8A8Linear(bench.device, bench.quantize_weight(weight), max_batch=TOKENS)
+        out = torch.empty((TOKENS, n), dtype=torch.float32, device=bench.cuda)
+        prefill.append(PrefillProjection(bench, shape.name, plan, srcs[k], out, k, n))
+        q4_plans.append(PreparedQ4_0Linear(bench.device, bench.q4_0_blocks(weight), rows=1))
+        keep.append(out)
+        del weight
+    try:
+        step_ms, quant_ms, gemm_ms = timed_prefill(bench, prefill, 10, 3)
+        ops = [2.0 * TOKENS * p.count * p.k for p in prefill]
+        decode = []
+        q4_bytes = 0.0
+        for shape, q4 in zip(workloads.LLAMA2_7B_FFN, q4_plans):
+            act = bench.q8_0(srcs[shape.in_features][:1])
+            decode.append((q4, act, torch.empty((1, shape.out_features), dtype=torch.float32, device=bench.cuda)))
+            q4_bytes += 18.0 * shape.out_features * shape.in_features / 32 + 34.0 * shape.in_features / 32 + 4.0 * shape.out_features
+
+        def decode_ffn() -> None:
+            for q4, act, out in decode:
+                q4.forward(act, out=out)
+
+        q4_ms = statistics.median(bench.brackets(decode_ffn, 20))
+    finally:
+        for p in prefill:
+            p.plan.close()
+        for q4 in q4_plans:
+            q4.close()
+    return {
+        "metric": "Llama-2-7B FFN: W8A8 prefill TOPS at M = 4096, Q4_0 decode GB/s at M = 1",
+        "value": round(sum(ops) / (step_ms * 1e-3) / 1e12, 2),
+        "unit": "TOPS",
+        "ms_per_step": round(step_ms, 4),
+        "gemm_ms_per_projection": [round(x, 4) for x in gemm_ms],
+        "row_quantizer_ms_per_projection": [round(x, 4) for x in quant_ms],
+        "roofline": roofline(kernel="w8a8_gemm_sm100 (in-step events)", seconds=sum(gemm_ms) * 1e-3, ops=sum(ops), nbytes=0.0,
+                             int8_peak=int8_peak, hbm_peak=hbm_peak, peak_note=int8_note,
+                             traffic=profile_traffic("objects_traffic", "llama7b_gemm_gate"), traffic_launches=1),
+        "q4_0_decode": {
+            "gbs": round(q4_bytes / (q4_ms * 1e-3) / 1e9, 1),
+            "us_per_decode_ffn": round(q4_ms * 1e3, 2),
+            "roofline": roofline(kernel="q4_0_direct_kernel (gate, up, down)", seconds=q4_ms * 1e-3, ops=0.0, nbytes=q4_bytes,
+                                 int8_peak=int8_peak, hbm_peak=hbm_peak, peak_note=hbm_note,
+                                 traffic=profile_traffic("objects_traffic", "llama7b_q4_0_decode_ffn")),
+        },
+    }
+
+
+OBJECT_RUNNERS: dict[str, Callable[..., dict[str, Any]]] = {
+    "square": object_square,
+    "tinyllama_w8a8": object_tinyllama_w8a8,
+    "tinyllama_q4_0": object_tinyllama_q4_0,
+    "llama7b_ffn": object_llama7b_ffn,
+}
+
+
 # ---------------------------------------------------------------------------- reference (CPU)
 
 
-_CPU_SAMPLES: list[tuple[object, object, object]] = []
+_CPU_SAMPLES: dict[tuple[tuple[str, int, int], ...], list[tuple[object, object, object]]] = {}
 CPU_COLUMNS = 1024
 
 
-def cpu_reference_sample(*, target_seconds: float, rows: int | None = None) -> dict[str, object]:
-    """The reference's CPU path (oracle port of quantization.py:1065-1082: NumPy per-row
-    quantization, int32 matmul, fp32 dequant) on a bounded sample of the workload: ``rows``
-    token rows (sized to ``target_seconds``, at most the full 4096) x 1024 output columns of
-    each projection at its full K, split over all host threads."""
+def host_cores() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def cpu_reference_sample(*, target_seconds: float, rows: int | None = None,
+                         workload_shapes: list[tuple[str, int, int]] | None = None, tokens: int = TOKENS,
+                         label: str = "70B FFN") -> dict[str, object]:
+    """The reference's CPU path (NumPy port of quantization.py:1065-1082: per-row quantization,
+    int32 matmul, fp32 dequant) on a bounded sample of a prefill workload: ``rows`` token rows
+    (sized to ``target_seconds``, at most ``tokens``) x at most 1024 output columns of each
+    projection at its full K, the matmul split over all host threads."""
     import numpy as np
 
     from oracle import qpu_oracle as oracle
 
-    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
-    columns = CPU_COLUMNS
-    if not _CPU_SAMPLES:
+    cores = host_cores()
+    workload_shapes = shapes() if workload_shapes is None else workload_shapes
+    key = tuple(workload_shapes)
+    if key not in _CPU_SAMPLES:
         rng = np.random.default_rng(SEED)
-        for _, k, _n in shapes():
-            x = rng.standard_normal((TOKENS, k), dtype=np.float32)
-            w = (rng.standard_normal((columns, k), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        samples = []
+        for _, k, n in workload_shapes:
+            x = rng.standard_normal((tokens, k), dtype=np.float32)
+            w = (rng.standard_normal((min(CPU_COLUMNS, n), k), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
             values, scales = oracle.quantize_per_output_channel_int8(w)
-            _CPU_SAMPLES.append((x, values.astype(np.int32), scales))
+            samples.append((x, values.astype(np.int32), scales))
+        _CPU_SAMPLES[key] = samples
     pool = ThreadPoolExecutor(max_workers=cores)
 
-    def run(sample_rows: int) -> float:
-        ops = 0.0
-        for x, w32, scales in _CPU_SAMPLES:
+    def run(sample_rows: int) -> tuple[float, float]:
+        ops = full_ops = 0.0
+        for (x, w32, scales), (_, k, n) in zip(_CPU_SAMPLES[key], workload_shapes):
             xs = x[:sample_rows]  # type: ignore[index]
             q, s = oracle.quantize_rows_int8(xs)
             q32 = q.astype(np.int32)
@@ -633,15 +954,16 @@ def cpu_reference_sample(*, target_seconds: float, rows: int | None = None) -> d
             acc = np.concatenate(parts, axis=1)
             oracle.w8a8_dequantize(acc, s, scales)  # type: ignore[arg-type]
             ops += 2.0 * xs.shape[0] * w32.shape[0] * xs.shape[1]  # type: ignore[union-attr]
-        return ops
+        return ops, full_ops
 
     if rows is None:
+        probe_rows = min(8, tokens)
         t0 = time.perf_counter()
-        probe_ops = run(8)
+        probe_ops, _ = run(probe_rows)
         rate = probe_ops / max(time.perf_counter() - t0, 1e-6)
-        rows = int(max(8, min(TOKENS, target_seconds * rate / (probe_ops / 8))))
+        rows = int(max(probe_rows, min(tokens, target_seconds * rate / (probe_ops / probe_rows))))
     t0 = time.perf_counter()
-    ops = run(rows)
+    ops, _ = run(rows)
     seconds = time.perf_counter() - t0
     pool.shutdown()
     return {
@@ -650,9 +972,133 @@ def cpu_reference_sample(*, target_seconds: float, rows: int | None = None) -> d
         "cores": cores,
         "kind": "port",
         "seconds": round(seconds, 3),
-        "sample": f"{rows} token rows x {columns} output columns of each 70B FFN projection at full K "
+        "sample": f"{rows} token rows x {CPU_COLUMNS} output columns of each {label} projection at full K "
         "(NumPy int32 matmul split over output columns across host threads)",
     }
+
+
+def cpu_torch_int32_sample(*, workload_shapes: list[tuple[str, int, int]], tokens: int, target_seconds: float) -> dict[str, object]:
+    """The reference benchmark's second CPU baseline, its torch int32 path
+    (examples/benchmark_qpu_xla_w8a8.py:227-238: amax/127 floored at 1/127, round, clamp, int32
+    matmul, fp32 dequant), on ``rows`` token rows x at most 1024 output columns per projection,
+    torch using every host thread."""
+    import torch
+
+    cores = host_cores()
+    torch.set_num_threads(cores)
+    generator = torch.Generator().manual_seed(SEED)
+    samples = []
+    for _, k, n in workload_shapes:
+        x = torch.randn((tokens, k), generator=generator, dtype=torch.float32)
+        w = torch.randint(-127, 128, (min(CPU_COLUMNS, n), k), generator=generator, dtype=torch.int32)
+        ws = torch.rand((min(CPU_COLUMNS, n),), generator=generator, dtype=torch.float32) * 0.001 + 1e-4
+        samples.append((x, w, ws))
+
+    def run(rows: int) -> float:
+        ops = 0.0
+        for x, w, ws in samples:
+            xs = x[:rows]
+            scales = torch.maximum(torch.amax(torch.abs(xs), dim=1) / 127, torch.tensor(1.0 / 127.0))
+            q = torch.round(xs / scales[:, None]).clamp(-127, 127).to(torch.int32)
+            acc = q @ w.T
+            _ = acc.to(torch.float32) * scales[:, None] * ws[None, :]
+            ops += 2.0 * rows * w.shape[0] * w.shape[1]
+        return ops
+
+    probe_rows = min(32, tokens)
+    t0 = time.perf_counter()
+    probe = run(probe_rows)
+    rate = probe / max(time.perf_counter() - t0, 1e-6)
+    rows = int(max(probe_rows, min(tokens, target_seconds * rate / (probe / probe_rows))))
+    t0 = time.perf_counter()
+    ops = run(rows)
+    seconds = time.perf_counter() - t0
+    return {
+        "value": ops / seconds / 1e12,
+        "unit": "TOPS",
+        "cores": cores,
+        "kind": "port",
+        "seconds": round(seconds, 3),
+        "sample": f"{rows} token rows x {CPU_COLUMNS} output columns per projection at full K (torch int32 matmul)",
+    }
+
+
+def cpu_square(target_seconds: float) -> dict[str, object]:
+    """The reference's CPU path on the square cases, whole workload (NumPy int32 and torch int32)."""
+    import numpy as np
+
+    from oracle import qpu_oracle as oracle
+    from qpu_xla import workloads
+
+    result: dict[str, object] = {"kind": "port", "cores": host_cores()}
+    for size in (64, 512):
+        case = workloads.square_case(size)
+        values, scales = oracle.quantize_per_output_channel_int8(case.weight)
+        w32 = values.astype(np.int32)
+        reps = 0
+        t0 = time.perf_counter()
+        while reps < 3 or time.perf_counter() - t0 < min(1.0, target_seconds / 2):
+            q, s = oracle.quantize_rows_int8(case.source)
+            y = oracle.w8a8_dequantize(q.astype(np.int32) @ w32.T, s, scales)
+            if case.bias is not None:
+                y = y + case.bias
+            reps += 1
+        seconds = (time.perf_counter() - t0) / reps
+        result[str(size)] = {"numpy_int32_tops": 2.0 * size**3 / seconds / 1e12, "us_per_call": round(seconds * 1e6, 1)}
+    result["sample"] = "the whole square workload per call (NumPy int32 path of quantization.py:1065-1082)"
+    return result
+
+
+def cpu_tinyllama_w8a8(target_seconds: float) -> dict[str, object]:
+    from qpu_xla import workloads
+
+    layer = [(s.name, s.in_features, s.out_features) for s in workloads.TINYLLAMA_LAYER]
+    result: dict[str, object] = {"kind": "port", "cores": host_cores()}
+    for tokens in workloads.TINYLLAMA_TOKENS:
+        sample = cpu_reference_sample(target_seconds=target_seconds / 3, workload_shapes=layer, tokens=tokens, label="TinyLlama")
+        result[str(tokens)] = {"numpy_int32_tops": sample["value"], "sample": sample["sample"]}
+    result["torch_int32"] = cpu_torch_int32_sample(workload_shapes=layer, tokens=2048, target_seconds=target_seconds / 3)
+    return result
+
+
+def cpu_q4_0(target_seconds: float) -> dict[str, object]:
+    """ggml_q4_0_q8_0_reference (NumPy port, ggml_q4_0.py:81-100) on the TinyLlama Q4_0 shapes."""
+    import numpy as np
+
+    from oracle import qpu_oracle as oracle
+    from qpu_xla import workloads
+
+    result: dict[str, object] = {"kind": "port", "cores": 1}
+    for shape in workloads.TINYLLAMA_Q4_0_SHAPES:
+        for rows in (1, 4):
+            source, weight = workloads.q4_0_case(shape, rows)
+            blocks = oracle.quantize_q4_0(weight)
+            act = oracle.quantize_q8_0(source)
+            reps = 0
+            t0 = time.perf_counter()
+            while reps < 2 or time.perf_counter() - t0 < target_seconds / 4:
+                oracle.q4_0_q8_0_linear(act, blocks)
+                reps += 1
+            seconds = (time.perf_counter() - t0) / reps
+            nbytes = 18.0 * shape.out_features * shape.in_features / 32 + 34.0 * rows * shape.in_features / 32 + 4.0 * rows * shape.out_features
+            result[f"{shape.name}_m{rows}"] = {"gbs": round(nbytes / seconds / 1e9, 3), "ms_per_call": round(seconds * 1e3, 2)}
+    result["sample"] = "the whole matvec per call (NumPy block loop of ggml_q4_0_q8_0_reference)"
+    return result
+
+
+def cpu_llama7b(target_seconds: float) -> dict[str, object]:
+    from qpu_xla import workloads
+
+    ffn = [(s.name, s.in_features, s.out_features) for s in workloads.LLAMA2_7B_FFN]
+    return cpu_reference_sample(target_seconds=target_seconds, workload_shapes=ffn, tokens=TOKENS, label="7B FFN")
+
+
+OBJECT_CPU: dict[str, Callable[[float], dict[str, object]]] = {
+    "square": cpu_square,
+    "tinyllama_w8a8": cpu_tinyllama_w8a8,
+    "tinyllama_q4_0": cpu_q4_0,
+    "llama7b_ffn": cpu_llama7b,
+}
 
 
 def run_reference(args: argparse.Namespace) -> None:
@@ -684,8 +1130,13 @@ def run_reference(args: argparse.Namespace) -> None:
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "int8",
-        "data": "synthetic: seeded N(0,1) activations, N(0,0.02) weights",
-        "config": {"workload": WORKLOAD, "tokens": TOKENS, "parallelism": "host CPU (reference CPU path)"},
+        "data": "synthetic: seeded N(0,1) activations, N(0,0.02) random-init weights (torch CUDA generator, seed 4)",
+        "config": {
+            "workload": WORKLOAD,
+            "tokens": TOKENS,
+            "projections": [f"{name} {k}->{n}" for name, k, n in shapes()],
+            "parallelism": "host CPU (the reference's CPU path, NumPy port)",
+        },
         "cpu_baseline": {"value": value, "unit": "TOPS", "cores": first["cores"], "kind": "port", "sample": first["sample"]},
         "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -695,13 +1146,15 @@ def run_reference(args: argparse.Namespace) -> None:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=300)
+    parser.add_argument("--steps", type=int, default=20)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-seconds", type=float, default=15.0)
     parser.add_argument("--only", default="", help="comma-separated projections (profiling captures only)")
+    parser.add_argument("--objects", default=None,
+                        help=f"comma-separated subset of {','.join(OBJECTS)} to time at N = 1 (default all; empty string: none)")
     parser.add_argument(
         "--exchange",
         choices=("fused", "nccl"),
@@ -712,6 +1165,15 @@ def main() -> None:
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     ONLY.update(name for name in args.only.split(",") if name)
+    if args.objects is None:
+        args.objects = list(OBJECTS)
+    else:
+        args.objects = [o for o in args.objects.split(",") if o]
+        unknown = set(args.objects) - set(OBJECTS)
+        if unknown:
+            raise SystemExit(f"unknown --objects {sorted(unknown)}; choose from {OBJECTS}")
+        if not args.objects:
+            args.objects = ["__none__"]
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -84,6 +84,17 @@ size_t qpucuda_w8a8_linear_resident_bytes(const qpucuda_w8a8_linear *linear);
  * the wait for the whole call has succeeded. */
 qpucuda_status qpucuda_w8a8_linear_execute(qpucuda_w8a8_linear *linear, const qpucuda_w8a8_execution *execution);
 
+/* qpucuda_w8a8_linear_execute for a destination in page-locked host memory
+ * (cudaMallocHost, cudaHostAlloc or cudaHostRegister over the whole range;
+ * otherwise QPUCUDA_INVALID_ARGUMENT): the device-to-host copies write the
+ * results straight into it, overlapping the kernels, with no staging copy on
+ * the host. The price is the failure rule: after a failed or timed-out wait the
+ * destination may hold part of the results (the staged entry point above leaves
+ * it untouched, as the reference's Q4_0 operator does). No counterpart in the
+ * reference, whose W8A8 operator has no C form. */
+qpucuda_status qpucuda_w8a8_linear_execute_direct(qpucuda_w8a8_linear *linear,
+                                                  const qpucuda_w8a8_execution *execution);
+
 /* Device pointers, asynchronous on the context stream:
  * quantize source rows into the plan scratch, GEMM (tcgen05 kind::i8 for
  * rows > 8, int8 dot-product GEMV otherwise), fused dequant (+ bias) into

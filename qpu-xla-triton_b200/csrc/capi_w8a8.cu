@@ -107,10 +107,12 @@ qpucuda_status enqueue(qpucuda_w8a8_linear *linear, const float *source, size_t 
                        float *destination, size_t destination_stride);
 
 // Pipelined host-buffer execution: slice s is copied in on copy_in, quantized and multiplied on
-// the context stream after its copy, and copied out to the pinned staging on copy_out after its
+// the context stream after its copy, and copied out to host_out (the plan's pinned staging, or
+// the caller's page-locked destination in direct mode) on copy_out after its
 // GEMM (events 1 + 2s copied in, 2 + 2s computed); the last copy-out is joined back into the
 // context stream, whose bounded wait then covers every copy and kernel of the call.
-qpucuda_status enqueue_sliced(qpucuda_w8a8_linear *linear, const float *source, uint32_t rows, uint32_t slices) {
+qpucuda_status enqueue_sliced(qpucuda_w8a8_linear *linear, const float *source, uint32_t rows, uint32_t slices,
+                              float *host_out) {
     qpucuda_context *context = linear->context;
     cudaEvent_t *events = linear->events.data();
     cudaError_t error = cudaEventRecord(events[0], context->stream);  // earlier work on the stream comes first
@@ -135,7 +137,7 @@ qpucuda_status enqueue_sliced(qpucuda_w8a8_linear *linear, const float *source, 
         error = cudaEventRecord(computed, context->stream);
         if (error == cudaSuccess) error = cudaStreamWaitEvent(linear->copy_out, computed, 0);
         if (error == cudaSuccess)
-            error = cudaMemcpyAsync(linear->h_destination + static_cast<size_t>(first) * linear->columns,
+            error = cudaMemcpyAsync(host_out + static_cast<size_t>(first) * linear->columns,
                                     linear->d_destination + static_cast<size_t>(first) * linear->columns,
                                     static_cast<size_t>(count) * linear->columns * sizeof(float),
                                     cudaMemcpyDeviceToHost, linear->copy_out);
@@ -442,7 +444,23 @@ qpucuda_status qpucuda_w8a8_linear_execute_prepared_device(qpucuda_w8a8_linear *
     return enqueue(linear, nullptr, 0, quantized, quantized_stride, row_scales, rows, destination, destination_stride);
 }
 
-qpucuda_status qpucuda_w8a8_linear_execute(qpucuda_w8a8_linear *linear, const qpucuda_w8a8_execution *execution) {
+}  // extern "C"
+
+namespace {
+
+bool page_locked(const void *pointer) {
+    cudaPointerAttributes attributes;
+    if (cudaPointerGetAttributes(&attributes, pointer) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return false;
+    }
+    return attributes.type == cudaMemoryTypeHost;
+}
+
+// Host-buffer execution. Staged (direct == false): results land in plan-owned pinned staging and
+// reach the caller's destination only after a successful wait. Direct: the destination is the
+// caller's page-locked memory and the device-to-host copies write it in place.
+qpucuda_status execute_host(qpucuda_w8a8_linear *linear, const qpucuda_w8a8_execution *execution, bool direct) {
     if (linear == nullptr || execution == nullptr) return QPUCUDA_INVALID_ARGUMENT;
     qpucuda_context *context = linear->context;
     const uint32_t rows = execution->rows;
@@ -455,6 +473,11 @@ qpucuda_status qpucuda_w8a8_linear_execute(qpucuda_w8a8_linear *linear, const qp
     }
     if (rows > kGemvMaxRows && !(context->cc_major == 10 && context->cc_minor == 0)) {
         return fail(context, QPUCUDA_CAPABILITY_MISSING, "the tcgen05 int8 GEMM needs an sm_100 device");
+    }
+    if (direct && (!page_locked(execution->destination) ||
+                   !page_locked(reinterpret_cast<const char *>(execution->destination) + destination_bytes - 1))) {
+        return fail(context, QPUCUDA_INVALID_ARGUMENT,
+                    "direct W8A8 execution needs a page-locked destination (cudaMallocHost or cudaHostRegister)");
     }
     {
         std::lock_guard<std::mutex> guard(linear->mutex);
@@ -499,6 +522,7 @@ qpucuda_status qpucuda_w8a8_linear_execute(qpucuda_w8a8_linear *linear, const qp
     if (slices > 1 && !ensure_pipeline(linear, slices)) {
         return release(fail(context, QPUCUDA_ALLOCATION_FAILED, "create W8A8 copy streams"));
     }
+    float *host_out = direct ? execution->destination : linear->h_destination;
     cudaError_t error = cudaSuccess;
     if (slices == 1) {
         error = cudaMemcpyAsync(linear->d_source, execution->source, source_bytes, cudaMemcpyHostToDevice,
@@ -507,11 +531,11 @@ qpucuda_status qpucuda_w8a8_linear_execute(qpucuda_w8a8_linear *linear, const qp
         status = enqueue(linear, linear->d_source, linear->k, nullptr, 0, nullptr, rows, linear->d_destination,
                          linear->columns);
         if (status != QPUCUDA_OK) return release(status);
-        error = cudaMemcpyAsync(linear->h_destination, linear->d_destination, destination_bytes,
-                                cudaMemcpyDeviceToHost, context->stream);
+        error = cudaMemcpyAsync(host_out, linear->d_destination, destination_bytes, cudaMemcpyDeviceToHost,
+                                context->stream);
         if (error != cudaSuccess) return release(cuda_fail(context, error, "copy W8A8 destination"));
     } else {
-        status = enqueue_sliced(linear, static_cast<const float *>(execution->source), rows, slices);
+        status = enqueue_sliced(linear, static_cast<const float *>(execution->source), rows, slices, host_out);
         if (status != QPUCUDA_OK) {
             (void)wait_stream(context);  // drain whatever was issued before the failure (bounded)
             drain_copies(linear);
@@ -520,11 +544,24 @@ qpucuda_status qpucuda_w8a8_linear_execute(qpucuda_w8a8_linear *linear, const qp
     }
     status = wait_stream(context);
     if (status == QPUCUDA_OK) {
-        parallel_memcpy(execution->destination, linear->h_destination, destination_bytes);
+        if (!direct) parallel_memcpy(execution->destination, linear->h_destination, destination_bytes);
     } else if (slices > 1) {
         drain_copies(linear);
     }
     return release(status);
+}
+
+}  // namespace
+
+extern "C" {
+
+qpucuda_status qpucuda_w8a8_linear_execute(qpucuda_w8a8_linear *linear, const qpucuda_w8a8_execution *execution) {
+    return execute_host(linear, execution, false);
+}
+
+qpucuda_status qpucuda_w8a8_linear_execute_direct(qpucuda_w8a8_linear *linear,
+                                                  const qpucuda_w8a8_execution *execution) {
+    return execute_host(linear, execution, true);
 }
 
 qpucuda_status qpucuda_w8a8_linear_scratch(const qpucuda_w8a8_linear *linear, const int8_t **quantized,

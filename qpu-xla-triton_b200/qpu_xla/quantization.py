@@ -429,17 +429,27 @@ class PreparedW8A8Linear:
             ),
         )
 
-    def execute_host(self: Self, source: npt.NDArray[np.float32], destination: npt.NDArray[np.float32] | None = None) -> npt.NDArray[np.float32]:
-        """Host buffers through ``qpucuda_w8a8_linear_execute`` (synchronous, bounded wait)."""
+    def execute_host(
+        self: Self, source: npt.NDArray[np.float32], destination: npt.NDArray[np.float32] | None = None, *, direct: bool = False
+    ) -> npt.NDArray[np.float32]:
+        """Host buffers through ``qpucuda_w8a8_linear_execute`` (synchronous, bounded wait).
+
+        ``direct=True`` calls ``qpucuda_w8a8_linear_execute_direct`` instead: ``destination`` must
+        then be page-locked host memory (e.g. a ``pin_memory=True`` torch tensor's ``.numpy()``),
+        the results are copied into it by DMA with no staging copy, and a failed wait may leave
+        part of the results in it."""
         source = np.ascontiguousarray(source, dtype=np.float32)
         batch = source.shape[0]
         if destination is None:
+            if direct:
+                raise ValueError("direct host execution needs a page-locked destination")
             destination = np.empty((batch, self.output_count), dtype=np.float32)
         execution = _native.W8A8Execution(source.ctypes.data, source.nbytes, destination.ctypes.data, destination.nbytes, batch)
+        name = "qpucuda_w8a8_linear_execute_direct" if direct else "qpucuda_w8a8_linear_execute"
         with self._backend.launch_lock:  # type: ignore[attr-defined]
             self._native.use_library_stream()
-            status = self._native.library.qpucuda_w8a8_linear_execute(self._handle, ctypes.byref(execution))
-        self._native.check(status, "qpucuda_w8a8_linear_execute")
+            status = getattr(self._native.library, name)(self._handle, ctypes.byref(execution))
+        self._native.check(status, name)
         return destination
 
 

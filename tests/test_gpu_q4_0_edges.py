@@ -128,12 +128,12 @@ def test_extreme_codes_and_short_reductions(native, rows: int, blocks: int) -> N
         # the single-kernel entry point reads the native 18-byte blocks without a repack
         act = torch.from_numpy(activation).cuda()
         weight = torch.from_numpy(np.ascontiguousarray(weights[16:48])).cuda()
-        out = torch.full((rows, 40), float("nan"), dtype=torch.float32, device="cuda")
-        native.check("qpucuda_ggml_q4_0_q8_0_linear", act.data_ptr(), rows, blocks, weight.data_ptr(), 32, out.data_ptr(), 40, 0, 8, 32)
+        out = torch.full((rows, 48), float("nan"), dtype=torch.float32, device="cuda")
+        native.check("qpucuda_ggml_q4_0_q8_0_linear", act.data_ptr(), rows, blocks, weight.data_ptr(), 32, out.data_ptr(), 48, 0, 16, 32)
         native.sync()
         got = out.cpu().numpy()
-        np.testing.assert_array_equal(got[:, 8:40], expected[:, 16:48])
-        assert np.isnan(got[:, :8]).all()
+        np.testing.assert_array_equal(got[:, 16:48], expected[:, 16:48])
+        assert np.isnan(got[:, :16]).all()
 
 
 def test_repack_keeps_extreme_blocks(native) -> None:  # type: ignore[no-untyped-def]

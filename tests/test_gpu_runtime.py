@@ -102,6 +102,28 @@ def test_host_execute_of_a_large_batch_is_sliced_and_exact(cuda_device: Device) 
             np.testing.assert_array_equal(plan.execute_host(source), expected)
 
 
+def test_direct_host_execute_writes_a_page_locked_destination_in_place(cuda_device: Device) -> None:
+    """qpucuda_w8a8_linear_execute_direct: the same results as the staged host call, written by
+    DMA into a page-locked destination (sliced and single-slice batches, GEMM and GEMV rows);
+    a pageable destination is refused before anything runs."""
+    import torch
+
+    rng = np.random.default_rng(72)
+    rows, k, n = 2300, 256, 512
+    weight = rng.standard_normal((n, k)).astype(np.float32)
+    values, scales = oracle.quantize_per_output_channel_int8(weight)
+    with PreparedW8A8Linear(cuda_device, QuantizedMatrixInt8(values, scales), max_batch=rows) as plan:
+        for batch in (rows, 700, 3):
+            source = torch.from_numpy(rng.standard_normal((batch, k)).astype(np.float32)).pin_memory()
+            pinned = torch.full((batch, n), float("nan"), dtype=torch.float32).pin_memory()
+            plan.execute_host(source.numpy(), pinned.numpy(), direct=True)
+            np.testing.assert_array_equal(pinned.numpy(), oracle.w8a8_linear(source.numpy(), values, scales))
+        pageable = np.full((3, n), np.nan, dtype=np.float32)
+        with pytest.raises(ValueError, match="page-locked"):
+            plan.execute_host(rng.standard_normal((3, k)).astype(np.float32), pageable, direct=True)
+        assert np.isnan(pageable).all()
+
+
 def test_two_contexts_driven_from_two_threads_at_once() -> None:
     """Two contexts on one device, each called from its own host thread at the same time (the C
     calls release the GIL): every kernel's one-time set-up is per device and thread-safe, and each

@@ -221,25 +221,27 @@ class Bench:
         """A C-ABI call on the bench stream: ``call(library, context handle) -> status``."""
         self.device.backend.launch(self.stream, lambda n: n.check(call(n.library, n.handle), "bench"))
 
-    def prime(self) -> None:
+    def prime(self, launches: int = 2) -> None:
         """Flush L2 (write one buffer larger than L2, then read another so the lines left are
-        clean), then hold the stream ~60 us so the host has queued the bracketed launches
-        before the start event executes (no host launch latency inside a timed bracket)."""
+        clean), then hold the stream long enough (~40 us per bracketed launch, at least 60 us)
+        for the host to queue the bracketed launches before the start event executes, so no
+        host launch latency falls inside a timed bracket."""
         import torch
 
         self.flush.zero_()
         self.flush_clean.sum()
-        torch.cuda._sleep(120_000)
+        torch.cuda._sleep(max(120_000, 80_000 * launches))
 
-    def brackets(self, fn: Callable[[], None], reps: int, warmup: int = 3) -> list[float]:
-        """``reps`` CUDA-event brackets of ``fn`` on the bench stream, L2 flushed before each; ms."""
+    def brackets(self, fn: Callable[[], None], reps: int, warmup: int = 3, launches: int = 2) -> list[float]:
+        """``reps`` CUDA-event brackets of ``fn`` (``launches`` kernel launches) on the bench
+        stream, L2 flushed before each; ms."""
         import torch
 
         for _ in range(warmup):
             fn()
         events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
         for start, end in events:
-            self.prime()
+            self.prime(launches)
             start.record(self.stream)
             fn()
             end.record(self.stream)
@@ -529,7 +531,7 @@ def run_ours(args: argparse.Namespace) -> None:
             for q4, act, out in q4_inputs:
                 q4.forward(act, out=out)
 
-        q4_ms = statistics.mean(bench.brackets(decode_ffn, reps))
+        q4_ms = statistics.mean(bench.brackets(decode_ffn, reps, launches=len(q4_inputs)))
         q4_seconds = max_over_ranks(q4_ms * 1e-3)
         q4_rows[str(rows)] = {
             "value": round(sum_over_ranks(q4_bytes_rank) / q4_seconds / 1e9, 1),
@@ -556,7 +558,7 @@ def run_ours(args: argparse.Namespace) -> None:
             float(p["gather"].count) * p["k"] + gemv_rows * p["k"] + 4.0 * (p["gather"].count + gemv_rows + gemv_rows * p["gather"].count)
             for p in projections
         )
-        gemv_step_ms = max_over_ranks(statistics.mean(bench.brackets(decode_w8a8, reps)))
+        gemv_step_ms = max_over_ranks(statistics.mean(bench.brackets(decode_w8a8, reps, launches=2 * len(projections))))
         w8a8_gemv[str(gemv_rows)] = {
             "value": round(sum_over_ranks(gemv_bytes_rank) / (gemv_step_ms * 1e-3) / 1e9, 1),
             "rank_gbs": round(gemv_bytes_rank / (gemv_step_ms * 1e-3) / 1e9, 1),
@@ -769,7 +771,7 @@ def object_tinyllama_w8a8(bench: Bench, int8_peak: float, hbm_peak: float, int8_
                 for plan, src, out in zip(plans, sources, outs):
                     plan.forward(src, out=out)
 
-            ms = statistics.median(bench.brackets(layer, 20))
+            ms = statistics.median(bench.brackets(layer, 20, launches=2 * len(plans)))
             ops = sum(2.0 * tokens * s.in_features * s.out_features for s in shapes7)
             k16 = [((s.in_features + 15) // 16) * 16 for s in shapes7]
             nbytes = sum(s.out_features * k + tokens * s.in_features * 4.0 + tokens * k + 4.0 * (s.out_features + tokens + tokens * s.out_features)
@@ -816,7 +818,7 @@ def object_tinyllama_q4_0(bench: Bench, int8_peak: float, hbm_peak: float, int8_
                     for plan in copies:
                         plan.forward(act, out=out)
 
-                ms = statistics.median(bench.brackets(run, 20))
+                ms = statistics.median(bench.brackets(run, 20, launches=len(copies)))
                 per_launch = 18.0 * shape.out_features * shape.in_features / 32 + 34.0 * rows * shape.in_features / 32 + 4.0 * rows * shape.out_features
                 seconds = ms * 1e-3 / Q4_0_COPIES
                 entry[str(rows)] = {
@@ -873,7 +875,7 @@ def object_llama7b_ffn(bench: Bench, int8_peak: float, hbm_peak: float, int8_not
             for q4, act, out in decode:
                 q4.forward(act, out=out)
 
-        q4_ms = statistics.median(bench.brackets(decode_ffn, 20))
+        q4_ms = statistics.median(bench.brackets(decode_ffn, 20, launches=len(decode)))
     finally:
         for p in prefill:
             p.plan.close()

@@ -247,6 +247,73 @@ __device__ __forceinline__ float dequant(uint32_t bits, float row_scale, float c
     return __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(bits)), row_scale), col_scale);
 }
 
+// Packed fp32 pairs (sm_100 mul.f32x2 with explicit round-to-nearest): each half rounds exactly
+// as __fmul_rn, two values per instruction.
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+    return static_cast<unsigned long long>(__float_as_uint(lo)) | (static_cast<unsigned long long>(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// One row's 32 accumulators of columns n0 .. n0 + 31 (all in range), dequantized in place:
+// ((float)acc * row_scale) * col_scale[n] (+ bias[n]) in that order, the scales and bias read
+// with one 16-byte load per four columns (every lane reads the same address). `cs` and `cb` are
+// 16-byte aligned.
+template <bool BIAS>
+__device__ __forceinline__ void dequant_chunk_vec(uint32_t (&r)[32], float row_scale, const float *cs, const float *cb) {
+    const unsigned long long row2 = pack2(row_scale, row_scale);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const float4 c = __ldg(reinterpret_cast<const float4 *>(cs) + q);
+        unsigned long long lo = pack2(__int2float_rn(static_cast<int>(r[4 * q])), __int2float_rn(static_cast<int>(r[4 * q + 1])));
+        unsigned long long hi = pack2(__int2float_rn(static_cast<int>(r[4 * q + 2])), __int2float_rn(static_cast<int>(r[4 * q + 3])));
+        lo = mul2(mul2(lo, row2), pack2(c.x, c.y));
+        hi = mul2(mul2(hi, row2), pack2(c.z, c.w));
+        float v0 = __uint_as_float(static_cast<uint32_t>(lo)), v1 = __uint_as_float(static_cast<uint32_t>(lo >> 32));
+        float v2 = __uint_as_float(static_cast<uint32_t>(hi)), v3 = __uint_as_float(static_cast<uint32_t>(hi >> 32));
+        if constexpr (BIAS) {
+            const float4 b = __ldg(reinterpret_cast<const float4 *>(cb) + q);
+            v0 = __fadd_rn(v0, b.x);
+            v1 = __fadd_rn(v1, b.y);
+            v2 = __fadd_rn(v2, b.z);
+            v3 = __fadd_rn(v3, b.w);
+        }
+        r[4 * q] = __float_as_uint(v0);
+        r[4 * q + 1] = __float_as_uint(v1);
+        r[4 * q + 2] = __float_as_uint(v2);
+        r[4 * q + 3] = __float_as_uint(v3);
+    }
+}
+
+// The same for a chunk with `valid` (< 32) columns in range, or unaligned scales: scalar loads
+// (every lane reads the same address), zeros past the last column.
+__device__ __forceinline__ void dequant_chunk_scalar(uint32_t (&r)[32], float row_scale, const float *cs, const float *cb,
+                                                     bool with_bias, uint32_t valid) {
+#pragma unroll
+    for (uint32_t j = 0; j < 32; ++j) {
+        const bool in_range = j < valid;
+        float v = dequant(r[j], row_scale, in_range ? __ldg(cs + j) : 0.0f);
+        if (with_bias) v = __fadd_rn(v, in_range ? __ldg(cb + j) : 0.0f);
+        r[j] = __float_as_uint(v);
+    }
+}
+
+__device__ __forceinline__ void dequant_chunk(uint32_t (&r)[32], float row_scale, const float *cs, const float *cb,
+                                              bool with_bias, uint32_t valid, bool vector_scales) {
+    if (valid >= 32 && vector_scales) {
+        if (with_bias) {
+            dequant_chunk_vec<true>(r, row_scale, cs, cb);
+        } else {
+            dequant_chunk_vec<false>(r, row_scale, cs, cb);
+        }
+    } else {
+        dequant_chunk_scalar(r, row_scale, cs, cb, with_bias, valid);
+    }
+}
+
 // Four consecutive 4-byte outputs of one row, columns col..col+3 (the caller guarantees
 // col < n); a 16-byte store when the whole group is in range and aligned.
 __device__ __forceinline__ void store_group(void *base, size_t offset, uint4 value, uint32_t valid, bool aligned) {
@@ -333,9 +400,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             prefetch_tensor_map(&map_a);
             prefetch_tensor_map(&map_w);
             uint32_t stage = 0, phase = 0;
-            uint32_t issued_phase[STAGES];
-            bool issued[STAGES];
-            for (int s = 0; s < STAGES; ++s) issued[s] = false;
+            // Per stage (bit s): a copy was issued on it, and the phase it was issued in. Bit masks
+            // rather than arrays indexed by the runtime stage, which would live in local memory.
+            uint32_t issued_mask = 0, issued_phases = 0;
             bool ok = true;
             for (uint32_t tile = first_tile; ok && tile < num_tiles; tile += tile_step) {
                 const int m0 = static_cast<int>((tile % params.m_blocks) * kTileRows + rank * BM);
@@ -365,8 +432,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         tma_load_2d(smem_u32(stage_b + stage * B_STAGE_BYTES + W_BOX_ROWS * BK), &map_w, full, x,
                                     n0 + W_BOX_ROWS);
                     }
-                    issued[stage] = true;
-                    issued_phase[stage] = phase;
+                    issued_mask |= 1u << stage;
+                    issued_phases = (issued_phases & ~(1u << stage)) | (phase << stage);
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1u;
@@ -379,7 +446,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 // gives its copies in flight a bounded 200 us instead.
                 if (!PAIR || leader) {
                     for (int s = 0; s < STAGES; ++s) {
-                        if (issued[s]) wait_drain(smem_u32(&control->full[s]), issued_phase[s]);
+                        if ((issued_mask >> s) & 1u) wait_drain(smem_u32(&control->full[s]), (issued_phases >> s) & 1u);
                     }
                 } else {
                     const uint64_t start = globaltimer();
@@ -469,6 +536,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (tma_store && lane == 0) prefetch_tensor_map(&map_out);
         const bool s32 = params.mode == static_cast<int>(EpilogueMode::kStoreS32);
         const bool with_bias = params.mode == static_cast<int>(EpilogueMode::kDequantizeBias);
+        // Column scales and bias in 16-byte loads (chunks start at multiples of 32 columns).
+        const bool vector_scales = (reinterpret_cast<uintptr_t>(params.col_scales) & 15u) == 0 &&
+                                   (!with_bias || (reinterpret_cast<uintptr_t>(params.bias) & 15u) == 0);
         // Row-segment stores need unit column stride; otherwise (NCHW outputs) each lane stores its
         // own row's values straight from registers, which is coalesced when rows are adjacent.
         const bool row_segments = params.col_stride == 1;
@@ -516,13 +586,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     // Rows past m and columns past n fall outside the tensor map and are not written.
                     if (row0 >= params.m) continue;  // warp-uniform
                     if (!s32) {
-#pragma unroll
-                        for (uint32_t j = 0; j < 32; ++j) {
-                            const bool in_range = full_chunk || n0 + j < params.n;
-                            float v = dequant(r[j], row_scale, in_range ? __ldg(params.col_scales + n0 + j) : 0.0f);
-                            if (with_bias) v = __fadd_rn(v, in_range ? __ldg(params.bias + n0 + j) : 0.0f);
-                            r[j] = __float_as_uint(v);
-                        }
+                        dequant_chunk(r, row_scale, params.col_scales + n0, params.bias + n0, with_bias,
+                                      full_chunk ? 32u : params.n - n0, vector_scales);
                     }
                     uint4 *buffer = staging + (stores_issued & 1u) * 256u;
                     if (lane == 0) bulk_wait_read_all_but_one();  // the store from this buffer has read it
@@ -554,7 +619,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                     make_int4(static_cast<int>(r[j]), static_cast<int>(r[j + 1]), static_cast<int>(r[j + 2]),
                                               static_cast<int>(r[j + 3]));
                         } else {
-                            for (uint32_t j = 0; j < 32 && n0 + j < params.n; ++j) row[j] = static_cast<int>(r[j]);
+                            // fully unrolled: r stays in registers (a runtime-bounded index would
+                            // move the whole array to local memory)
+#pragma unroll
+                            for (uint32_t j = 0; j < 32; ++j)
+                                if (n0 + j < params.n) row[j] = static_cast<int>(r[j]);
                         }
                     } else {
                         // Column scales / bias: every lane reads the same address (an L1 broadcast).
@@ -562,43 +631,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         const float *cb = params.bias + n0;
                         float *row = static_cast<float *>(params.out) + row_base + n0;
                         if (full_chunk && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
-                            float v[32];
-#pragma unroll
-                            for (int j = 0; j < 32; ++j) {
-                                v[j] = dequant(r[j], row_scale, __ldg(cs + j));
-                                if (with_bias) v[j] = __fadd_rn(v[j], __ldg(cb + j));
-                            }
+                            dequant_chunk(r, row_scale, cs, cb, with_bias, 32u, vector_scales);
 #pragma unroll
                             for (int j = 0; j < 32; j += 4)
-                                *reinterpret_cast<float4 *>(row + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                                *reinterpret_cast<uint4 *>(row + j) = make_uint4(r[j], r[j + 1], r[j + 2], r[j + 3]);
                         } else {
-                            for (uint32_t j = 0; j < 32 && n0 + j < params.n; ++j) {
-                                float v = dequant(r[j], row_scale, __ldg(cs + j));
-                                if (with_bias) v = __fadd_rn(v, __ldg(cb + j));
-                                row[j] = v;
-                            }
+                            const uint32_t valid = full_chunk ? 32u : params.n - n0;
+                            dequant_chunk(r, row_scale, cs, cb, with_bias, valid, vector_scales);
+#pragma unroll
+                            for (uint32_t j = 0; j < 32; ++j)
+                                if (j < valid) row[j] = __uint_as_float(r[j]);
                         }
                     }
                     continue;
                 }
                 if (!s32) {
-                    // Column scales / bias: every lane reads the same address (an L1 broadcast).
-                    if (full_chunk) {
-#pragma unroll
-                        for (uint32_t j = 0; j < 32; ++j) {
-                            float v = dequant(r[j], row_scale, __ldg(params.col_scales + n0 + j));
-                            if (with_bias) v = __fadd_rn(v, __ldg(params.bias + n0 + j));
-                            r[j] = __float_as_uint(v);
-                        }
-                    } else {
-#pragma unroll
-                        for (uint32_t j = 0; j < 32; ++j) {
-                            const bool in_range = n0 + j < params.n;
-                            float v = dequant(r[j], row_scale, in_range ? __ldg(params.col_scales + n0 + j) : 0.0f);
-                            if (with_bias) v = __fadd_rn(v, in_range ? __ldg(params.bias + n0 + j) : 0.0f);
-                            r[j] = __float_as_uint(v);
-                        }
-                    }
+                    dequant_chunk(r, row_scale, params.col_scales + n0, params.bias + n0, with_bias,
+                                  full_chunk ? 32u : params.n - n0, vector_scales);
                 }
                 if (!row_segments) {
                     // Column-strided (NCHW) output: each lane stores its own row's values element by

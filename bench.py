@@ -366,6 +366,10 @@ def run_ours(args: argparse.Namespace) -> None:
     if world > 1:
         from datetime import timedelta
 
+        # NCCL's communicator set-up lines (rank count, transports) go to stderr, so a scaling
+        # record shows the ranks the run really had
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=cuda)
     device = Device.open(device_ordinal=local_rank)
     stream = torch.cuda.current_stream(cuda)
@@ -688,7 +692,7 @@ def run_ours(args: argparse.Namespace) -> None:
                 "unit": "GB/s",
                 "frac": w8a8_gemv["1"]["frac"],
                 "peak_source": hbm_note,
-                "traffic": profile_traffic("w8a8_gemv_70b_decode"),
+                "traffic": profile_traffic("objects_traffic", "w8a8_gemv_70b_decode"),
             },
         },
         "clocks": clocks,
@@ -890,7 +894,7 @@ def object_llama7b_ffn(bench: Bench, int8_peak: float, hbm_peak: float, int8_not
         "row_quantizer_ms_per_projection": [round(x, 4) for x in quant_ms],
         "roofline": roofline(kernel="w8a8_gemm_sm100 (in-step events)", seconds=sum(gemm_ms) * 1e-3, ops=sum(ops), nbytes=0.0,
                              int8_peak=int8_peak, hbm_peak=hbm_peak, peak_note=int8_note,
-                             traffic=profile_traffic("objects_traffic", "llama7b_gemm_gate"), traffic_launches=1),
+                             traffic=profile_traffic("objects_traffic", "llama7b_gemm_step")),
         "q4_0_decode": {
             "gbs": round(q4_bytes / (q4_ms * 1e-3) / 1e9, 1),
             "us_per_decode_ffn": round(q4_ms * 1e3, 2),

@@ -128,6 +128,23 @@ struct GemmParams {
 
 using namespace sm100;
 
+// Tile order: groups of kTileGroupRows row blocks, and within a group the row block fastest. The
+// CTAs (pairs) resident at once then cover about 8 row blocks x 9 column blocks, so a group's A
+// rows stay in L2 while its columns stream past, where a row-fastest order over all row blocks
+// re-read the whole A from DRAM on every wave once A outgrew L2 (the 70B down projection's 117 MB
+// A was read 7 times).
+constexpr uint32_t kTileGroupRows = 8;
+__device__ __forceinline__ void tile_coords(uint32_t tile, uint32_t m_blocks, uint32_t n_blocks, uint32_t &m_block,
+                                            uint32_t &n_block) {
+    const uint32_t group_tiles = kTileGroupRows * n_blocks;
+    const uint32_t group = tile / group_tiles;
+    const uint32_t first = group * kTileGroupRows;
+    const uint32_t rows = min(kTileGroupRows, m_blocks - first);
+    const uint32_t local = tile - group * group_tiles;
+    m_block = first + local % rows;
+    n_block = local / rows;
+}
+
 // Bounded wait on this CTA's abort flag (see sm100_sync.cuh).
 template <int NSTAGES>
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, Control<NSTAGES> *control,
@@ -405,8 +422,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t issued_mask = 0, issued_phases = 0;
             bool ok = true;
             for (uint32_t tile = first_tile; ok && tile < num_tiles; tile += tile_step) {
-                const int m0 = static_cast<int>((tile % params.m_blocks) * kTileRows + rank * BM);
-                const int n0 = static_cast<int>((tile / params.m_blocks) * BN);
+                uint32_t m_block, n_block;
+                tile_coords(tile, params.m_blocks, params.n_blocks, m_block, n_block);
+                const int m0 = static_cast<int>(m_block * kTileRows + rank * BM);
+                const int n0 = static_cast<int>(n_block * BN);
                 for (uint32_t kb = 0; kb < params.num_kb; ++kb) {
                     if (!wait_bounded(smem_u32(&control->empty[stage]), phase ^ 1u, control, params.error_word)) {
                         ok = false;
@@ -559,8 +578,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (uint32_t tile = first_tile; tile < num_tiles; tile += tile_step, ++local_tile) {
             const uint32_t acc = local_tile & 1u;
             const uint32_t acc_phase = (local_tile >> 1) & 1u;
-            const uint32_t m_block = tile % params.m_blocks;
-            const uint32_t n_block = tile / params.m_blocks;
+            uint32_t m_block, n_block;
+            tile_coords(tile, params.m_blocks, params.n_blocks, m_block, n_block);
             const uint32_t n_base = n_block * BN;
             bool ok = true;
             if (lane == 0) ok = wait_bounded(smem_u32(&control->tmem_full[acc]), acc_phase, control, params.error_word);

@@ -54,6 +54,12 @@ def main() -> None:
             source = torch.from_numpy(rng.standard_normal((rows, k), dtype=np.float32)).to(cuda)
             full = PreparedW8A8Linear(device, matrix, max_batch=rows, bias=bias)
             expected = full.forward(source)
+            # the 1-GPU result itself against the oracle (the reference's CPU arithmetic), on a row
+            # sample: rows are quantized independently, so a row subset must match bit for bit
+            sample = np.unique(np.linspace(0, rows - 1, num=min(rows, 64)).astype(np.int64))
+            reference = oracle.w8a8_linear(source.cpu().numpy()[sample], values, scales, bias)
+            if not np.array_equal(expected.cpu().numpy()[sample], reference):
+                raise AssertionError(f"rank {rank}: the 1-GPU result differs from the oracle (case {rows}x{k}x{n})")
             sharded = ShardedW8A8Linear(device, matrix, max_batch=rows, bias=bias)
             output = PeerOutput(device, rows, n)
             for attempt in range(2):

@@ -1,22 +1,29 @@
-"""Candidate evidence records (src/qpu_xla/benchmark/candidates.py:13-295), with ``placement="cuda"``.
+"""Candidate evidence records (the drop-in surface of src/qpu_xla/benchmark/candidates.py).
 
 A record ties one kernel specialization (operation, dtype, layout, exact shape
-class) to its numerical and timing evidence. ``CandidateRegistry.supported_for``
-returns only "supported-win" records of one exact operation class; the JSON
-archive (``save`` / ``load``, schema 3) persists every record, including slower
-and quarantined ones.
+class) to the evidence behind its status; ``placement`` may also be ``"cuda"``.
+Only ``supported-win`` records reach placement (``CandidateRegistry.supported_for``);
+the JSON archive keeps every record, slower and quarantined ones included.
+
+The record and evidence classes are frozen dataclasses whose field names are the
+archive's JSON keys. Their checks are written as (condition, message) rules, and the
+archive is read and written generically from the dataclass fields: nested evidence
+objects become JSON objects and tuples become lists, and back.
 """
 
 from __future__ import annotations
 
+import dataclasses
 import json
-from dataclasses import asdict, dataclass
+import typing
+from dataclasses import dataclass
 from enum import Enum
 from os import PathLike
 from statistics import median
 from typing import Any, Self
 
 PLACEMENTS = frozenset({"cpu", "qpu", "hybrid", "cuda"})
+WIN_THRESHOLD = 1.05  # a measured win is at least 5 % faster than the comparison
 
 
 class CandidateStatus(Enum):
@@ -25,6 +32,13 @@ class CandidateStatus(Enum):
     EXPERIMENTAL_CORRECT_SLOWER = "experimental-correct-slower"
     QUARANTINED_INCORRECT = "quarantined-incorrect"
     REFERENCE_ONLY = "reference-only"
+
+
+def _enforce(rules: tuple[tuple[bool, str], ...]) -> None:
+    """Raise ValueError with the message of the first rule that does not hold."""
+    for holds, message in rules:
+        if not holds:
+            raise ValueError(message)
 
 
 @dataclass(frozen=True, slots=True)
@@ -41,12 +55,16 @@ class CorrectnessEvidence:
     inf_count: int = 0
 
     def __post_init__(self: Self) -> None:
-        if not self.reference or self.cases <= 0:
-            raise ValueError("correctness evidence requires a reference and at least one case")
-        errors = (self.max_abs_error, self.mean_abs_error, self.p99_abs_error, self.max_relative_error)
-        counts = (self.saturation_count, self.nan_count, self.inf_count)
-        if any(value < 0 for value in errors) or any(value < 0 for value in counts):
-            raise ValueError("correctness errors and counts cannot be negative")
+        magnitudes = (self.max_abs_error, self.mean_abs_error, self.p99_abs_error, self.max_relative_error,
+                      self.saturation_count, self.nan_count, self.inf_count)
+        _enforce((
+            (bool(self.reference) and self.cases > 0, "correctness evidence requires a reference and at least one case"),
+            (min(magnitudes) >= 0, "correctness errors and counts cannot be negative"),
+        ))
+
+    @property
+    def finite(self: Self) -> bool:
+        return self.nan_count == 0 and self.inf_count == 0
 
 
 @dataclass(frozen=True, slots=True)
@@ -63,21 +81,14 @@ class PerformanceEvidence:
     same_contract_seconds: tuple[float, ...] = ()
 
     def __post_init__(self: Self) -> None:
-        if not self.cpu_reference or not self.cpu_seconds or not self.candidate_seconds:
-            raise ValueError("performance evidence requires both CPU and candidate samples")
-        samples = (
-            *self.cpu_seconds,
-            *self.candidate_seconds,
-            *self.host_prep_seconds,
-            *self.kernel_seconds,
-            *self.cold_start_seconds,
-            *self.dequantization_seconds,
-            *self.same_contract_seconds,
-        )
-        if any(value <= 0 for value in samples):
-            raise ValueError("performance samples must be positive")
-        if bool(self.same_contract_reference) != bool(self.same_contract_seconds):
-            raise ValueError("same-contract performance requires both a reference and samples")
+        samples = [value for item in dataclasses.fields(self) if item.name.endswith("_seconds") for value in getattr(self, item.name)]
+        _enforce((
+            (bool(self.cpu_reference and self.cpu_seconds and self.candidate_seconds),
+             "performance evidence requires both CPU and candidate samples"),
+            (all(value > 0 for value in samples), "performance samples must be positive"),
+            (bool(self.same_contract_reference) == bool(self.same_contract_seconds),
+             "same-contract performance requires both a reference and samples"),
+        ))
 
     @property
     def cpu_median_seconds(self: Self) -> float:
@@ -93,8 +104,7 @@ class PerformanceEvidence:
 
     @property
     def measured_win(self: Self) -> bool:
-        """The reference's five-percent gate (candidates.py:97-100)."""
-        return self.speedup >= 1.05 or self.fused_model_win
+        return self.fused_model_win or self.speedup >= WIN_THRESHOLD
 
     @property
     def same_contract_speedup(self: Self) -> float | None:
@@ -104,8 +114,8 @@ class PerformanceEvidence:
 
     @property
     def same_contract_win(self: Self) -> bool:
-        speedup = self.same_contract_speedup
-        return speedup is not None and speedup >= 1.05
+        ratio = self.same_contract_speedup
+        return ratio is not None and ratio >= WIN_THRESHOLD
 
 
 @dataclass(frozen=True, slots=True)
@@ -118,12 +128,63 @@ class PartitionEvidence:
     alignment: int = 1
 
     def __post_init__(self: Self) -> None:
-        if not self.axis or self.total_units <= 0 or self.alignment <= 0:
-            raise ValueError("partition evidence requires an axis and positive sizes")
-        if self.qpu_units <= 0 or self.qpu_units >= self.total_units:
-            raise ValueError("partition evidence must retain work on both sides")
-        if self.qpu_units % self.alignment:
-            raise ValueError("partition evidence does not satisfy its alignment")
+        _enforce((
+            (bool(self.axis) and min(self.total_units, self.alignment) > 0, "partition evidence requires an axis and positive sizes"),
+            (0 < self.qpu_units < self.total_units, "partition evidence must retain work on both CPU and QPU"),
+            (self.qpu_units % self.alignment == 0, "partition evidence does not satisfy its alignment"),
+        ))
+
+
+@dataclass(frozen=True, slots=True)
+class QualityEvidence:
+    """Error of a quantized format against its fp32 source-domain reference."""
+
+    reference: str
+    normalized_rmse: float
+    cosine_similarity: float
+    max_abs_error: float = 0.0
+    mean_abs_error: float = 0.0
+    p99_abs_error: float = 0.0
+    nan_count: int = 0
+    inf_count: int = 0
+    top1_agreement: float | None = None
+
+    def __post_init__(self: Self) -> None:
+        errors = (self.normalized_rmse, self.max_abs_error, self.mean_abs_error, self.p99_abs_error)
+        _enforce((
+            (bool(self.reference) and min(errors) >= 0, "quality evidence requires a reference and non-negative NRMSE"),
+            (-1.0 <= self.cosine_similarity <= 1.0, "quality cosine similarity must be within [-1, 1]"),
+            (min(self.nan_count, self.inf_count) >= 0, "quality NaN and Inf counts cannot be negative"),
+            (self.top1_agreement is None or 0.0 <= self.top1_agreement <= 1.0, "quality top-1 agreement must be within [0, 1]"),
+        ))
+
+    @property
+    def passes_default_gate(self: Self) -> bool:
+        """NRMSE at most 0.10, cosine similarity at least 0.99, and no NaN or Inf."""
+        return self.normalized_rmse <= 0.10 and self.cosine_similarity >= 0.99 and self.nan_count == 0 and self.inf_count == 0
+
+
+def _status_rules(record: CandidateRecord) -> tuple[tuple[bool, str], ...]:
+    """The evidence each lifecycle state needs."""
+    correct, timed = record.correctness, record.performance
+    status = record.status
+    if status is CandidateStatus.SUPPORTED_WIN:
+        return (
+            (correct is not None and timed is not None and timed.measured_win,
+             "supported candidates require correctness and a measured or fused win"),
+            (correct is None or correct.finite, "supported candidates cannot produce NaN or Inf outputs"),
+        )
+    if status is CandidateStatus.SAME_CONTRACT_WIN:
+        return (
+            (correct is not None and timed is not None and timed.same_contract_win,
+             "same-contract winners require correctness and a measured W8A8 CPU win"),
+            (correct is None or correct.finite, "same-contract winners cannot produce NaN or Inf outputs"),
+        )
+    if status is CandidateStatus.EXPERIMENTAL_CORRECT_SLOWER:
+        return ((correct is not None, "correct experimental candidates require correctness evidence"),)
+    if status is CandidateStatus.QUARANTINED_INCORRECT:
+        return ((bool(record.reason), "quarantined candidates require a failure reason"),)
+    return ()
 
 
 @dataclass(frozen=True, slots=True)
@@ -141,29 +202,59 @@ class CandidateRecord:
     placement: str = "cuda"
     kernels: tuple[str, ...] = ()
     partition: PartitionEvidence | None = None
+    quality: QualityEvidence | None = None
 
     def __post_init__(self: Self) -> None:
         identity = (self.name, self.operation, self.dtype, self.layout, self.shape_class, self.source_hash)
-        if any(not value for value in identity):
-            raise ValueError("candidate identity fields must be non-empty")
-        if self.placement not in PLACEMENTS:
-            raise ValueError("candidate placement must be cpu, qpu, hybrid or cuda")
-        if self.placement == "hybrid" and self.partition is None:
-            raise ValueError("hybrid candidate records require partition evidence")
-        if self.placement != "hybrid" and self.partition is not None:
-            raise ValueError("only hybrid candidate records may include partition evidence")
-        if self.status is CandidateStatus.SUPPORTED_WIN:
-            if self.correctness is None or self.performance is None or not self.performance.measured_win:
-                raise ValueError("supported candidates require correctness and a measured or fused win")
-            if self.correctness.nan_count or self.correctness.inf_count:
-                raise ValueError("supported candidates cannot produce NaN or Inf outputs")
-        if self.status is CandidateStatus.SAME_CONTRACT_WIN:
-            if self.correctness is None or self.performance is None or not self.performance.same_contract_win:
-                raise ValueError("same-contract winners require correctness and a measured CPU win")
-        if self.status is CandidateStatus.EXPERIMENTAL_CORRECT_SLOWER and self.correctness is None:
-            raise ValueError("correct experimental candidates require correctness evidence")
-        if self.status is CandidateStatus.QUARANTINED_INCORRECT and not self.reason:
-            raise ValueError("quarantined candidates require a failure reason")
+        hybrid = self.placement == "hybrid"
+        _enforce((
+            (all(identity), "candidate identity fields must be non-empty"),
+            (self.placement in PLACEMENTS, "candidate placement must be cpu, qpu, hybrid or cuda"),
+            (not hybrid or self.partition is not None, "hybrid candidate records require partition evidence"),
+            (hybrid or self.partition is None, "only hybrid candidate records may include partition evidence"),
+        ))
+        _enforce(_status_rules(self))
+
+    def shape_key(self: Self) -> tuple[str, str, str, str]:
+        """The exact operation class placement looks records up by."""
+        return (self.operation, self.dtype, self.layout, self.shape_class)
+
+
+# ---- archive (de)serialization, driven by the dataclass fields ---------------------------------
+
+
+def _to_json(value: Any) -> Any:
+    if isinstance(value, Enum):
+        return value.value
+    if dataclasses.is_dataclass(value):
+        return {item.name: _to_json(getattr(value, item.name)) for item in dataclasses.fields(value)}
+    if isinstance(value, tuple):
+        return [_to_json(item) for item in value]
+    return value
+
+
+_NESTED: dict[str, type] = {}  # field name -> evidence class, filled below
+
+
+def _from_json(cls: type, payload: dict[str, Any]) -> Any:
+    """Build ``cls`` from a JSON object: nested evidence objects and enums are rebuilt, lists
+    become tuples; unknown keys are an error (TypeError from the constructor)."""
+    hints = typing.get_type_hints(cls)
+    arguments: dict[str, Any] = {}
+    for key, raw in payload.items():
+        if key in _NESTED and raw is not None:
+            arguments[key] = _from_json(_NESTED[key], raw)
+        elif hints.get(key) is CandidateStatus:
+            arguments[key] = CandidateStatus(raw)
+        elif isinstance(raw, list):
+            arguments[key] = tuple(raw)
+        else:
+            arguments[key] = raw
+    return cls(**arguments)
+
+
+_NESTED.update(correctness=CorrectnessEvidence, performance=PerformanceEvidence, partition=PartitionEvidence,
+               quality=QualityEvidence)
 
 
 class CandidateRegistry:
@@ -180,14 +271,11 @@ class CandidateRegistry:
 
     @property
     def supported(self: Self) -> tuple[CandidateRecord, ...]:
-        return tuple(r for r in self._records.values() if r.status is CandidateStatus.SUPPORTED_WIN)
+        return tuple(record for record in self._records.values() if record.status is CandidateStatus.SUPPORTED_WIN)
 
     def supported_for(self: Self, *, operation: str, dtype: str, layout: str, shape_class: str) -> tuple[CandidateRecord, ...]:
-        return tuple(
-            r
-            for r in self.supported
-            if r.operation == operation and r.dtype == dtype and r.layout == layout and r.shape_class == shape_class
-        )
+        wanted = (operation, dtype, layout, shape_class)
+        return tuple(record for record in self.supported if record.shape_key() == wanted)
 
     def register(self: Self, record: CandidateRecord) -> None:
         if record.name in self._records:
@@ -199,12 +287,7 @@ class CandidateRegistry:
         return cls(tuple(record for registry in registries for record in registry.records))
 
     def to_dict(self: Self) -> dict[str, object]:
-        payload: list[dict[str, object]] = []
-        for record in self.records:
-            item = asdict(record)
-            item["status"] = record.status.value
-            payload.append(item)
-        return {"schema_version": 3, "records": payload}
+        return {"schema_version": 3, "records": [_to_json(record) for record in self.records]}
 
     def save(self: Self, path: str | PathLike[str]) -> None:
         with open(path, "w", encoding="utf-8") as output:
@@ -216,28 +299,17 @@ class CandidateRegistry:
             payload: Any = json.load(source)
         if not isinstance(payload, dict) or payload.get("schema_version") not in (1, 2, 3):
             raise ValueError("unsupported candidate registry schema")
-        raw_records = payload.get("records")
-        if not isinstance(raw_records, list):
+        entries = payload.get("records")
+        if not isinstance(entries, list):
             raise ValueError("candidate registry records must be a list")
-        records: list[CandidateRecord] = []
-        for raw in raw_records:
-            if not isinstance(raw, dict):
+        records = []
+        for entry in entries:
+            if not isinstance(entry, dict):
                 raise ValueError("candidate registry records must be objects")
-            item = dict(raw)
-            item.pop("quality", None)
-            item["status"] = CandidateStatus(item["status"])
-            if item.get("correctness") is not None:
-                item["correctness"] = CorrectnessEvidence(**item["correctness"])
-            if item.get("performance") is not None:
-                perf = dict(item["performance"])
-                for key, value in perf.items():
-                    if isinstance(value, list):
-                        perf[key] = tuple(value)
-                item["performance"] = PerformanceEvidence(**perf)
-            if item.get("partition") is not None:
-                item["partition"] = PartitionEvidence(**item["partition"])
-            item["kernels"] = tuple(item.get("kernels", ()))
-            records.append(CandidateRecord(**item))
+            try:
+                records.append(_from_json(CandidateRecord, entry))
+            except (KeyError, TypeError, ValueError) as error:
+                raise ValueError("candidate registry contains an invalid record") from error
         return cls(tuple(records))
 
 
@@ -248,4 +320,5 @@ __all__ = [
     "CorrectnessEvidence",
     "PartitionEvidence",
     "PerformanceEvidence",
+    "QualityEvidence",
 ]

@@ -1,11 +1,20 @@
-"""Device lifetime and allocation entry points (src/qpu_xla/device.py:17-121).
+"""Device lifetime and allocation (the drop-in surface of src/qpu_xla/device.py).
 
 ``Device.open()`` opens the CUDA backend on one GPU (the reference opened the
 VideoCore DRM driver); ``Device.fake()`` keeps the CPU-only test backend.
+
+Allocations come from a per-device :class:`_Pool`. A buffer that is closed
+returns its allocation to the pool, where the next request reuses the smallest
+released allocation that is large enough and suitably aligned (so a closed
+buffer's address comes back for a request it fits); requests nothing fits go to
+the backend. Closing the device retires every block still lent out, which makes
+all buffers and tensor views over them raise ``BufferClosedError``.
 """
 
 from __future__ import annotations
 
+import bisect
+import itertools
 from typing import TYPE_CHECKING, Any, Self
 from weakref import WeakSet
 
@@ -14,10 +23,48 @@ import numpy.typing as npt
 
 from qpu_xla.backend import Backend, BackendAllocation, CudaBackend, FakeBackend, _validate_allocation_request
 from qpu_xla.errors import DeviceClosedError
-from qpu_xla.memory import Buffer, Tensor, _AllocationState
+from qpu_xla.memory import Buffer, Tensor, _Block
 
 if TYPE_CHECKING:
     from qpu_xla.queue import Queue
+
+
+class _Pool:
+    """Released allocations ordered by size, plus every block currently lent out."""
+
+    def __init__(self: Self, backend: Backend) -> None:
+        self._backend = backend
+        self._free: list[tuple[int, int, BackendAllocation]] = []  # (nbytes, arrival, allocation), sorted
+        self._arrivals = itertools.count()
+        self._lent: list[_Block] = []
+
+    def lend(self: Self, nbytes: int, alignment: int) -> _Block:
+        allocation = self._reuse(nbytes, alignment) or self._backend.allocate(nbytes, alignment=alignment)
+        block = _Block(allocation, self._give_back)
+        self._lent.append(block)
+        return block
+
+    def _reuse(self: Self, nbytes: int, alignment: int) -> BackendAllocation | None:
+        first = bisect.bisect_left(self._free, (nbytes, -1))
+        for position in range(first, len(self._free)):
+            allocation = self._free[position][2]
+            if allocation.address % alignment == 0:
+                del self._free[position]
+                return allocation
+        return None
+
+    def _give_back(self: Self, allocation: BackendAllocation) -> None:
+        if self._backend is None:  # the device is closed: nothing is reused any more
+            return
+        bisect.insort(self._free, (allocation.nbytes, next(self._arrivals), allocation))
+        self._lent = [block for block in self._lent if block.live]
+
+    def retire_all(self: Self) -> None:
+        for block in self._lent:
+            block.retire(recycle=False)
+        self._lent.clear()
+        self._free.clear()
+        self._backend = None  # type: ignore[assignment]
 
 
 class Device:
@@ -25,14 +72,13 @@ class Device:
 
     def __init__(self: Self, backend: Backend) -> None:
         self._backend = backend
+        self._pool = _Pool(backend)
         self._closed = False
-        self._allocations: list[_AllocationState] = []
-        self._free_allocations: list[BackendAllocation] = []
         self._queues: WeakSet[Queue] = WeakSet()
 
     @classmethod
     def fake(cls: type[Device]) -> Device:
-        """CPU-only device for runtime tests; it cannot launch kernels."""
+        """CPU-only device for runtime tests; it cannot launch CUDA kernels."""
         return cls(FakeBackend())
 
     @classmethod
@@ -64,40 +110,20 @@ class Device:
             raise DeviceClosedError("device is closed")
 
     def allocate(self: Self, nbytes: int, *, alignment: int = 1) -> Buffer:
-        """Allocate (or reuse a released) byte buffer owned by this device."""
+        """A byte buffer owned by this device (a released allocation is reused when one fits)."""
         self._require_open()
         _validate_allocation_request(nbytes, alignment)
-        allocation = self._take_free_allocation(nbytes, alignment)
-        state = _AllocationState(allocation)
-        self._allocations.append(state)
-        return Buffer(self, state, nbytes=nbytes)
-
-    def _take_free_allocation(self: Self, nbytes: int, alignment: int) -> BackendAllocation:
-        compatible = [
-            (index, allocation)
-            for index, allocation in enumerate(self._free_allocations)
-            if allocation.nbytes >= nbytes and allocation.address % alignment == 0
-        ]
-        if not compatible:
-            return self._backend.allocate(nbytes, alignment=alignment)
-        index, allocation = min(compatible, key=lambda candidate: candidate[1].nbytes)
-        del self._free_allocations[index]
-        return allocation
-
-    def _release_allocation(self: Self, state: _AllocationState) -> None:
-        if self._closed:
-            return
-        self._free_allocations.append(state.allocation)
+        return Buffer(self, self._pool.lend(nbytes, alignment), nbytes=nbytes)
 
     def tensor(self: Self, shape: tuple[int, ...], dtype: npt.DTypeLike, *, alignment: int = 1) -> Tensor:
-        """Allocate a contiguous typed tensor."""
-        if not shape or any(dimension <= 0 for dimension in shape):
+        """A contiguous typed tensor in a buffer of its own."""
+        if not shape or min(shape) <= 0:
             raise ValueError("tensor shape must contain only positive dimensions")
         nbytes = int(np.prod(shape, dtype=np.int64)) * np.dtype(dtype).itemsize
         return self.allocate(nbytes, alignment=alignment).tensor(shape, dtype)
 
     def queue(self: Self) -> Queue:
-        """Create an in-order submission queue (a CUDA stream on the cuda backend)."""
+        """A new in-order submission queue (a CUDA stream on the cuda backend)."""
         from qpu_xla.queue import Queue
 
         self._require_open()
@@ -106,14 +132,12 @@ class Device:
         return queue
 
     def close(self: Self) -> None:
-        """Wait for submitted work, close queues and invalidate allocations."""
+        """Finish and close every queue, invalidate every allocation, release the backend."""
         if self._closed:
             return
-        for queue in tuple(self._queues):
+        for queue in list(self._queues):
             queue.close()
-        for state in self._allocations:
-            state.closed = True
-        self._free_allocations.clear()
+        self._pool.retire_all()
         self._backend.close()
         self._closed = True
 

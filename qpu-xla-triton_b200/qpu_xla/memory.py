@@ -1,18 +1,24 @@
-"""Buffers and typed tensor views over backend allocations.
+"""Buffers and typed tensor views over device allocations.
 
-Same surface and checks as src/qpu_xla/memory.py:18-265 (``AccessMode``,
-``BufferAccess`` hazard ranges, ``Buffer.slice/access/tensor``, strided
-``Tensor`` views with unit-step ``slice``). Differences forced by CUDA memory:
+The drop-in surface of src/qpu_xla/memory.py (``AccessMode``, ``BufferAccess``,
+``Buffer.slice/access/tensor``, strided ``Tensor`` views with unit-step
+``slice``), built around this build's allocation blocks:
 
-* ``Tensor.numpy()`` is zero-copy on the fake backend, as in the reference, but
-  a device-to-host *copy* on the CUDA backend (device memory is not host-mapped);
-* ``Tensor.torch()`` is the zero-copy view of CUDA memory, and
+* every allocation handed out by a device is a :class:`_Block`; buffers and
+  tensors are byte windows ``[start, start + length)`` of one block, and a block
+  retired by ``Buffer.close()`` or ``Device.close()`` invalidates every window
+  over it at once;
+* a declared access is the byte interval it covers in its block, so hazard
+  checks are interval tests between accesses of the same block;
+* CUDA memory is not host-mapped: ``Tensor.numpy()`` is a zero-copy view on the
+  fake backend but a device-to-host copy on the CUDA backend,
+  ``Tensor.torch()`` is the zero-copy view of CUDA memory, and
   ``Tensor.write(values)`` copies host data in.
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass
+import math
 from enum import Enum
 from typing import TYPE_CHECKING, Any, Self
 
@@ -27,7 +33,7 @@ if TYPE_CHECKING:
 
 
 class AccessMode(Enum):
-    """Declared access mode for a buffer range used by a queue submission."""
+    """How a queue submission uses a declared byte range."""
 
     READ = "read"
     WRITE = "write"
@@ -35,65 +41,88 @@ class AccessMode(Enum):
 
     @property
     def writes(self: Self) -> bool:
-        return self is not AccessMode.READ
+        return self in _WRITING_MODES
 
 
-@dataclass(slots=True)
-class _AllocationState:
-    """Close state shared by a buffer and every view derived from it."""
+_WRITING_MODES = frozenset({AccessMode.WRITE, AccessMode.READ_WRITE})
 
-    allocation: BackendAllocation
-    closed: bool = False
 
-    def require_open(self: Self) -> None:
-        if self.closed:
+class _Block:
+    """One allocation lent out by a device's pool. ``live`` turns false exactly once, when the
+    block is retired; every buffer, tensor and access over it checks that flag."""
+
+    __slots__ = ("allocation", "live", "_on_retire")
+
+    def __init__(self: Self, allocation: BackendAllocation, on_retire: Any = None) -> None:
+        self.allocation = allocation
+        self.live = True
+        self._on_retire = on_retire
+
+    @property
+    def size(self: Self) -> int:
+        return self.allocation.nbytes
+
+    def check(self: Self) -> None:
+        if not self.live:
             raise BufferClosedError("buffer is closed")
 
+    def retire(self: Self, *, recycle: bool) -> None:
+        """Invalidate the block; with ``recycle`` its allocation goes back to the owner's pool."""
+        if not self.live:
+            return
+        self.live = False
+        if recycle and self._on_retire is not None:
+            self._on_retire(self.allocation)
 
-@dataclass(frozen=True, slots=True)
+
+def _window(size: int, start: int, length: int | None, message: str) -> tuple[int, int]:
+    """``[start, start + length)`` inside ``[0, size)`` with a non-empty length (default: to the end)."""
+    length = size - start if length is None else length
+    if start < 0 or length <= 0 or start + length > size:
+        raise AllocationError(message)
+    return start, length
+
+
 class BufferAccess:
-    """A declared byte range and access mode, used for hazard tracking."""
+    """A declared byte range of a buffer and its access mode, for queue hazard tracking."""
 
-    buffer: Buffer
-    mode: AccessMode
-    offset: int = 0
-    nbytes: int | None = None
+    __slots__ = ("buffer", "mode", "offset", "nbytes", "_lo", "_hi")
 
-    def __post_init__(self: Self) -> None:
-        self.buffer._state.require_open()
-        nbytes = self.buffer.nbytes - self.offset if self.nbytes is None else self.nbytes
-        if self.offset < 0 or nbytes <= 0 or self.offset + nbytes > self.buffer.nbytes:
-            raise AllocationError("buffer access range is outside the buffer")
-        object.__setattr__(self, "nbytes", nbytes)
+    def __init__(self: Self, buffer: Buffer, mode: AccessMode, offset: int = 0, nbytes: int | None = None) -> None:
+        buffer._block.check()
+        offset, nbytes = _window(buffer._length, offset, nbytes, "buffer access range is outside the buffer")
+        self.buffer = buffer
+        self.mode = mode
+        self.offset = offset
+        self.nbytes = nbytes
+        self._lo = buffer._start + offset
+        self._hi = self._lo + nbytes
 
     @property
     def absolute_offset(self: Self) -> int:
-        return self.buffer.offset + self.offset
+        """Offset of the range from the start of its allocation."""
+        return self._lo
 
     def conflicts_with(self: Self, other: BufferAccess) -> bool:
-        """Two accesses conflict when they overlap in one allocation and one of them writes."""
-        if self.buffer._state is not other.buffer._state or not (self.mode.writes or other.mode.writes):
+        """True when both ranges lie in one allocation, overlap, and at least one of them writes."""
+        if self.buffer._block is not other.buffer._block:
             return False
-        assert self.nbytes is not None and other.nbytes is not None
-        return (
-            self.absolute_offset < other.absolute_offset + other.nbytes
-            and other.absolute_offset < self.absolute_offset + self.nbytes
-        )
+        if not (self.mode.writes or other.mode.writes):
+            return False
+        return max(self._lo, other._lo) < min(self._hi, other._hi)
+
+    def __repr__(self: Self) -> str:
+        return f"BufferAccess({self.mode.value}, [{self._lo}, {self._hi}))"
 
 
 class Buffer:
-    """A runtime-owned byte range of one allocation."""
+    """A byte window of one device allocation."""
 
-    def __init__(self: Self, device: Device, state: _AllocationState, *, offset: int = 0, nbytes: int | None = None) -> None:
-        state.require_open()
-        total = state.allocation.nbytes
-        nbytes = total - offset if nbytes is None else nbytes
-        if offset < 0 or nbytes <= 0 or offset + nbytes > total:
-            raise AllocationError("buffer range is outside its allocation")
+    def __init__(self: Self, device: Device, block: _Block, *, offset: int = 0, nbytes: int | None = None) -> None:
+        block.check()
+        self._start, self._length = _window(block.size, offset, nbytes, "buffer range is outside its allocation")
         self._device = device
-        self._state = state
-        self._offset = offset
-        self._nbytes = nbytes
+        self._block = block
 
     @property
     def device(self: Self) -> Device:
@@ -101,33 +130,32 @@ class Buffer:
 
     @property
     def offset(self: Self) -> int:
-        return self._offset
+        """Byte offset of this window in its allocation."""
+        return self._start
 
     @property
     def nbytes(self: Self) -> int:
-        self._state.require_open()
-        return self._nbytes
+        self._block.check()
+        return self._length
 
     @property
     def address(self: Self) -> int:
-        """Device address of this range (a 64-bit CUDA pointer on the cuda backend)."""
-        self._state.require_open()
-        return self._state.allocation.address + self._offset
+        """Device address of the window (a 64-bit CUDA pointer on the cuda backend)."""
+        self._block.check()
+        return self._block.allocation.address + self._start
 
     @property
     def closed(self: Self) -> bool:
-        return self._state.closed
+        return not self._block.live
 
     def close(self: Self) -> None:
-        if self._state.closed:
-            return
-        self._state.closed = True
-        self._device._release_allocation(self._state)
+        """Invalidate this allocation and every view of it, and give it back to the device."""
+        self._block.retire(recycle=True)
 
     def slice(self: Self, offset: int, nbytes: int | None = None) -> Buffer:
-        self._state.require_open()
-        nbytes = self._nbytes - offset if nbytes is None else nbytes
-        return Buffer(self._device, self._state, offset=self._offset + offset, nbytes=nbytes)
+        self._block.check()
+        offset, nbytes = _window(self._length, offset, nbytes, "buffer range is outside its allocation")
+        return Buffer(self._device, self._block, offset=self._start + offset, nbytes=nbytes)
 
     def access(self: Self, mode: AccessMode, *, offset: int = 0, nbytes: int | None = None) -> BufferAccess:
         return BufferAccess(self, mode, offset, nbytes)
@@ -138,30 +166,31 @@ class Buffer:
         return Tensor(self, shape, dtype, offset=offset, strides=strides)
 
 
-_TORCH_DTYPES: dict[str, str] = {
-    "float32": "float32",
-    "float16": "float16",
-    "int8": "int8",
-    "uint8": "uint8",
-    "int16": "int16",
-    "int32": "int32",
-    "int64": "int64",
-    "uint16": "uint16",
-    "uint32": "uint32",
-}
+_TORCH_DTYPES = frozenset({"float32", "float16", "int8", "uint8", "int16", "int32", "int64", "uint16", "uint32"})
 
 
 def torch_dtype(dtype: np.dtype[Any]) -> Any:
     import torch
 
-    name = _TORCH_DTYPES.get(np.dtype(dtype).name)
-    if name is None:
+    name = np.dtype(dtype).name
+    if name not in _TORCH_DTYPES:
         raise AllocationError(f"dtype {dtype} has no torch equivalent")
     return getattr(torch, name)
 
 
+def _row_major(shape: tuple[int, ...], itemsize: int) -> tuple[int, ...]:
+    """Byte strides of a C-ordered array of ``shape``."""
+    tail = np.cumprod((1,) + shape[:0:-1])[::-1] if len(shape) > 1 else np.ones(1, dtype=np.int64)
+    return tuple(int(value) * itemsize for value in tail)
+
+
+def _extent(shape: tuple[int, ...], itemsize: int, strides: tuple[int, ...]) -> int:
+    """Bytes from the first element to the end of the last one, for positive strides."""
+    return itemsize + math.sumprod((d - 1 for d in shape), strides)
+
+
 class Tensor:
-    """A typed, strided view of one buffer (byte offsets and byte strides)."""
+    """A typed, strided view of a buffer (byte offset, byte strides)."""
 
     def __init__(
         self: Self,
@@ -172,36 +201,24 @@ class Tensor:
         offset: int = 0,
         strides: tuple[int, ...] | None = None,
     ) -> None:
-        buffer._state.require_open()
-        shape = tuple(int(d) for d in shape)
-        if not shape or any(dimension <= 0 for dimension in shape):
+        buffer._block.check()
+        dims = tuple(int(d) for d in shape)
+        if not dims or min(dims) <= 0:
             raise AllocationError("tensor shape must contain only positive dimensions")
-        dtype = np.dtype(dtype)
-        if offset < 0 or offset % dtype.itemsize:
+        element = np.dtype(dtype)
+        size = element.itemsize
+        if offset < 0 or offset % size:
             raise AllocationError("tensor offset must be non-negative and aligned to the dtype")
-        strides = self._contiguous_strides(shape, dtype.itemsize) if strides is None else tuple(int(s) for s in strides)
-        if len(strides) != len(shape) or any(stride <= 0 or stride % dtype.itemsize for stride in strides):
+        steps = _row_major(dims, size) if strides is None else tuple(int(s) for s in strides)
+        if len(steps) != len(dims) or any(s <= 0 or s % size for s in steps):
             raise AllocationError("tensor strides must be positive, dtype-aligned byte strides for every dimension")
-        if offset + self._required_nbytes(shape, dtype.itemsize, strides) > buffer.nbytes:
+        if offset + _extent(dims, size, steps) > buffer.nbytes:
             raise AllocationError("tensor view exceeds its buffer")
         self._buffer = buffer
-        self._shape = shape
-        self._dtype = dtype
+        self._shape = dims
+        self._dtype = element
         self._offset = offset
-        self._strides = strides
-
-    @staticmethod
-    def _contiguous_strides(shape: tuple[int, ...], itemsize: int) -> tuple[int, ...]:
-        strides: list[int] = []
-        stride = itemsize
-        for dimension in reversed(shape):
-            strides.append(stride)
-            stride *= dimension
-        return tuple(reversed(strides))
-
-    @staticmethod
-    def _required_nbytes(shape: tuple[int, ...], itemsize: int, strides: tuple[int, ...]) -> int:
-        return itemsize + sum((dimension - 1) * stride for dimension, stride in zip(shape, strides, strict=True))
+        self._strides = steps
 
     @property
     def buffer(self: Self) -> Buffer:
@@ -221,40 +238,40 @@ class Tensor:
 
     @property
     def nbytes(self: Self) -> int:
-        self._buffer._state.require_open()
-        return self._required_nbytes(self._shape, self._dtype.itemsize, self._strides)
+        """Bytes the view spans in its buffer."""
+        self._buffer._block.check()
+        return _extent(self._shape, self._dtype.itemsize, self._strides)
 
     @property
     def address(self: Self) -> int:
-        self._buffer._state.require_open()
+        """Device address of element [0, ..., 0]."""
         return self._buffer.address + self._offset
 
     @property
     def is_contiguous(self: Self) -> bool:
-        return self._strides == self._contiguous_strides(self._shape, self._dtype.itemsize)
+        return self._strides == _row_major(self._shape, self._dtype.itemsize)
 
     @property
     def row_stride_elements(self: Self) -> int:
         """Leading-dimension stride in elements (rank-2 views)."""
         return self._strides[0] // self._dtype.itemsize
 
-    def _host_mapped(self: Self) -> bool:
-        return bool(self._buffer._state.allocation.host_mapped)
+    def _allocation(self: Self) -> BackendAllocation:
+        block = self._buffer._block
+        block.check()
+        return block.allocation
 
     def numpy(self: Self) -> npt.NDArray[Any]:
         """Zero-copy view on the fake backend; a device-to-host copy on the CUDA backend.
 
-        On CUDA the copy is taken after synchronizing the device, so call it
-        once the producing event has been waited on.
+        On CUDA the copy is taken after synchronizing the device, so call it once the
+        producing event has been waited on.
         """
-        self._buffer._state.require_open()
-        if self._host_mapped():
+        allocation = self._allocation()
+        if allocation.host_mapped:
             return np.ndarray(
-                self._shape,
-                dtype=self._dtype,
-                buffer=self._buffer._state.allocation.storage,
-                offset=self._buffer.offset + self._offset,
-                strides=self._strides,
+                self._shape, dtype=self._dtype, buffer=allocation.storage,
+                offset=self._buffer.offset + self._offset, strides=self._strides,
             )
         import torch
 
@@ -263,47 +280,39 @@ class Tensor:
         return view.cpu().numpy()
 
     def torch(self: Self) -> Any:
-        """Zero-copy torch view (CUDA backend) or a torch view of the NumPy memory (fake backend)."""
+        """Zero-copy torch view (CUDA backend), or a torch view of the NumPy memory (fake backend)."""
         import torch
 
-        self._buffer._state.require_open()
-        if self._host_mapped():
+        allocation = self._allocation()
+        if allocation.host_mapped:
             return torch.from_numpy(self.numpy())
-        storage = self._buffer._state.allocation.storage
-        start = self._buffer.offset + self._offset
-        span = self.nbytes
-        flat = storage[start : start + span].view(torch_dtype(self._dtype))
-        itemsize = self._dtype.itemsize
-        return flat.as_strided(self._shape, tuple(stride // itemsize for stride in self._strides))
+        first = self._buffer.offset + self._offset
+        flat = allocation.storage[first : first + self.nbytes].view(torch_dtype(self._dtype))
+        size = self._dtype.itemsize
+        return flat.as_strided(self._shape, tuple(step // size for step in self._strides))
 
     def write(self: Self, values: npt.ArrayLike) -> None:
         """Copy host ``values`` (broadcast to this shape) into the tensor."""
-        array = np.broadcast_to(np.asarray(values, dtype=self._dtype), self._shape)
-        if self._host_mapped():
-            self.numpy()[...] = array
+        host = np.broadcast_to(np.asarray(values, dtype=self._dtype), self._shape)
+        if self._allocation().host_mapped:
+            self.numpy()[...] = host
             return
         import torch
 
-        host = np.ascontiguousarray(array)
-        if not host.flags.writeable:
-            host = host.copy()
-        self.torch().copy_(torch.from_numpy(host))
+        self.torch().copy_(torch.from_numpy(np.array(host, order="C", copy=True)))
 
     def slice(self: Self, slices: tuple[slice, ...]) -> Tensor:
-        """Unit-step slice without copying (memory.py:247-261)."""
+        """A unit-step sub-view sharing this tensor's memory."""
         if len(slices) != len(self._shape):
             raise AllocationError("one slice is required for each tensor dimension")
-        shape: list[int] = []
-        offset = self._offset
-        for dimension, stride, item in zip(self._shape, self._strides, slices, strict=True):
-            start, stop, step = item.indices(dimension)
-            if step != 1:
-                raise AllocationError("only unit-step tensor slices are currently supported")
-            if stop <= start:
-                raise AllocationError("tensor slices must not be empty")
-            shape.append(stop - start)
-            offset += start * stride
-        return Tensor(self._buffer, tuple(shape), self._dtype, offset=offset, strides=self._strides)
+        bounds = [item.indices(extent) for item, extent in zip(slices, self._shape, strict=True)]
+        if any(step != 1 for _, _, step in bounds):
+            raise AllocationError("only unit-step tensor slices are currently supported")
+        if any(stop <= start for start, stop, _ in bounds):
+            raise AllocationError("tensor slices must not be empty")
+        first = self._offset + sum(start * step for (start, _, _), step in zip(bounds, self._strides, strict=True))
+        shape = tuple(stop - start for start, stop, _ in bounds)
+        return Tensor(self._buffer, shape, self._dtype, offset=first, strides=self._strides)
 
     def access(self: Self, mode: AccessMode) -> BufferAccess:
         return self._buffer.access(mode, offset=self._offset, nbytes=self.nbytes)

@@ -1,31 +1,40 @@
 """In-order queues and events over CUDA streams and CUDA events.
 
-Same surface as src/qpu_xla/queue.py:23-393: ``Queue.submit(kernel, args, *,
-grid, wait_for, buffers) -> Event``, ``Queue.host_task``, ``Event.wait(timeout)``
-/ ``status`` / ``done`` / ``cancel``, the hazard ledger, Chrome-trace export and
-``consume_completed_event_counts``. One worker thread per queue preserves
-submission order, exactly as the reference's ``Queue._run`` (:376-393).
+The drop-in surface of src/qpu_xla/queue.py: ``Queue.submit(kernel, args, *, grid,
+wait_for, buffers) -> Event``, ``Queue.host_task``, ``Event.wait(timeout)`` /
+``status`` / ``done`` / ``cancel``, buffer hazards, Chrome-trace export and
+``consume_completed_event_counts``.
 
-On the CUDA backend each queue owns one CUDA stream. A kernel submission
-launches on that stream and its event completes when a CUDA event recorded
-after the launch completes (no host round trip in between); a dependency on an
-event of another queue becomes ``cudaStreamWaitEvent`` on the GPU. Host tasks
-first wait (on the host) for the queue's earlier GPU work, so host code always
-observes the results of the kernels submitted before it.
+How it runs here. Each queue has one worker thread that takes submissions in order,
+so a queue never reorders its own work. On the CUDA backend the queue also owns a
+CUDA stream:
+
+* a kernel submission is *launched* by the worker -- the executor enqueues its CUDA
+  work on the stream between two CUDA events -- and its :class:`Event` completes when
+  the second CUDA event has; the host never waits in between;
+* a dependency on another queue's kernel becomes ``cudaStreamWaitEvent`` on the GPU
+  (the worker only waits until that kernel has been launched);
+* a host task first waits for the queue's earlier GPU work and for its dependencies,
+  so host code sees the results of everything submitted before it.
+
+Every declared buffer access of a submission that has not finished is kept in a
+ledger indexed by allocation; ``Queue.hazards`` reports the events whose ranges
+overlap a given access with at least one side writing.
 """
 
 from __future__ import annotations
 
+import itertools
 import json
+import threading
 import time
-from collections.abc import Callable, Iterable
-from dataclasses import dataclass
+from collections import Counter, defaultdict
+from collections.abc import Callable, Iterable, Iterator
 from enum import Enum
 from os import PathLike
-from queue import Queue as ThreadQueue
-from threading import Condition, Lock, Thread
+from queue import SimpleQueue
 from time import monotonic_ns
-from typing import TYPE_CHECKING, Any, Self
+from typing import TYPE_CHECKING, Any, NamedTuple, Self
 
 from qpu_xla.errors import DependencyError, DeviceClosedError, EventCancelledError, EventTimeoutError
 from qpu_xla.kernel import Kernel, LaunchConfig
@@ -43,8 +52,16 @@ class EventStatus(Enum):
     CANCELLED = "cancelled"
 
 
+_FINAL = frozenset({EventStatus.SUCCEEDED, EventStatus.FAILED, EventStatus.CANCELLED})
+
+
 class Event:
-    """Completion state, failure propagation and timestamps of one submission."""
+    """One submission: its state, its failure, host timestamps and (kernels) GPU completion.
+
+    Two latches carry the state to waiters: ``_launched`` opens once the submission's
+    CUDA work is on the stream (or the event has ended without any), ``_ended`` once the
+    event is final.
+    """
 
     def __init__(self: Self, queue: Queue, *, sequence: int, name: str, category: str, dependencies: tuple[Event, ...]) -> None:
         self._queue = queue
@@ -52,17 +69,18 @@ class Event:
         self._name = name
         self._category = category
         self._dependencies = dependencies
-        self._condition = Condition()
-        self._status = EventStatus.PENDING
-        self._exception: BaseException | None = None
+        self._guard = threading.Lock()
+        self._launched = threading.Event()
+        self._ended = threading.Event()
+        self._state = EventStatus.PENDING
+        self._error: BaseException | None = None
         self._submitted_ns = monotonic_ns()
         self._started_ns: int | None = None
         self._finished_ns: int | None = None
-        # CUDA completion (kernel submissions): events recorded around the launch.
-        self._launched = False
-        self._cuda_start: Any = None
-        self._cuda_end: Any = None
+        self._gpu_marks: tuple[Any, Any] | None = None  # CUDA events before / after the launch
         self._device_ms: float | None = None
+
+    # -- read side ------------------------------------------------------------------
 
     @property
     def queue(self: Self) -> Queue:
@@ -79,13 +97,13 @@ class Event:
     @property
     def cuda_event(self: Self) -> Any:
         """The CUDA event recorded after this submission's launch (None for host tasks)."""
-        return self._cuda_end
+        marks = self._gpu_marks
+        return None if marks is None else marks[1]
 
     @property
     def status(self: Self) -> EventStatus:
-        self._poll_device()
-        with self._condition:
-            return self._status
+        self._refresh()
+        return self._state
 
     @property
     def submitted_ns(self: Self) -> int:
@@ -93,137 +111,143 @@ class Event:
 
     @property
     def started_ns(self: Self) -> int | None:
-        with self._condition:
-            return self._started_ns
+        return self._started_ns
 
     @property
     def finished_ns(self: Self) -> int | None:
-        self._poll_device()
-        with self._condition:
-            return self._finished_ns
+        self._refresh()
+        return self._finished_ns
 
     @property
     def device_milliseconds(self: Self) -> float | None:
         """GPU time between the CUDA events around the launch, once complete."""
-        self._poll_device()
+        self._refresh()
         return self._device_ms
 
     @property
     def exception(self: Self) -> BaseException | None:
-        with self._condition:
-            return self._exception
+        return self._error
 
     @property
     def done(self: Self) -> bool:
-        self._poll_device()
-        with self._condition:
-            return self._status in {EventStatus.SUCCEEDED, EventStatus.FAILED, EventStatus.CANCELLED}
+        self._refresh()
+        return self._state in _FINAL
 
     def cancel(self: Self) -> bool:
-        """Cancel a queued submission the worker has not started."""
-        with self._condition:
-            if self._status is not EventStatus.PENDING:
-                return False
-            self._status = EventStatus.CANCELLED
-            self._finished_ns = monotonic_ns()
-            self._condition.notify_all()
-            return True
+        """Cancel the submission if its queue's worker has not started it."""
+        return self._end(EventStatus.CANCELLED, None, only_from=EventStatus.PENDING)
 
     def wait(self: Self, timeout: float | None = None) -> None:
-        """Wait for completion; re-raise a cancellation or failure (queue.py:113-126)."""
+        """Block until the event ends; raise its failure, or EventCancelledError if cancelled."""
         if timeout is not None and timeout < 0:
             raise ValueError("timeout must be non-negative or None")
         deadline = None if timeout is None else time.monotonic() + timeout
-        with self._condition:
-            ready = self._condition.wait_for(
-                lambda: self._launched or self._status in {EventStatus.SUCCEEDED, EventStatus.FAILED, EventStatus.CANCELLED},
-                timeout=timeout,
-            )
-            if not ready:
+
+        def remaining() -> float | None:
+            return None if deadline is None else max(0.0, deadline - time.monotonic())
+
+        if not self._launched.wait(remaining()):
+            raise EventTimeoutError("event did not complete before the timeout")
+        pause = 2e-6
+        while not self._refresh():
+            if deadline is not None and time.monotonic() >= deadline:
                 raise EventTimeoutError("event did not complete before the timeout")
-        if self._cuda_end is not None:
-            delay = 2e-6
-            while not self._poll_device():
-                if deadline is not None and time.monotonic() > deadline:
-                    raise EventTimeoutError("event did not complete before the timeout")
-                time.sleep(delay)
-                delay = min(delay * 2, 1e-3)
-        with self._condition:
-            if self._status is EventStatus.CANCELLED:
-                raise EventCancelledError("event was cancelled")
-            if self._status is EventStatus.FAILED:
-                assert self._exception is not None
-                raise self._exception
+            time.sleep(pause)
+            pause = min(2 * pause, 1e-3)
+        self._raise_outcome(EventCancelledError("event was cancelled"))
 
-    # -- worker-side transitions ------------------------------------------------
+    def _raise_outcome(self: Self, cancelled: BaseException) -> None:
+        if self._state is EventStatus.CANCELLED:
+            raise cancelled
+        if self._state is EventStatus.FAILED:
+            assert self._error is not None
+            raise self._error
 
-    def _start(self: Self) -> bool:
-        with self._condition:
-            if self._status is EventStatus.CANCELLED:
+    # -- worker side ------------------------------------------------------------------
+
+    def _end(self: Self, state: EventStatus, error: BaseException | None, *, only_from: EventStatus | None = None) -> bool:
+        """Move to a final state (from ``only_from`` only, when given); False if that is not allowed."""
+        with self._guard:
+            if self._state in _FINAL or (only_from is not None and self._state is not only_from):
                 return False
-            if self._status is not EventStatus.PENDING:
+            self._state = state
+            self._error = error
+            self._finished_ns = monotonic_ns()
+        self._launched.set()
+        self._ended.set()
+        return True
+
+    def _begin(self: Self) -> bool:
+        """PENDING -> RUNNING when the worker picks the submission up; False if it was cancelled."""
+        with self._guard:
+            if self._state is EventStatus.CANCELLED:
+                return False
+            if self._state is not EventStatus.PENDING:
                 raise RuntimeError("event cannot be started more than once")
-            self._status = EventStatus.RUNNING
+            self._state = EventStatus.RUNNING
             self._started_ns = monotonic_ns()
             return True
 
-    def _mark_launched(self: Self, start: Any, end: Any) -> None:
-        with self._condition:
-            self._cuda_start = start
-            self._cuda_end = end
-            self._launched = True
-            self._condition.notify_all()
+    def _on_stream(self: Self, before: Any, after: Any) -> None:
+        """The submission's CUDA work is enqueued between ``before`` and ``after``."""
+        self._gpu_marks = (before, after)
+        self._launched.set()
 
-    def _poll_device(self: Self) -> bool:
-        """Complete a launched kernel event once its CUDA event has completed."""
-        with self._condition:
-            if self._status is not EventStatus.RUNNING or not self._launched or self._cuda_end is None:
-                return self._status is not EventStatus.RUNNING and self._status is not EventStatus.PENDING
-        if not self._cuda_end.query():
+    def _refresh(self: Self) -> bool:
+        """Final yet? A launched kernel event becomes final when its closing CUDA event has completed."""
+        if self._ended.is_set():
+            return True
+        marks = self._gpu_marks
+        if marks is None or self._state is not EventStatus.RUNNING or not marks[1].query():
             return False
-        exception: BaseException | None = None
         try:
-            self._queue._check_device_errors()
-        except BaseException as exc:  # a kernel-side bounded wait expired
-            exception = exc
-        with self._condition:
-            if self._status is EventStatus.RUNNING:
-                if self._cuda_start is not None:
-                    self._device_ms = float(self._cuda_start.elapsed_time(self._cuda_end))
-                self._exception = exception
-                self._status = EventStatus.FAILED if exception is not None else EventStatus.SUCCEEDED
-                self._finished_ns = monotonic_ns()
-                self._condition.notify_all()
+            self._queue._raise_device_errors()
+        except BaseException as error:  # a kernel's bounded wait expired on the device
+            self._end(EventStatus.FAILED, error)
+            return True
+        self._device_ms = float(marks[0].elapsed_time(marks[1]))
+        self._end(EventStatus.SUCCEEDED, None)
         return True
 
-    def _finish(self: Self, exception: BaseException | None = None) -> None:
-        with self._condition:
-            if self._status is EventStatus.CANCELLED:
-                return
-            self._exception = exception
-            self._status = EventStatus.FAILED if exception is not None else EventStatus.SUCCEEDED
-            self._finished_ns = monotonic_ns()
-            self._condition.notify_all()
-
-    def _wait_launched(self: Self) -> None:
-        """Host wait until a kernel event is launched (or the event ends); re-raise its failure."""
-        with self._condition:
-            self._condition.wait_for(
-                lambda: self._launched or self._status in {EventStatus.SUCCEEDED, EventStatus.FAILED, EventStatus.CANCELLED}
-            )
-            if self._status is EventStatus.CANCELLED:
-                raise EventCancelledError("dependency was cancelled")
-            if self._status is EventStatus.FAILED:
-                assert self._exception is not None
-                raise self._exception
+    def _await_launch(self: Self) -> None:
+        """Block until this dependency's GPU work is enqueued (or it ended); raise if it did not succeed."""
+        self._launched.wait()
+        if self._ended.is_set():
+            self._raise_outcome(EventCancelledError("dependency was cancelled"))
 
 
-@dataclass(slots=True)
-class _Submission:
+class _Job(NamedTuple):
     event: Event
-    action: Callable[[], None]
+    run: Callable[[], None]
     dependencies: tuple[Event, ...]
-    kernel: bool
+    on_gpu: bool
+
+
+class _Ledger:
+    """Declared accesses of unfinished submissions, grouped by the allocation they touch."""
+
+    def __init__(self: Self) -> None:
+        self._by_block: dict[int, list[tuple[BufferAccess, Event]]] = defaultdict(list)
+
+    def add(self: Self, accesses: Iterable[BufferAccess], event: Event) -> None:
+        for access in accesses:
+            self._by_block[id(access.buffer._block)].append((access, event))
+
+    def conflicts(self: Self, accesses: Iterable[BufferAccess]) -> list[Event]:
+        found: list[Event] = []
+        for access in accesses:
+            for held, event in self._by_block.get(id(access.buffer._block), ()):
+                if event not in found and not event.done and access.conflicts_with(held):
+                    found.append(event)
+        return found
+
+    def prune(self: Self) -> None:
+        for key in list(self._by_block):
+            live = [(access, event) for access, event in self._by_block[key] if not event.done]
+            if live:
+                self._by_block[key] = live
+            else:
+                del self._by_block[key]
 
 
 class Queue:
@@ -236,14 +260,13 @@ class Queue:
             import torch
 
             self._stream = torch.cuda.Stream(device=device.backend.torch_device)  # type: ignore[attr-defined]
-        self._submissions: ThreadQueue[_Submission | None] = ThreadQueue()
-        self._lock = Lock()
+        self._jobs: SimpleQueue[_Job | None] = SimpleQueue()
+        self._lock = threading.Lock()
         self._closed = False
-        self._tail: Event | None = None
-        self._events: list[Event] = []
-        self._next_sequence = 0
-        self._live_accesses: list[tuple[BufferAccess, Event]] = []
-        self._worker = Thread(target=self._run, name="qpu-xla-submit", daemon=True)
+        self._history: list[Event] = []
+        self._numbers = itertools.count()
+        self._ledger = _Ledger()
+        self._worker = threading.Thread(target=self._serve, name="qpu-xla-submit", daemon=True)
         self._worker.start()
 
     @property
@@ -257,8 +280,9 @@ class Queue:
 
     @property
     def closed(self: Self) -> bool:
-        with self._lock:
-            return self._closed
+        return self._closed
+
+    # -- submission ----------------------------------------------------------------------
 
     def submit(
         self: Self,
@@ -269,15 +293,12 @@ class Queue:
         wait_for: Iterable[Event] = (),
         buffers: Iterable[BufferAccess] = (),
     ) -> Event:
-        """Queue a kernel launch and return its completion event (queue.py:186-210)."""
+        """Queue a kernel launch; the returned event completes with its GPU work."""
         launch = LaunchConfig(tuple(grid))  # type: ignore[arg-type]
-        backend = self._device.backend
-        stream = self._stream
-
-        def action() -> None:
-            kernel.execute(backend, args, launch, stream)
-
-        return self._enqueue(action, wait_for=wait_for, buffers=buffers, name=kernel.name, category="cuda", kernel=True)
+        backend, stream = self._device.backend, self._stream
+        return self._admit(
+            lambda: kernel.execute(backend, args, launch, stream), wait_for, buffers, kernel.name, "cuda", on_gpu=True
+        )
 
     def host_task(
         self: Self,
@@ -287,114 +308,93 @@ class Queue:
         buffers: Iterable[BufferAccess] = (),
         name: str | None = None,
     ) -> Event:
-        """Queue host work with the same dependency and hazard declarations (queue.py:212-222)."""
-        task_name = name if name is not None else str(getattr(fn, "__qualname__", "host_task"))
-        return self._enqueue(fn, wait_for=wait_for, buffers=buffers, name=task_name, category="host", kernel=False)
+        """Queue host work, ordered after this queue's earlier work and ``wait_for``."""
+        label = name if name is not None else str(getattr(fn, "__qualname__", "host_task"))
+        return self._admit(fn, wait_for, buffers, label, "host", on_gpu=False)
 
-    def _enqueue(
-        self: Self,
-        action: Callable[[], None],
-        *,
-        wait_for: Iterable[Event],
-        buffers: Iterable[BufferAccess],
-        name: str,
-        category: str,
-        kernel: bool,
+    def _admit(
+        self: Self, run: Callable[[], None], wait_for: Iterable[Event], buffers: Iterable[BufferAccess],
+        name: str, category: str, *, on_gpu: bool,
     ) -> Event:
-        declared = tuple(buffers)
-        for access in declared:
-            if access.buffer.device is not self._device:
-                raise DependencyError("a buffer access belongs to a different device")
+        accesses = tuple(buffers)
+        if any(access.buffer.device is not self._device for access in accesses):
+            raise DependencyError("a buffer access belongs to a different device")
         with self._lock:
             if self._closed:
                 raise DeviceClosedError("queue is closed")
-            dependencies = self._normalize_dependencies(wait_for)
-            # The in-order worker already serialises conflicting accesses on this
-            # queue; the ledger keeps them for cross-queue diagnostics.
-            self._live_accesses = [(access, event) for access, event in self._live_accesses if not event.done]
-            event = Event(self, sequence=self._next_sequence, name=name, category=category, dependencies=dependencies)
-            self._next_sequence += 1
-            self._tail = event
-            self._events.append(event)
-            self._live_accesses.extend((access, event) for access in declared)
-            self._submissions.put(_Submission(event, action, dependencies, kernel))
-            return event
+            dependencies = self._own_dependencies(wait_for)
+            event = Event(self, sequence=next(self._numbers), name=name, category=category, dependencies=dependencies)
+            self._history.append(event)
+            self._ledger.prune()
+            self._ledger.add(accesses, event)
+            self._jobs.put(_Job(event, run, dependencies, on_gpu))
+        return event
 
-    def hazards(self: Self, accesses: Iterable[BufferAccess]) -> list[Event]:
-        """Live events whose declared accesses conflict with ``accesses``."""
-        wanted = tuple(accesses)
-        with self._lock:
-            return [event for access, event in self._live_accesses if not event.done and any(access.conflicts_with(other) for other in wanted)]
-
-    def _normalize_dependencies(self: Self, wait_for: Iterable[Event]) -> tuple[Event, ...]:
-        dependencies: list[Event] = []
+    def _own_dependencies(self: Self, wait_for: Iterable[Event]) -> tuple[Event, ...]:
+        """The distinct events of ``wait_for``, each checked to come from this device."""
+        unique: dict[int, Event] = {}
         for event in wait_for:
             if not isinstance(event, Event):
                 raise DependencyError("wait_for must contain Event instances")
             if event.queue.device is not self._device:
                 raise DependencyError("event dependency belongs to a different device")
-            if event not in dependencies:
-                dependencies.append(event)
-        return tuple(dependencies)
+            unique.setdefault(id(event), event)
+        return tuple(unique.values())
 
-    def _check_device_errors(self: Self) -> None:
-        """Raise if a kernel on this device reported an expired bounded wait."""
+    def hazards(self: Self, accesses: Iterable[BufferAccess]) -> list[Event]:
+        """Unfinished events of this queue whose declared ranges conflict with ``accesses``."""
+        with self._lock:
+            return self._ledger.conflicts(tuple(accesses))
+
+    # -- worker ----------------------------------------------------------------------
+
+    def _serve(self: Self) -> None:
+        while (job := self._jobs.get()) is not None:
+            try:
+                if job.event._begin():
+                    (self._launch if job.on_gpu and self._stream is not None else self._run_on_host)(job)
+            except BaseException as error:
+                job.event._end(EventStatus.FAILED, error)
+
+    def _run_on_host(self: Self, job: _Job) -> None:
+        for dependency in job.dependencies:
+            dependency.wait()
+        if self._stream is not None:
+            self._stream.synchronize()  # this queue's earlier kernels are complete
+        job.run()
+        job.event._end(EventStatus.SUCCEEDED, None)
+
+    def _launch(self: Self, job: _Job) -> None:
+        import torch
+
+        stream = self._stream
+        for dependency in job.dependencies:
+            dependency._await_launch()
+            marker = dependency.cuda_event
+            if marker is None:
+                dependency.wait()  # a host task: it must have finished
+            else:
+                stream.wait_event(marker)
+        before, after = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            before.record(stream)
+            job.run()
+            after.record(stream)
+        job.event._on_stream(before, after)
+
+    def _raise_device_errors(self: Self) -> None:
+        """Raise if a kernel on this device recorded an expired bounded wait (CUDA backend)."""
         backend = self._device.backend
         if getattr(backend, "kind", "") == "cuda" and self._stream is not None:
             backend.launch(self._stream, lambda native: native.synchronize())  # type: ignore[attr-defined]
 
-    def _run(self: Self) -> None:
-        while True:
-            submission = self._submissions.get()
-            if submission is None:
-                self._submissions.task_done()
-                return
-            event = submission.event
-            try:
-                if event._start():
-                    self._run_one(submission)
-            except BaseException as exc:
-                event._finish(exc)
-            finally:
-                self._submissions.task_done()
-
-    def _run_one(self: Self, submission: _Submission) -> None:
-        event = submission.event
-        stream = self._stream
-        if stream is None:
-            for dependency in submission.dependencies:
-                dependency.wait()
-            submission.action()
-            event._finish()
-            return
-        import torch
-
-        if submission.kernel:
-            for dependency in submission.dependencies:
-                dependency._wait_launched()
-                if dependency.cuda_event is not None:
-                    stream.wait_event(dependency.cuda_event)
-                else:
-                    dependency.wait()
-            start = torch.cuda.Event(enable_timing=True)
-            end = torch.cuda.Event(enable_timing=True)
-            with torch.cuda.stream(stream):
-                start.record(stream)
-                submission.action()
-                end.record(stream)
-            event._mark_launched(start, end)
-        else:
-            for dependency in submission.dependencies:
-                dependency.wait()
-            stream.synchronize()  # in-order: earlier kernels of this queue are complete
-            submission.action()
-            event._finish()
+    # -- completion and profiling ----------------------------------------------------------
 
     def finish(self: Self, timeout: float | None = None) -> None:
-        """Wait for every submitted event (failures are left on their events)."""
+        """Wait for every submitted event; failures stay on their events, a timeout or cancel raises."""
         with self._lock:
-            events = tuple(self._events)
-        for event in events:
+            pending = list(self._history)
+        for event in pending:
             try:
                 event.wait(timeout)
             except (EventCancelledError, EventTimeoutError):
@@ -403,72 +403,35 @@ class Queue:
                 pass
 
     def chrome_trace(self: Self) -> dict[str, list[dict[str, object]]]:
-        """Chrome Trace Event payload (queue.py:275-347): queue delay, execution and dependency flows.
+        """Chrome Trace Event payload: queue delay and execution slices, and a flow per dependency.
 
-        Kernel slices use the GPU time measured between the CUDA events around the launch.
+        Kernel slices last the GPU time measured between the CUDA events around the launch.
         """
         with self._lock:
-            events = tuple(self._events)
-        trace: list[dict[str, object]] = []
-        for event in events:
-            started_ns = event.started_ns
-            finished_ns = event.finished_ns
-            if started_ns is None:
-                continue
-            submitted_us = event.submitted_ns / 1_000
-            started_us = started_ns / 1_000
-            if started_ns > event.submitted_ns:
-                trace.append(
-                    {"name": f"queue delay: {event.name}", "cat": "queue", "ph": "X", "pid": "qpu-xla", "tid": "submission",
-                     "ts": submitted_us, "dur": started_us - submitted_us, "args": {"event": event._sequence}}
-                )
-            if finished_ns is not None:
-                device_ms = event.device_milliseconds
-                duration_us = device_ms * 1_000 if device_ms is not None else max(0, finished_ns - started_ns) / 1_000
-                trace.append(
-                    {"name": event.name, "cat": event._category, "ph": "X", "pid": "qpu-xla", "tid": event._category,
-                     "ts": started_us, "dur": duration_us, "args": {"event": event._sequence, "status": event.status.value}}
-                )
-            for dependency in event._dependencies:
-                dependency_finished_ns = dependency.finished_ns
-                if dependency_finished_ns is None:
-                    continue
-                flow_id = f"{dependency._sequence}->{event._sequence}"
-                trace.extend(
-                    (
-                        {"name": "dependency", "cat": "sync", "ph": "s", "pid": "qpu-xla", "tid": dependency._category,
-                         "ts": dependency_finished_ns / 1_000, "id": flow_id},
-                        {"name": "dependency", "cat": "sync", "ph": "f", "pid": "qpu-xla", "tid": event._category,
-                         "ts": started_us, "id": flow_id},
-                    )
-                )
-        return {"traceEvents": trace}
-
-    def consume_completed_event_counts(self: Self) -> dict[str, int]:
-        """Count and drop completed events by category, bounding profiling memory (queue.py:349-369)."""
-        with self._lock:
-            completed: list[Event] = []
-            retained: list[Event] = []
-            for event in self._events:
-                (completed if event.done else retained).append(event)
-            self._events = retained
-            self._live_accesses = [(access, event) for access, event in self._live_accesses if not event.done]
-        counts: dict[str, int] = {}
-        for event in completed:
-            counts[event._category] = counts.get(event._category, 0) + 1
-        return counts
+            events = list(self._history)
+        return {"traceEvents": list(_trace_records(events))}
 
     def write_chrome_trace(self: Self, path: str | PathLike[str]) -> None:
         with open(path, "w", encoding="utf-8") as trace_file:
             json.dump(self.chrome_trace(), trace_file, separators=(",", ":"))
 
+    def consume_completed_event_counts(self: Self) -> dict[str, int]:
+        """Count finished events per category and forget them (bounds profiling memory)."""
+        with self._lock:
+            finished = [event for event in self._history if event.done]
+            self._history = [event for event in self._history if not event.done]
+            self._ledger.prune()
+        return dict(Counter(event.category for event in finished))
+
+    # -- lifetime ----------------------------------------------------------------------
+
     def close(self: Self) -> None:
-        """Stop accepting work and wait until submitted work has finished."""
+        """Stop accepting work and wait until everything submitted has finished."""
         with self._lock:
             if self._closed:
                 return
             self._closed = True
-        self._submissions.put(None)
+        self._jobs.put(None)
         self._worker.join()
         if self._stream is not None:
             self._stream.synchronize()
@@ -478,6 +441,37 @@ class Queue:
 
     def __exit__(self: Self, exc_type: object, exc_value: object, traceback: object) -> None:
         self.close()
+
+
+_PROCESS = "qpu-xla"
+
+
+def _trace_records(events: list[Event]) -> Iterator[dict[str, object]]:
+    """Complete ('X') slices for the wait in the queue and for the work of every started event,
+    and a start/finish ('s'/'f') flow pair from each finished dependency to its dependent."""
+    for event in events:
+        started = event.started_ns
+        if started is None:
+            continue
+        if started > event.submitted_ns:
+            yield {"name": f"queue delay: {event.name}", "cat": "queue", "ph": "X", "pid": _PROCESS, "tid": "submission",
+                   "ts": event.submitted_ns / 1e3, "dur": (started - event.submitted_ns) / 1e3,
+                   "args": {"event": event._sequence}}
+        finished = event.finished_ns
+        if finished is not None:
+            gpu_ms = event.device_milliseconds
+            span_us = gpu_ms * 1e3 if gpu_ms is not None else max(0, finished - started) / 1e3
+            yield {"name": event.name, "cat": event.category, "ph": "X", "pid": _PROCESS, "tid": event.category,
+                   "ts": started / 1e3, "dur": span_us, "args": {"event": event._sequence, "status": event.status.value}}
+        for dependency in event._dependencies:
+            ready = dependency.finished_ns
+            if ready is None:
+                continue
+            link = f"{dependency._sequence}->{event._sequence}"
+            yield {"name": "dependency", "cat": "sync", "ph": "s", "pid": _PROCESS, "tid": dependency.category,
+                   "ts": ready / 1e3, "id": link}
+            yield {"name": "dependency", "cat": "sync", "ph": "f", "pid": _PROCESS, "tid": event.category,
+                   "ts": started / 1e3, "id": link}
 
 
 __all__ = ["Event", "EventStatus", "Queue"]

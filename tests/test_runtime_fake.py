@@ -245,3 +245,48 @@ def test_capability_registry_prefers_calibrated_cuda(tmp_path: Path) -> None:
         PartitionSpec("outputs", 0, 16)
     with pytest.raises(ValueError):
         ExecutionCandidate("h", Placement.HYBRID, lambda s: True, lambda s: 1.0)
+
+
+def test_reference_style_three_argument_executors_run() -> None:
+    """``Kernel(name, executor)`` with the reference's ``executor(backend, args, grid)`` form
+    (src/qpu_xla/kernel.py:24-38) runs as submitted; this build's stream-aware form takes a fourth
+    argument."""
+    with Device.fake() as device, device.queue() as queue:
+        calls: list[object] = []
+        queue.submit(Kernel("three", lambda backend, args, grid: calls.append((args, grid))), ("a",), grid=(2, 3, 4)).wait()
+        queue.submit(Kernel("four", lambda backend, args, grid, stream: calls.append((args, grid, stream))), ("b",)).wait()
+        assert calls == [(("a",), (2, 3, 4)), (("b",), (1, 1, 1), None)]
+
+
+def test_cost_model_reads_the_reference_file_format(tmp_path: Path) -> None:
+    """A cost model saved in the reference's JSON form (fingerprint + records) loads and drives
+    placement; malformed records are refused."""
+    path = tmp_path / "reference-cost.json"
+    path.write_text(json.dumps({
+        "fingerprint": {"device": "b200"},
+        "records": [{"name": "linear", "dtype": "w8a8", "shape": [1, 64, 64], "layout": "", "candidate": "cuda", "seconds": [3e-6, 1e-6, 2e-6]}],
+    }))
+    model = CostModel.load(path)
+    assert model.fingerprint == {"device": "b200"}
+    assert model.estimate(OperationSpec("linear", "w8a8", (1, 64, 64)), "cuda") == pytest.approx(2e-6)
+    model.save(path)
+    assert CostModel.load(path).to_dict() == model.to_dict()
+    path.write_text(json.dumps({"fingerprint": {}, "records": [{"name": "x", "dtype": "d", "shape": [0], "layout": "", "candidate": "c", "seconds": [1.0]}]}))
+    with pytest.raises(ValueError, match="invalid fields"):
+        CostModel.load(path)
+
+
+def test_candidate_records_keep_quality_evidence(tmp_path: Path) -> None:
+    from qpu_xla.candidates import QualityEvidence
+
+    quality = QualityEvidence("numpy-fp32", 0.02, 0.999, max_abs_error=0.1, top1_agreement=1.0)
+    record = CandidateRecord(
+        "q", "linear", "w8a8-i32-fp32", "row-major-k", "1x64x64", "hash", CandidateStatus.SUPPORTED_WIN, correctness(),
+        PerformanceEvidence("numpy", (0.1,), (0.001,)), quality=quality,
+    )
+    path = tmp_path / "candidates.json"
+    CandidateRegistry((record,)).save(path)
+    assert CandidateRegistry.load(path).records == (record,)
+    assert quality.passes_default_gate
+    with pytest.raises(ValueError, match="cosine"):
+        QualityEvidence("numpy-fp32", 0.02, 1.5)

@@ -64,7 +64,7 @@ TOKENS = 4096
 SEED = 4
 L2_FLUSH_BYTES = 256 << 20
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
-OBJECTS = ("square", "tinyllama_w8a8", "tinyllama_q4_0", "llama7b_ffn")
+OBJECTS = ("square", "tinyllama_w8a8", "tinyllama_q4_0", "llama7b_ffn", "q4_0_mx")
 Q4_0_COPIES = 16  # distinct TinyLlama weight copies streamed per bracket (16 x 6.5 MB)
 
 
@@ -905,11 +905,51 @@ def object_llama7b_ffn(bench: Bench, int8_peak: float, hbm_peak: float, int8_not
     }
 
 
+def object_q4_0_mx(bench: Bench, int8_peak: float, hbm_peak: float, int8_note: str, hbm_note: str) -> dict[str, Any]:
+    """The reference's MX path (Q4_0 x Q8_0 with rows > 4, exact per-block scaling) at prefill size:
+    M = 4096 rows on the 70B gate (8192 -> 28672) and down (28672 -> 8192) shapes, Q8_0 activations
+    on the device; one projection per bracket (split activation + tcgen05 MX kernel)."""
+    import torch
+
+    from qpu_xla.ggml import PreparedQ4_0Linear
+
+    rows = TOKENS
+    generator = torch.Generator(device=bench.cuda)
+    generator.manual_seed(SEED + 5)
+    result: dict[str, Any] = {"metric": "Q4_0 x Q8_0 MX path TOPS (2MNK / time), M = 4096", "unit": "TOPS", "shapes": {}}
+    for name, k, n in (("gate_proj", 8192, 28672), ("down_proj", 28672, 8192)):
+        weight = torch.randn((n, k), generator=generator, device=bench.cuda, dtype=torch.float32) * 0.02
+        plan = PreparedQ4_0Linear(bench.device, bench.q4_0_blocks(weight), rows=rows)
+        del weight
+        source = torch.randn((rows, k), generator=generator, device=bench.cuda, dtype=torch.float32)
+        act = bench.q8_0(source)
+        del source
+        out = torch.empty((rows, n), dtype=torch.float32, device=bench.cuda)
+        try:
+            ms = statistics.median(bench.brackets(lambda plan=plan, act=act, out=out: plan.forward(act, out=out), 5))
+        finally:
+            plan.close()
+        ops = 2.0 * rows * n * k
+        result["shapes"][f"{name} {k}->{n}"] = {
+            "tops": round(ops / (ms * 1e-3) / 1e12, 1),
+            "ms_per_call": round(ms, 4),
+            "roofline": roofline(kernel="activation split + q4_0_mx_sm100_kernel (tcgen05 kind::i8, one MMA per block)",
+                                 seconds=ms * 1e-3, ops=ops, nbytes=0.0, int8_peak=int8_peak, hbm_peak=hbm_peak,
+                                 peak_note=int8_note, traffic=None),
+        }
+        del act, out
+    result["value"] = next(iter(result["shapes"].values()))["tops"]
+    result["note"] = ("the exact per-block fp32 scaling (((float)dot * d_a) * d_w, then a sequential fp32 add per "
+                      "output and block) runs on the CUDA cores and bounds this path, not the tensor pipe")
+    return result
+
+
 OBJECT_RUNNERS: dict[str, Callable[..., dict[str, Any]]] = {
     "square": object_square,
     "tinyllama_w8a8": object_tinyllama_w8a8,
     "tinyllama_q4_0": object_tinyllama_q4_0,
     "llama7b_ffn": object_llama7b_ffn,
+    "q4_0_mx": object_q4_0_mx,
 }
 
 
@@ -1099,11 +1139,32 @@ def cpu_llama7b(target_seconds: float) -> dict[str, object]:
     return cpu_reference_sample(target_seconds=target_seconds, workload_shapes=ffn, tokens=TOKENS, label="7B FFN")
 
 
+def cpu_q4_0_mx(target_seconds: float) -> dict[str, object]:
+    """The reference program's MX arithmetic (NumPy port, per-block exact scaling) on a row sample of
+    the 70B gate shape: 16 rows x 1024 output columns at full K, scaled to TOPS."""
+    import numpy as np
+
+    from oracle import qpu_oracle as oracle
+
+    rng = np.random.default_rng(SEED)
+    k, columns, rows = 8192, 1024, 16
+    blocks = oracle.quantize_q4_0((rng.standard_normal((columns, k), dtype=np.float32) * np.float32(0.02)).astype(np.float32))
+    act = oracle.quantize_q8_0(rng.standard_normal((rows, k), dtype=np.float32))
+    reps, t0 = 0, time.perf_counter()
+    while reps < 1 or time.perf_counter() - t0 < target_seconds / 4:
+        oracle.q4_0_q8_0_linear_mx(act, blocks)
+        reps += 1
+    seconds = (time.perf_counter() - t0) / reps
+    return {"value": 2.0 * rows * columns * k / seconds / 1e12, "unit": "TOPS", "cores": 1, "kind": "port",
+            "sample": f"{rows} rows x {columns} output columns of the 70B gate shape at full K (NumPy port of the MX program)"}
+
+
 OBJECT_CPU: dict[str, Callable[[float], dict[str, object]]] = {
     "square": cpu_square,
     "tinyllama_w8a8": cpu_tinyllama_w8a8,
     "tinyllama_q4_0": cpu_q4_0,
     "llama7b_ffn": cpu_llama7b,
+    "q4_0_mx": cpu_q4_0_mx,
 }
 
 

@@ -36,7 +36,7 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found; the CUDA toolkit is required to build libqpucuda.so")
 
 
-Q4_0_KERNEL_SOURCES = ("q4_0_gemv.cu",)
+Q4_0_KERNEL_SOURCES = ("q4_0_gemv.cu", "q4_0_mx_sm100.cu")
 
 
 def q4_0_source_hash() -> str:

@@ -34,6 +34,8 @@ struct qpucuda_q4_0_linear {
     uint16_t *d_scales = nullptr;     // [resident][scale_stride], zero padded
     uint8_t *d_activation = nullptr;  // [rows][blocks][34] staging
     uint8_t *d_mx = nullptr;          // rows > 4: split activation for the tensor-core path
+    int8_t *d_mx_values = nullptr;    // rows > 4: codes as int8 (code - 8), [resident][blocks_pad * 32]
+    float *d_mx_scales_t = nullptr;   // rows > 4: fp32 scales, [blocks_pad][resident]
     float *d_output = nullptr;        // [rows][resident] staging
     uint8_t *h_activation = nullptr;  // pinned
     float *h_output = nullptr;        // pinned
@@ -66,6 +68,8 @@ void free_linear(qpucuda_q4_0_linear *linear) {
     cudaFree(linear->d_scales);
     cudaFree(linear->d_activation);
     cudaFree(linear->d_mx);
+    cudaFree(linear->d_mx_values);
+    cudaFree(linear->d_mx_scales_t);
     cudaFree(linear->d_output);
     cudaFreeHost(linear->h_activation);
     cudaFreeHost(linear->h_output);
@@ -85,6 +89,8 @@ Q40Weights weights_of(const qpucuda_q4_0_linear *linear) {
     weights.columns = linear->resident_column_count;
     weights.blocks = linear->blocks;
     weights.scale_stride = q4_0_scale_stride(linear->blocks);
+    weights.mx_values = linear->d_mx_values;
+    weights.mx_scales_t = linear->d_mx_scales_t;
     return weights;
 }
 
@@ -96,8 +102,8 @@ cudaError_t launch_linear(const qpucuda_q4_0_linear *linear, const uint8_t *q8_0
     qpucuda_context *context = linear->context;
     if (rows > kMaxRows) {
         return launch_q4_0_mx(weights_of(linear), q8_0, f32, f32_stride, rows, interleave, linear->d_mx, destination,
-                              destination_stride, local_start, output_column_start, column_count, context->sm_count,
-                              context->stream);
+                              destination_stride, local_start, output_column_start, column_count, context->d_error,
+                              context->sm_count, context->stream);
     }
     if (f32 != nullptr) {
         return launch_q4_0_f32_gemv(weights_of(linear), f32, f32_stride, rows, destination, destination_stride,
@@ -174,12 +180,22 @@ qpucuda_status qpucuda_q4_0_linear_prepare(qpucuda_context *context, const qpucu
     const size_t activation_bytes = static_cast<size_t>(desc->rows) * blocks * kActivationBlockBytes;
     const size_t output_bytes = static_cast<size_t>(desc->rows) * desc->resident_column_count * sizeof(float);
     const size_t mx_bytes = desc->rows > kMaxRows ? q4_0_mx_scratch_bytes(desc->rows, linear->blocks) : 0;
+    // Rows > 4 on sm_100: the tcgen05 MX kernel reads the codes expanded to int8 and the scales as
+    // fp32, block-major (made once here from the repacked weights).
+    const bool mx_tcgen05 = mx_bytes != 0 && context->cc_major == 10 && context->cc_minor == 0;
+    const size_t mx_blocks_pad = q4_0_mx_blocks_pad(linear->blocks);
+    const size_t mx_value_bytes = mx_tcgen05 ? static_cast<size_t>(desc->resident_column_count) * mx_blocks_pad * 32 : 0;
+    const size_t mx_scale_bytes = mx_tcgen05 ? static_cast<size_t>(desc->resident_column_count) * mx_blocks_pad * 4 : 0;
     uint8_t *d_native = nullptr;
     cudaError_t error = cudaMalloc(reinterpret_cast<void **>(&linear->d_nibbles), resident_blocks * 16);
     if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_scales), scale_bytes);
     if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_activation), activation_bytes);
     if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_output), output_bytes);
     if (error == cudaSuccess && mx_bytes != 0) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_mx), mx_bytes);
+    if (error == cudaSuccess && mx_tcgen05)
+        error = cudaMalloc(reinterpret_cast<void **>(&linear->d_mx_values), mx_value_bytes);
+    if (error == cudaSuccess && mx_tcgen05)
+        error = cudaMalloc(reinterpret_cast<void **>(&linear->d_mx_scales_t), mx_scale_bytes);
     if (error == cudaSuccess) error = cudaMallocHost(reinterpret_cast<void **>(&linear->h_activation), activation_bytes);
     if (error == cudaSuccess) error = cudaMallocHost(reinterpret_cast<void **>(&linear->h_output), output_bytes);
     if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&d_native), native_bytes);
@@ -197,6 +213,10 @@ qpucuda_status qpucuda_q4_0_linear_prepare(qpucuda_context *context, const qpucu
         error = launch_q4_0_repack(d_native, desc->resident_column_count, linear->blocks,
                                    q4_0_scale_stride(linear->blocks), linear->d_nibbles, linear->d_scales,
                                    context->stream);
+    if (error == cudaSuccess && mx_tcgen05)
+        error = launch_q4_0_mx_expand(linear->d_nibbles, linear->d_scales, desc->resident_column_count, linear->blocks,
+                                      static_cast<uint32_t>(mx_blocks_pad), q4_0_scale_stride(linear->blocks),
+                                      linear->d_mx_values, linear->d_mx_scales_t, context->stream);
     qpucuda_status status = error == cudaSuccess ? wait_stream(context)
                                                  : cuda_fail(context, error, "stage Q4_0 weights", QPUCUDA_IO_FAILED);
     cudaFree(d_native);
@@ -204,7 +224,8 @@ qpucuda_status qpucuda_q4_0_linear_prepare(qpucuda_context *context, const qpucu
         free_linear(linear);
         return status;
     }
-    linear->resident_bytes = resident_blocks * kWeightBlockBytes + activation_bytes + output_bytes + mx_bytes;
+    linear->resident_bytes =
+        resident_blocks * kWeightBlockBytes + activation_bytes + output_bytes + mx_bytes + mx_value_bytes + mx_scale_bytes;
     *result = linear;
     return QPUCUDA_OK;
 }

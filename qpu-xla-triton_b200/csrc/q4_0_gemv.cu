@@ -631,6 +631,7 @@ struct MxSplitParams {
     uint32_t rows_pad, blocks_pad;
     int8_t *q;
     int2 *meta;
+    float *da_t;  // tcgen05 path: the block scales again, block-major [blocks_pad][rows_pad]; or null
 };
 
 // One thread per (row, block) of the padded split activation; padding is written as zeros.
@@ -661,6 +662,7 @@ __global__ void __launch_bounds__(256) q4_0_mx_split_kernel(const MxSplitParams 
         q[0] = make_uint4(words[0], words[1], words[2], words[3]);
         q[1] = make_uint4(words[4], words[5], words[6], words[7]);
         p.meta[static_cast<size_t>(row) * p.blocks_pad + block] = make_int2(__float_as_int(d), 8 * sum);
+        if (p.da_t != nullptr) p.da_t[static_cast<size_t>(block) * p.rows_pad + row] = d;
     }
 }
 
@@ -848,17 +850,25 @@ cudaError_t launch_mx_tiles(const MxParams &p, uint32_t rows_pad, uint32_t count
 }
 
 cudaError_t launch_mx(const Q40Weights &weights, const ActivationView &view, uint8_t *scratch, float *destination,
-                      size_t destination_stride, uint32_t col0, uint32_t out_col0, uint32_t count, int sm_count,
-                      cudaStream_t stream) {
+                      size_t destination_stride, uint32_t col0, uint32_t out_col0, uint32_t count,
+                      unsigned int *error_word, int sm_count, cudaStream_t stream) {
     const uint32_t rows_pad = mx_rows_pad(view.rows);
     const uint32_t blocks_pad = mx_blocks_pad(weights.blocks);
+    const size_t items_bytes = static_cast<size_t>(rows_pad) * blocks_pad;
+    const bool tcgen05 = weights.mx_values != nullptr && weights.mx_scales_t != nullptr;
     MxSplitParams split{view, rows_pad, blocks_pad, reinterpret_cast<int8_t *>(scratch),
-                        reinterpret_cast<int2 *>(scratch + static_cast<size_t>(rows_pad) * blocks_pad * 32)};
+                        reinterpret_cast<int2 *>(scratch + items_bytes * 32),
+                        tcgen05 ? reinterpret_cast<float *>(scratch + items_bytes * 40) : nullptr};
     const uint64_t items = static_cast<uint64_t>(rows_pad) * blocks_pad;
     const uint32_t split_grid = static_cast<uint32_t>(items / 256 + 1 < 148ull * 32ull ? items / 256 + 1 : 148ull * 32ull);
     q4_0_mx_split_kernel<<<split_grid, 256, 0, stream>>>(split);
     cudaError_t error = cudaGetLastError();
     if (error != cudaSuccess) return error;
+    if (tcgen05) {
+        return launch_q4_0_mx_sm100(split.q, split.da_t, view.rows, rows_pad, weights.mx_values, weights.mx_scales_t,
+                                    weights.columns, weights.blocks, blocks_pad, destination, destination_stride, col0,
+                                    out_col0, count, error_word, sm_count, stream);
+    }
     MxParams p{};
     p.q = split.q;
     p.meta = split.meta;
@@ -944,14 +954,17 @@ cudaError_t launch_q4_0_f32_gemv(const Q40Weights &weights, const float *source,
     }
 }
 
+// int8 rows (32 bytes per block), {d_a, 8 * sum} pairs (8), and the block-major d_a copy (4).
 size_t q4_0_mx_scratch_bytes(uint32_t rows, uint32_t blocks) {
-    return static_cast<size_t>(mx_rows_pad(rows)) * mx_blocks_pad(blocks) * (32 + 8);
+    return static_cast<size_t>(mx_rows_pad(rows)) * mx_blocks_pad(blocks) * (32 + 8 + 4);
 }
+
+uint32_t q4_0_mx_blocks_pad(uint32_t blocks) { return mx_blocks_pad(blocks); }
 
 cudaError_t launch_q4_0_mx(const Q40Weights &weights, const uint8_t *activation, const float *f32_source,
                            size_t f32_stride, uint32_t rows, uint32_t interleave, uint8_t *scratch, float *destination,
-                           size_t destination_stride, uint32_t col0, uint32_t out_col0, uint32_t count, int sm_count,
-                           cudaStream_t stream) {
+                           size_t destination_stride, uint32_t col0, uint32_t out_col0, uint32_t count,
+                           unsigned int *error_word, int sm_count, cudaStream_t stream) {
     if (count == 0 || rows == 0) return cudaSuccess;
     if ((reinterpret_cast<uintptr_t>(weights.nibbles) & 15u) != 0 || (reinterpret_cast<uintptr_t>(weights.scales) & 15u) != 0 ||
         (reinterpret_cast<uintptr_t>(scratch) & 15u) != 0 || weights.scale_stride % 8 != 0 ||
@@ -963,7 +976,8 @@ cudaError_t launch_q4_0_mx(const Q40Weights &weights, const uint8_t *activation,
     }
     const ActivationView view{activation, rows, weights.blocks, f32_source != nullptr ? 0u : interleave, f32_source,
                               f32_stride};
-    return launch_mx(weights, view, scratch, destination, destination_stride, col0, out_col0, count, sm_count, stream);
+    return launch_mx(weights, view, scratch, destination, destination_stride, col0, out_col0, count, error_word, sm_count,
+                     stream);
 }
 
 cudaError_t launch_q4_0_q8_0_gemv_native(const uint8_t *activation, uint32_t rows, uint32_t blocks,

@@ -1,0 +1,481 @@
+// Q4_0 x Q8_0 for rows > 4 (the reference's MX path) on the 5th-generation tensor cores.
+//
+// The reference's tiled Q4_0 x Q8_0 program (src/qpu_xla/kernels/ggml_q4_0.py:310-547, prepared by
+// qpu_llama_q4_0.c:238-290 for rows > 4, EXACT weight mode) keeps one fp32 accumulator per output
+// and adds the blocks in order: acc += ((float)dot_b * d_a[m, b]) * d_w[n, b] (itof, fmul by the
+// activation scale, fmul by the weight scale, fadd; ggml_q4_0.py:506-513). Every block's integer
+// dot has to reach the fp32 arithmetic on its own, so the K reduction cannot stay inside the
+// tensor core: each 32-deep block is one tcgen05.mma (M = 128, N = 128, K = 32, s8 x s8 -> s32)
+// into its own tensor-memory slot, and the epilogue warps drain the slots block by block.
+//
+// Operands (prepared once): the weight codes expanded to int8 (code - 8), K-major rows of
+// blocks_pad * 32 bytes, and the fp32 weight scales block-major [blocks_pad][columns]; per call the
+// split activation (int8 rows of blocks_pad * 32 bytes, zero-padded) and its fp32 scales
+// block-major [blocks_pad][rows_pad]. TMA moves a stage of four blocks of each (A and W tiles in
+// the 128-byte swizzle the MMA descriptors read, the two scale boxes plain).
+//
+// Exact (float)dot without a conversion instruction: every slot is seeded with the int32 bits of
+// 1.5 * 2^23 (0x4B400000) and the MMA accumulates onto the seed, so the slot holds the float bits
+// of 1.5 * 2^23 + dot (|dot| <= 32 * 8 * 128 < 2^22, one ulp = 1); one subtraction of 1.5 * 2^23
+// gives (float)dot exactly. The epilogue re-seeds a slot as it drains it.
+//
+// Warps: 0 TMA producer, 1 tensor-memory allocator and MMA issuer (one thread), 2..9 epilogue.
+// Epilogue warp w reads the tensor-memory lanes of its quarter (w % 4: 32 rows, one per thread)
+// and half of the tile's columns ((w - 2) / 4), 32 columns at a time, and keeps 64 fp32
+// accumulators per thread. Stage reuse waits for the MMA commit and for all eight epilogue warps
+// (which read the stage's scales); slot reuse waits for the eight epilogue warps. Every mbarrier
+// wait is bounded.
+#include <cuda_fp16.h>
+
+#include <cstring>
+
+#include "qpucuda_internal.h"
+#include "sm100_sync.cuh"
+
+namespace qpucuda {
+namespace {
+
+constexpr int kBM = 128;              // rows per tile (tensor-memory lanes)
+constexpr int kBN = 128;              // output columns per tile
+constexpr int kKB = 4;                // Q4_0 blocks per stage: 128 bytes of K
+constexpr int kStages = 4;
+constexpr int kSlots = 4;             // tensor-memory accumulators of kBN columns (all 512 columns)
+constexpr int kEpilogueWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpilogueWarps;
+constexpr int kCols = kBN / (kEpilogueWarps / 4);  // columns per epilogue thread
+constexpr uint32_t kMagicBits = 0x4B400000u;  // 1.5 * 2^23
+constexpr float kMagic = 12582912.0f;
+
+constexpr int kTileA = kBM * 128;
+constexpr int kTileW = kBN * 128;
+constexpr int kTileDa = kKB * kBM * 4;
+constexpr int kTileDw = kKB * kBN * 4;
+constexpr int kStageBytes = kTileA + kTileW + kTileDa + kTileDw;
+static_assert(kStageBytes % 1024 == 0, "stages keep the 1024-byte alignment of the swizzled tiles");
+
+struct Control {
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
+    uint64_t slot_full[kSlots];
+    uint64_t slot_empty[kSlots];
+    uint64_t drain;
+    uint32_t tmem_base;
+    volatile int abort_flag;
+};
+
+constexpr size_t kSmemBytes = static_cast<size_t>(kStages) * kStageBytes + 1024 + sizeof(Control);
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+
+// D = s32, A = s8, B = s8, both K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
+constexpr uint32_t kInstrDesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
+                                (static_cast<uint32_t>(kBM >> 4) << 24);
+
+struct MxParams {
+    uint32_t rows;      // outputs are written for rows < rows
+    uint32_t blocks;    // real Q4_0 blocks (later ones are zero padding)
+    uint32_t k_stages;  // blocks_pad / kKB
+    uint32_t m_tiles, n_tiles;
+    uint32_t col0;      // first weight column of the call (within the resident window)
+    uint32_t count;     // columns computed
+    uint32_t out_col0;  // destination column of weight column col0
+    float *destination;
+    size_t destination_stride;
+    unsigned int *error_word;
+};
+
+using namespace sm100;
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t address) {
+    // start >> 4 (bits 0-13), leading byte offset 16 B (unused for swizzled K-major), stride byte
+    // offset 1024 B (8 rows of 128 B), descriptor version 1, 128-byte swizzle.
+    return static_cast<uint64_t>((address & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
+}
+
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc) {
+    // accumulate onto the slot's seed (enable-input-d = true)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 1, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(kInstrDesc)
+        : "memory");
+}
+
+__device__ __forceinline__ void commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// 32 lanes x 32 columns of 32-bit words from tensor memory (the caller waits with tmem_wait_ld,
+// which names the registers so nothing reads them early).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+                   "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                   "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
+
+// The seed into 32 lanes x 32 columns of tensor memory.
+__device__ __forceinline__ void tmem_seed32(uint32_t taddr) {
+    const uint32_t m = kMagicBits;
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+        "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
+        "r"(m)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+    return static_cast<unsigned long long>(__float_as_uint(lo)) | (static_cast<unsigned long long>(__float_as_uint(hi)) << 32);
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// 32 columns of one block: acc[j] += (((float)dot_j) * da) * dw[j], in that rounding order.
+// r holds the slot words (float bits of 1.5 * 2^23 + dot), dw points at the block's 32 column
+// scales in shared memory (the same address in every lane: a broadcast).
+__device__ __forceinline__ void accumulate32(float *acc, const uint32_t (&r)[32], float da, const float *dw) {
+    const unsigned long long minus_magic = pack2(-kMagic, -kMagic);
+    const unsigned long long da2 = pack2(da, da);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const float4 w = *reinterpret_cast<const float4 *>(dw + 4 * q);
+        unsigned long long lo = add2(pack2(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1])), minus_magic);
+        unsigned long long hi = add2(pack2(__uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])), minus_magic);
+        lo = mul2(mul2(lo, da2), pack2(w.x, w.y));
+        hi = mul2(mul2(hi, da2), pack2(w.z, w.w));
+        acc[4 * q] = __fadd_rn(acc[4 * q], __uint_as_float(static_cast<uint32_t>(lo)));
+        acc[4 * q + 1] = __fadd_rn(acc[4 * q + 1], __uint_as_float(static_cast<uint32_t>(lo >> 32)));
+        acc[4 * q + 2] = __fadd_rn(acc[4 * q + 2], __uint_as_float(static_cast<uint32_t>(hi)));
+        acc[4 * q + 3] = __fadd_rn(acc[4 * q + 3], __uint_as_float(static_cast<uint32_t>(hi >> 32)));
+    }
+}
+
+__global__ void __launch_bounds__(kThreads)
+    q4_0_mx_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
+                         const __grid_constant__ CUtensorMap map_da, const __grid_constant__ CUtensorMap map_dw,
+                         const MxParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Control *control = reinterpret_cast<Control *>(smem + kStages * kStageBytes);
+    auto stage_a = [&](uint32_t s) { return smem + s * kStageBytes; };
+    auto stage_w = [&](uint32_t s) { return smem + s * kStageBytes + kTileA; };
+    auto stage_da = [&](uint32_t s) { return reinterpret_cast<const float *>(smem + s * kStageBytes + kTileA + kTileW); };
+    auto stage_dw = [&](uint32_t s) {
+        return reinterpret_cast<const float *>(smem + s * kStageBytes + kTileA + kTileW + kTileDa);
+    };
+
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t tiles = p.m_tiles * p.n_tiles;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_u32(&control->full[s]), 1);
+            mbar_init(smem_u32(&control->empty[s]), 1 + kEpilogueWarps);
+        }
+        for (int s = 0; s < kSlots; ++s) {
+            mbar_init(smem_u32(&control->slot_full[s]), 1);
+            mbar_init(smem_u32(&control->slot_empty[s]), kEpilogueWarps);
+        }
+        mbar_init(smem_u32(&control->drain), 1);
+        control->abort_flag = 0;
+        mbar_init_fence();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&control->tmem_base)),
+                     "r"(kSlots * kBN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+    const uint32_t tmem_base = control->tmem_base;
+    const uint32_t quarter = warp & 3u;
+    const uint32_t part = warp >= 2 ? (warp - 2u) / 4u : 0u;  // column quarter of an epilogue warp
+    if (warp >= 2) {
+        // every slot starts out holding the seed
+        for (int s = 0; s < kSlots; ++s) {
+            for (int c = 0; c < kCols; c += 32) tmem_seed32(tmem_base + ((quarter * 32u) << 16) + s * kBN + part * kCols + c);
+        }
+        tmem_wait_st();
+    }
+    fence_before();
+    __syncthreads();
+    fence_after();
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            prefetch_tensor_map(&map_a);
+            prefetch_tensor_map(&map_w);
+            prefetch_tensor_map(&map_da);
+            prefetch_tensor_map(&map_dw);
+            uint32_t stage = 0, phase = 0, issued_mask = 0, issued_phases = 0;
+            bool ok = true;
+            for (uint32_t tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+                const int m0 = static_cast<int>((tile % p.m_tiles) * kBM);
+                const int n0 = static_cast<int>(p.col0 + (tile / p.m_tiles) * kBN);
+                for (uint32_t ks = 0; ks < p.k_stages; ++ks) {
+                    if (!wait_bounded(smem_u32(&control->empty[stage]), phase ^ 1u, &control->abort_flag, p.error_word)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t full = smem_u32(&control->full[stage]);
+                    mbar_expect_tx(full, kStageBytes);
+                    tma_load_2d(smem_u32(stage_a(stage)), &map_a, full, static_cast<int>(ks * 128), m0);
+                    tma_load_2d(smem_u32(stage_w(stage)), &map_w, full, static_cast<int>(ks * 128), n0);
+                    tma_load_2d(smem_u32(stage_da(stage)), &map_da, full, m0, static_cast<int>(ks * kKB));
+                    tma_load_2d(smem_u32(stage_dw(stage)), &map_dw, full, n0, static_cast<int>(ks * kKB));
+                    issued_mask |= 1u << stage;
+                    issued_phases = (issued_phases & ~(1u << stage)) | (phase << stage);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok) {
+                for (int s = 0; s < kStages; ++s)
+                    if ((issued_mask >> s) & 1u) wait_drain(smem_u32(&control->full[s]), (issued_phases >> s) & 1u);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer: one MMA per block, each into its own slot ----------------
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, slot = 0, slot_phase = 0;
+            bool ok = true, any = false;
+            for (uint32_t tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+                for (uint32_t ks = 0; ok && ks < p.k_stages; ++ks) {
+                    ok = wait_bounded(smem_u32(&control->full[stage]), phase, &control->abort_flag, p.error_word);
+                    if (!ok) break;
+                    fence_after();
+                    const uint64_t a_desc = smem_desc_sw128(smem_u32(stage_a(stage)));
+                    const uint64_t w_desc = smem_desc_sw128(smem_u32(stage_w(stage)));
+#pragma unroll 1
+                    for (uint32_t b = 0; b < kKB; ++b) {
+                        ok = wait_bounded(smem_u32(&control->slot_empty[slot]), slot_phase ^ 1u, &control->abort_flag,
+                                          p.error_word);
+                        if (!ok) break;
+                        fence_after();
+                        // block b starts 32 bytes further along the swizzled 128-byte rows
+                        mma_i8(tmem_base + slot * kBN, a_desc + 2u * b, w_desc + 2u * b);
+                        commit(smem_u32(&control->slot_full[slot]));
+                        any = true;
+                        if (++slot == kSlots) {
+                            slot = 0;
+                            slot_phase ^= 1u;
+                        }
+                    }
+                    if (!ok) break;
+                    commit(smem_u32(&control->empty[stage]));  // this stage's MMAs are done reading it
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            if (!ok && any) {
+                commit(smem_u32(&control->drain));
+                wait_drain(smem_u32(&control->drain), 0);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: drain, re-seed, scale and accumulate, block by block ----------------
+        const uint32_t row_in_tile = quarter * 32u + lane;
+        const uint32_t lane_base = tmem_base + ((quarter * 32u) << 16) + part * kCols;
+        uint32_t stage = 0, phase = 0, slot = 0, slot_phase = 0;
+        bool ok = true;
+        for (uint32_t tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
+            const uint32_t m = (tile % p.m_tiles) * kBM + row_in_tile;
+            const uint32_t n_local = (tile / p.m_tiles) * kBN + part * kCols;  // relative to col0
+            float acc[kCols];
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) acc[j] = 0.0f;
+            for (uint32_t ks = 0; ok && ks < p.k_stages; ++ks) {
+                if (lane == 0) ok = wait_bounded(smem_u32(&control->full[stage]), phase, &control->abort_flag, p.error_word);
+                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                if (!ok) break;
+                const float *da = stage_da(stage);
+                const float *dw = stage_dw(stage);
+#pragma unroll 1
+                for (uint32_t b = 0; b < kKB; ++b) {
+                    if (lane == 0)
+                        ok = wait_bounded(smem_u32(&control->slot_full[slot]), slot_phase, &control->abort_flag, p.error_word);
+                    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                    if (!ok) break;
+                    fence_after();
+                    const uint32_t taddr = lane_base + slot * kBN;
+                    const bool real = ks * kKB + b < p.blocks;
+                    const float scale_a = da[b * kBM + row_in_tile];
+#pragma unroll
+                    for (int c = 0; c < kCols; c += 32) {
+                        uint32_t r[32];
+                        tmem_ld32(taddr + c, r);
+                        tmem_wait_ld(r);
+                        tmem_seed32(taddr + c);
+                        if (real) accumulate32(acc + c, r, scale_a, dw + b * kBN + part * kCols + c);
+                    }
+                    tmem_wait_st();
+                    fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(&control->slot_empty[slot]));
+                    if (++slot == kSlots) {
+                        slot = 0;
+                        slot_phase ^= 1u;
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(&control->empty[stage]));  // done with this stage's scales
+                if (++stage == kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+            if (m < p.rows && n_local < p.count) {
+                float *out = p.destination + static_cast<size_t>(m) * p.destination_stride + p.out_col0 + n_local;
+                const uint32_t valid = p.count - n_local < static_cast<uint32_t>(kCols) ? p.count - n_local : kCols;
+                if (valid == static_cast<uint32_t>(kCols) && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+#pragma unroll
+                    for (int j = 0; j < kCols; j += 4)
+                        *reinterpret_cast<float4 *>(out + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < kCols; ++j)
+                        if (static_cast<uint32_t>(j) < valid) out[j] = acc[j];
+                }
+            }
+        }
+    }
+
+    fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kSlots * kBN) : "memory");
+    }
+}
+
+// Native-to-MX weight expansion (prepare time): codes of [columns][blocks][16] nibble bytes to
+// int8 (code - 8) rows of blocks_pad * 32 bytes (zero padding), fp16 scales [columns][scale_stride]
+// to fp32 block-major [blocks_pad][columns] (zeros for padded blocks). One thread per (column, block).
+__global__ void __launch_bounds__(256) q4_0_mx_expand_kernel(const uint8_t *__restrict__ nibbles,
+                                                             const uint16_t *__restrict__ scales, uint32_t columns,
+                                                             uint32_t blocks, uint32_t blocks_pad, uint32_t scale_stride,
+                                                             int8_t *__restrict__ values, float *__restrict__ scales_t) {
+    const uint64_t total = static_cast<uint64_t>(columns) * blocks_pad;
+    for (uint64_t item = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; item < total;
+         item += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        const uint32_t column = static_cast<uint32_t>(item / blocks_pad);
+        const uint32_t block = static_cast<uint32_t>(item % blocks_pad);
+        int8_t out[32] = {};
+        float d = 0.0f;
+        if (block < blocks) {
+            // byte j of the block holds code j in its low nibble and code j + 16 in its high nibble
+            const uint8_t *codes = nibbles + (static_cast<size_t>(column) * blocks + block) * 16;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                out[j] = static_cast<int8_t>(static_cast<int>(codes[j] & 0x0F) - 8);
+                out[16 + j] = static_cast<int8_t>(static_cast<int>(codes[j] >> 4) - 8);
+            }
+            d = __half2float(__ushort_as_half(scales[static_cast<size_t>(column) * scale_stride + block]));
+        }
+        int8_t *row = values + (static_cast<size_t>(column) * blocks_pad + block) * 32;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) row[j] = out[j];
+        scales_t[static_cast<size_t>(block) * columns + column] = d;
+    }
+}
+
+}  // namespace
+}  // namespace qpucuda
+
+namespace qpucuda {
+
+bool q4_0_mx_sm100_available(int cc_major, int cc_minor) { return cc_major == 10 && cc_minor == 0; }
+
+cudaError_t launch_q4_0_mx_expand(const uint8_t *nibbles, const uint16_t *scales, uint32_t columns, uint32_t blocks,
+                                  uint32_t blocks_pad, uint32_t scale_stride, int8_t *values, float *scales_t,
+                                  cudaStream_t stream) {
+    const uint64_t items = static_cast<uint64_t>(columns) * blocks_pad;
+    if (items == 0) return cudaSuccess;
+    const uint32_t grid = static_cast<uint32_t>(items / 256 + 1 < 148ull * 32ull ? items / 256 + 1 : 148ull * 32ull);
+    q4_0_mx_expand_kernel<<<grid, 256, 0, stream>>>(nibbles, scales, columns, blocks, blocks_pad, scale_stride, values,
+                                                    scales_t);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_q4_0_mx_sm100(const int8_t *q, const float *da_t, uint32_t rows, uint32_t rows_pad,
+                                 const int8_t *values, const float *scales_t, uint32_t columns, uint32_t blocks,
+                                 uint32_t blocks_pad, float *destination, size_t destination_stride, uint32_t col0,
+                                 uint32_t out_col0, uint32_t count, unsigned int *error_word, int sm_count,
+                                 cudaStream_t stream) {
+    if (rows == 0 || count == 0) return cudaSuccess;
+    if (blocks_pad % kKB != 0 || blocks_pad < blocks || col0 % 16 != 0 || columns % 4 != 0 || rows_pad % 4 != 0 ||
+        col0 + count > columns) {
+        return cudaErrorInvalidValue;
+    }
+    static PerDeviceOnce configured;
+    const cudaError_t configure_error = configured.run([] {
+        return cudaFuncSetAttribute(q4_0_mx_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    static_cast<int>(kSmemBytes));
+    });
+    if (configure_error != cudaSuccess) return configure_error;
+    const uint64_t k_bytes = static_cast<uint64_t>(blocks_pad) * 32;
+    CUtensorMap map_a, map_w, map_da, map_dw;
+    if (!encode_tensor_map_2d_u8(&map_a, q, k_bytes, rows_pad, k_bytes, 128, kBM) ||
+        !encode_tensor_map_2d_u8(&map_w, values, k_bytes, columns, k_bytes, 128, kBN) ||
+        !encode_tensor_map_2d_f32(&map_da, da_t, rows_pad, blocks_pad, static_cast<uint64_t>(rows_pad) * 4, kBM, kKB) ||
+        !encode_tensor_map_2d_f32(&map_dw, scales_t, columns, blocks_pad, static_cast<uint64_t>(columns) * 4, kBN, kKB)) {
+        return cudaErrorInvalidValue;
+    }
+    MxParams p{};
+    p.rows = rows;
+    p.blocks = blocks;
+    p.k_stages = blocks_pad / kKB;
+    p.m_tiles = (rows + kBM - 1) / kBM;
+    p.n_tiles = (count + kBN - 1) / kBN;
+    p.col0 = col0;
+    p.count = count;
+    p.out_col0 = out_col0;
+    p.destination = destination;
+    p.destination_stride = destination_stride;
+    p.error_word = error_word;
+    const uint64_t tiles = static_cast<uint64_t>(p.m_tiles) * p.n_tiles;
+    const uint32_t grid = static_cast<uint32_t>(tiles < static_cast<uint64_t>(sm_count) ? tiles : sm_count);
+    q4_0_mx_sm100_kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_w, map_da, map_dw, p);
+    return cudaGetLastError();
+}
+
+}  // namespace qpucuda

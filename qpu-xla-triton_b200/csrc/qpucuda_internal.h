@@ -107,6 +107,9 @@ bool encode_tensor_map_2d_u8(CUtensorMap *map, const void *base, uint64_t inner_
 // The same for 4-byte elements (fp32 / int32 outputs written by TMA stores), 128-byte swizzle.
 bool encode_tensor_map_2d_b32(CUtensorMap *map, const void *base, uint64_t columns, uint64_t rows,
                               uint64_t row_stride_bytes, uint32_t box_columns, uint32_t box_rows);
+// fp32 tiles without swizzle (scale boxes loaded next to swizzled operand tiles).
+bool encode_tensor_map_2d_f32(CUtensorMap *map, const void *base, uint64_t columns, uint64_t rows,
+                              uint64_t row_stride_bytes, uint32_t box_columns, uint32_t box_rows);
 
 // ---- kernel launchers (one per .cu file) -------------------------------------------------
 
@@ -194,7 +197,24 @@ struct Q40Weights {
     uint32_t columns = 0;
     uint32_t blocks = 0;
     uint32_t scale_stride = 0;  // blocks rounded up to a multiple of 8 (16-byte rows)
+    // Rows > 4 on sm_100 (the tcgen05 MX kernel), expanded once at prepare, or null: the codes as
+    // int8 (code - 8) [columns][q4_0_mx_blocks_pad(blocks) * 32] and the fp32 scales block-major
+    // [q4_0_mx_blocks_pad(blocks)][columns], both zero-padded.
+    const int8_t *mx_values = nullptr;
+    const float *mx_scales_t = nullptr;
 };
+uint32_t q4_0_mx_blocks_pad(uint32_t blocks);
+// Fills the expanded MX operands above from the prepared nibbles and fp16 scales.
+cudaError_t launch_q4_0_mx_expand(const uint8_t *nibbles, const uint16_t *scales, uint32_t columns, uint32_t blocks,
+                                  uint32_t blocks_pad, uint32_t scale_stride, int8_t *values, float *scales_t,
+                                  cudaStream_t stream);
+// The tcgen05 MX kernel: split activation q (int8 [rows_pad][blocks_pad * 32]) and its scales
+// da_t (fp32 [blocks_pad][rows_pad]) against the expanded weights; columns = resident columns.
+cudaError_t launch_q4_0_mx_sm100(const int8_t *q, const float *da_t, uint32_t rows, uint32_t rows_pad,
+                                 const int8_t *values, const float *scales_t, uint32_t columns, uint32_t blocks,
+                                 uint32_t blocks_pad, float *destination, size_t destination_stride, uint32_t col0,
+                                 uint32_t out_col0, uint32_t count, unsigned int *error_word, int sm_count,
+                                 cudaStream_t stream);
 inline uint32_t q4_0_scale_stride(uint32_t blocks) { return (blocks + 7u) & ~7u; }
 // activation: native Q8_0 rows [rows][blocks][34] (interleave 0) or CPU_REPACK
 // block_q8_0x4 groups (interleave 4/8). Writes destination[r * stride + out_col0 + j]
@@ -210,12 +230,13 @@ cudaError_t launch_q4_0_f32_gemv(const Q40Weights &weights, const float *source,
                                  uint32_t count, int sm_count, cudaStream_t stream);
 // Rows > 4 (the reference's MX path) on the tensor cores: splits the activation (Q8_0 blocks, or
 // fp32 rows quantized on the fly; exactly one of the two) into `scratch` of
-// q4_0_mx_scratch_bytes(rows, blocks) bytes (16-byte aligned), then the tiled mma.sync kernel.
+// q4_0_mx_scratch_bytes(rows, blocks) bytes (16-byte aligned), then the tcgen05 kernel when the
+// weights carry the expanded MX operands, else the tiled mma.sync kernel.
 size_t q4_0_mx_scratch_bytes(uint32_t rows, uint32_t blocks);
 cudaError_t launch_q4_0_mx(const Q40Weights &weights, const uint8_t *activation, const float *f32_source,
                            size_t f32_stride, uint32_t rows, uint32_t interleave, uint8_t *scratch, float *destination,
-                           size_t destination_stride, uint32_t col0, uint32_t out_col0, uint32_t count, int sm_count,
-                           cudaStream_t stream);
+                           size_t destination_stride, uint32_t col0, uint32_t out_col0, uint32_t count,
+                           unsigned int *error_word, int sm_count, cudaStream_t stream);
 // Native 18-byte blocks [columns][blocks][18] -> prepared layout (scales rows of scale_stride,
 // the padding must be zeroed beforehand).
 cudaError_t launch_q4_0_repack(const uint8_t *native, uint32_t columns, uint32_t blocks, uint32_t scale_stride,

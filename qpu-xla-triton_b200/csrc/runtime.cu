@@ -192,6 +192,24 @@ bool encode_tensor_map_2d_b32(CUtensorMap *map, const void *base, uint64_t colum
     return result == CUDA_SUCCESS;
 }
 
+bool encode_tensor_map_2d_f32(CUtensorMap *map, const void *base, uint64_t columns, uint64_t rows,
+                              uint64_t row_stride_bytes, uint32_t box_columns, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (fn == nullptr) return false;
+    if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (row_stride_bytes & 15u) != 0 || (box_columns * 4u) % 16u != 0) {
+        return false;
+    }
+    const cuuint64_t dims[2] = {columns, rows};
+    const cuuint64_t strides[1] = {row_stride_bytes};
+    const cuuint32_t box[2] = {box_columns, box_rows};
+    const cuuint32_t element_strides[2] = {1, 1};
+    const CUresult result =
+        fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box, element_strides,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return result == CUDA_SUCCESS;
+}
+
 }  // namespace qpucuda
 
 using namespace qpucuda;

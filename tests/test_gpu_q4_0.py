@@ -296,6 +296,7 @@ def test_decode_full_size_columns_sample(native, shape) -> None:  # type: ignore
         (64, 4128, 160, 0, 160),  # 129 blocks: a partial last K stage
         (100, 5632, 2048, 512, 1024),  # ragged rows, a column window
         (300, 8192, 384, 128, 256),  # several row tiles, a partial column tile
+        (1000, 4096, 528, 16, 512),  # 8 row tiles of 128 (ragged last), 4 column tiles from column 16
     ],
 )
 def test_mx_rows_match_the_reference_program(native, rows: int, k: int, n: int, start: int, count: int) -> None:  # type: ignore[no-untyped-def]

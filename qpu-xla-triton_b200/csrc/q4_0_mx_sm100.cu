@@ -14,17 +14,19 @@
 // block-major [blocks_pad][rows_pad]. TMA moves a stage of four blocks of each (A and W tiles in
 // the 128-byte swizzle the MMA descriptors read, the two scale boxes plain).
 //
-// Exact (float)dot without a conversion instruction: every slot is seeded with the int32 bits of
-// 1.5 * 2^23 (0x4B400000) and the MMA accumulates onto the seed, so the slot holds the float bits
-// of 1.5 * 2^23 + dot (|dot| <= 32 * 8 * 128 < 2^22, one ulp = 1); one subtraction of 1.5 * 2^23
-// gives (float)dot exactly. The epilogue re-seeds a slot as it drains it.
+// Exact (float)dot without a conversion instruction (an int-to-float convert runs at a quarter of
+// the fp32 rate): the MMA overwrites its slot with the s32 dot, and the epilogue adds the int32
+// bits of 1.5 * 2^23 (0x4B400000) to it with one integer add, which gives the float bits of
+// 1.5 * 2^23 + dot (|dot| <= 32 * 8 * 128 < 2^22, one ulp = 1); one fp32 subtraction of
+// 1.5 * 2^23 then gives (float)dot exactly.
 //
-// Warps: 0 TMA producer, 1 tensor-memory allocator and MMA issuer (one thread), 2..9 epilogue.
+// Warps: 0 TMA producer, 1 tensor-memory allocator and MMA issuer (one thread), 2..17 epilogue.
 // Epilogue warp w reads the tensor-memory lanes of its quarter (w % 4: 32 rows, one per thread)
-// and half of the tile's columns ((w - 2) / 4), 32 columns at a time, and keeps 64 fp32
-// accumulators per thread. Stage reuse waits for the MMA commit and for all eight epilogue warps
-// (which read the stage's scales); slot reuse waits for the eight epilogue warps. Every mbarrier
-// wait is bounded.
+// and a quarter of the tile's columns ((w - 2) / 4), and keeps 32 fp32 accumulators per thread.
+// Four epilogue warps per scheduler hide the latency of the tensor-memory loads. Stage reuse
+// waits for the MMA commit and for every epilogue thread (they read the stage's scales); a slot is
+// free again once every epilogue thread has loaded its words, before their fp32 work on them.
+// Every mbarrier wait is bounded.
 #include <cuda_fp16.h>
 
 #include <cstring>
@@ -40,9 +42,11 @@ constexpr int kBN = 128;              // output columns per tile
 constexpr int kKB = 4;                // Q4_0 blocks per stage: 128 bytes of K
 constexpr int kStages = 4;
 constexpr int kSlots = 4;             // tensor-memory accumulators of kBN columns (all 512 columns)
-constexpr int kEpilogueWarps = 8;
+constexpr int kEpilogueWarps = 16;
 constexpr int kThreads = 64 + 32 * kEpilogueWarps;
 constexpr int kCols = kBN / (kEpilogueWarps / 4);  // columns per epilogue thread
+constexpr int kChunks = kCols / 16;                // 16-column tensor-memory loads per block
+static_assert(kChunks % 2 == 0, "chunks alternate between two register buffers");
 constexpr uint32_t kMagicBits = 0x4B400000u;  // 1.5 * 2^23
 constexpr float kMagic = 12582912.0f;
 
@@ -96,9 +100,9 @@ __device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::be
 __device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 __device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc) {
-    // accumulate onto the slot's seed (enable-input-d = true)
+    // overwrite the slot (enable-input-d = false): it holds this block's dot alone
     asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 1, 0;\n\t"
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 0, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
         "l"(a_desc), "l"(b_desc), "r"(kInstrDesc)
         : "memory");
@@ -108,42 +112,23 @@ __device__ __forceinline__ void commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-// 32 lanes x 32 columns of 32-bit words from tensor memory (the caller waits with tmem_wait_ld,
-// which names the registers so nothing reads them early).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+// 32 lanes x 16 columns of 32-bit words from tensor memory; the caller waits with tmem_wait_ld16,
+// which names the registers so nothing reads them before the load has landed.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
-
-__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
+__device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;"
                  : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
-                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
-                   "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
-                   "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
                  :
                  : "memory");
 }
-
-// The seed into 32 lanes x 32 columns of tensor memory.
-__device__ __forceinline__ void tmem_seed32(uint32_t taddr) {
-    const uint32_t m = kMagicBits;
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-        "{%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-        "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
-        "r"(m)
-        : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
 __device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
     return static_cast<unsigned long long>(__float_as_uint(lo)) | (static_cast<unsigned long long>(__float_as_uint(hi)) << 32);
 }
@@ -158,17 +143,18 @@ __device__ __forceinline__ unsigned long long mul2(unsigned long long a, unsigne
     return d;
 }
 
-// 32 columns of one block: acc[j] += (((float)dot_j) * da) * dw[j], in that rounding order.
-// r holds the slot words (float bits of 1.5 * 2^23 + dot), dw points at the block's 32 column
-// scales in shared memory (the same address in every lane: a broadcast).
-__device__ __forceinline__ void accumulate32(float *acc, const uint32_t (&r)[32], float da, const float *dw) {
+// 16 columns of one block: acc[j] += (((float)dot_j) * da) * dw[j], in that rounding order. r holds
+// the slot words (s32 dots), dw the block's column scales in shared memory (the same address in
+// every lane: a broadcast). The subtraction and the two multiplies run on packed pairs (each half
+// rounded exactly as __fadd_rn / __fmul_rn); the accumulation is a scalar __fadd_rn per column.
+__device__ __forceinline__ void accumulate16(float *acc, const uint32_t (&r)[16], float da, const float *dw) {
     const unsigned long long minus_magic = pack2(-kMagic, -kMagic);
     const unsigned long long da2 = pack2(da, da);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
+    for (int q = 0; q < 4; ++q) {
         const float4 w = *reinterpret_cast<const float4 *>(dw + 4 * q);
-        unsigned long long lo = add2(pack2(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1])), minus_magic);
-        unsigned long long hi = add2(pack2(__uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])), minus_magic);
+        unsigned long long lo = add2(pack2(__uint_as_float(r[4 * q] + kMagicBits), __uint_as_float(r[4 * q + 1] + kMagicBits)), minus_magic);
+        unsigned long long hi = add2(pack2(__uint_as_float(r[4 * q + 2] + kMagicBits), __uint_as_float(r[4 * q + 3] + kMagicBits)), minus_magic);
         lo = mul2(mul2(lo, da2), pack2(w.x, w.y));
         hi = mul2(mul2(hi, da2), pack2(w.z, w.w));
         acc[4 * q] = __fadd_rn(acc[4 * q], __uint_as_float(static_cast<uint32_t>(lo)));
@@ -178,7 +164,7 @@ __device__ __forceinline__ void accumulate32(float *acc, const uint32_t (&r)[32]
     }
 }
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 1)
     q4_0_mx_sm100_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_w,
                          const __grid_constant__ CUtensorMap map_da, const __grid_constant__ CUtensorMap map_dw,
                          const MxParams p) {
@@ -199,11 +185,11 @@ __global__ void __launch_bounds__(kThreads)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(smem_u32(&control->full[s]), 1);
-            mbar_init(smem_u32(&control->empty[s]), 1 + kEpilogueWarps);
+            mbar_init(smem_u32(&control->empty[s]), 1 + 32 * kEpilogueWarps);  // the MMA commit + every epilogue thread
         }
         for (int s = 0; s < kSlots; ++s) {
             mbar_init(smem_u32(&control->slot_full[s]), 1);
-            mbar_init(smem_u32(&control->slot_empty[s]), kEpilogueWarps);
+            mbar_init(smem_u32(&control->slot_empty[s]), 32 * kEpilogueWarps);
         }
         mbar_init(smem_u32(&control->drain), 1);
         control->abort_flag = 0;
@@ -221,13 +207,6 @@ __global__ void __launch_bounds__(kThreads)
     const uint32_t tmem_base = control->tmem_base;
     const uint32_t quarter = warp & 3u;
     const uint32_t part = warp >= 2 ? (warp - 2u) / 4u : 0u;  // column quarter of an epilogue warp
-    if (warp >= 2) {
-        // every slot starts out holding the seed
-        for (int s = 0; s < kSlots; ++s) {
-            for (int c = 0; c < kCols; c += 32) tmem_seed32(tmem_base + ((quarter * 32u) << 16) + s * kBN + part * kCols + c);
-        }
-        tmem_wait_st();
-    }
     fence_before();
     __syncthreads();
     fence_after();
@@ -245,7 +224,7 @@ __global__ void __launch_bounds__(kThreads)
                 const int m0 = static_cast<int>((tile % p.m_tiles) * kBM);
                 const int n0 = static_cast<int>(p.col0 + (tile / p.m_tiles) * kBN);
                 for (uint32_t ks = 0; ks < p.k_stages; ++ks) {
-                    if (!wait_bounded(smem_u32(&control->empty[stage]), phase ^ 1u, &control->abort_flag, p.error_word)) {
+                    if (!wait_bounded_suspend(smem_u32(&control->empty[stage]), phase ^ 1u, &control->abort_flag, p.error_word)) {
                         ok = false;
                         break;
                     }
@@ -276,14 +255,14 @@ __global__ void __launch_bounds__(kThreads)
             bool ok = true, any = false;
             for (uint32_t tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
                 for (uint32_t ks = 0; ok && ks < p.k_stages; ++ks) {
-                    ok = wait_bounded(smem_u32(&control->full[stage]), phase, &control->abort_flag, p.error_word);
+                    ok = wait_bounded_suspend(smem_u32(&control->full[stage]), phase, &control->abort_flag, p.error_word);
                     if (!ok) break;
                     fence_after();
                     const uint64_t a_desc = smem_desc_sw128(smem_u32(stage_a(stage)));
                     const uint64_t w_desc = smem_desc_sw128(smem_u32(stage_w(stage)));
 #pragma unroll 1
                     for (uint32_t b = 0; b < kKB; ++b) {
-                        ok = wait_bounded(smem_u32(&control->slot_empty[slot]), slot_phase ^ 1u, &control->abort_flag,
+                        ok = wait_bounded_suspend(smem_u32(&control->slot_empty[slot]), slot_phase ^ 1u, &control->abort_flag,
                                           p.error_word);
                         if (!ok) break;
                         fence_after();
@@ -311,52 +290,79 @@ __global__ void __launch_bounds__(kThreads)
         }
         __syncwarp();
     } else {
-        // ---------------- epilogue: drain, re-seed, scale and accumulate, block by block ----------------
+        // ---------------- epilogue: drain, scale and accumulate, block by block ----------------
+        // Software pipeline over 16-column chunks (kChunks per block): while one chunk's fp32 work runs,
+        // the next chunk's tensor-memory load is in flight -- the block's second chunk, or, after it,
+        // the following block's first one (once its slot is full). Block b of a stage always lands in
+        // slot b (kSlots == kKB and every tile has whole stages), so the four blocks of a stage unroll
+        // with fixed slot addresses and scale offsets. Padding blocks need no test: their values and
+        // both scales are zero, and adding the +0 or -0 they produce leaves every sum unchanged (a sum
+        // that starts at +0 never becomes -0 under round-to-nearest).
+        static_assert(kSlots == kKB, "block b of every stage drains slot b");
         const uint32_t row_in_tile = quarter * 32u + lane;
         const uint32_t lane_base = tmem_base + ((quarter * 32u) << 16) + part * kCols;
-        uint32_t stage = 0, phase = 0, slot = 0, slot_phase = 0;
+        uint32_t stage = 0, phase = 0, slot_phase = 0;
         bool ok = true;
+        auto slot_ready = [&](uint32_t s, uint32_t parity) {
+            // every lane waits (the wait does not consume the phase); the vote keeps the warp uniform
+            const bool ready = __all_sync(0xffffffffu, wait_bounded_suspend(smem_u32(&control->slot_full[s]), parity,
+                                                                            &control->abort_flag, p.error_word));
+            fence_after();
+            return ready;
+        };
+        uint32_t ra[16], rb[16];
+        // the first block's first chunk
+        if (blockIdx.x < tiles) {
+            ok = slot_ready(0, 0);
+            if (ok) tmem_ld16(lane_base, ra);
+        }
         for (uint32_t tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x) {
             const uint32_t m = (tile % p.m_tiles) * kBM + row_in_tile;
             const uint32_t n_local = (tile / p.m_tiles) * kBN + part * kCols;  // relative to col0
+            const bool last_tile = tile + gridDim.x >= tiles;
             float acc[kCols];
 #pragma unroll
             for (int j = 0; j < kCols; ++j) acc[j] = 0.0f;
             for (uint32_t ks = 0; ok && ks < p.k_stages; ++ks) {
-                if (lane == 0) ok = wait_bounded(smem_u32(&control->full[stage]), phase, &control->abort_flag, p.error_word);
-                ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+                // this stage's scale boxes have landed
+                ok = __all_sync(0xffffffffu, wait_bounded_suspend(smem_u32(&control->full[stage]), phase,
+                                                                  &control->abort_flag, p.error_word));
                 if (!ok) break;
-                const float *da = stage_da(stage);
-                const float *dw = stage_dw(stage);
-#pragma unroll 1
-                for (uint32_t b = 0; b < kKB; ++b) {
-                    if (lane == 0)
-                        ok = wait_bounded(smem_u32(&control->slot_full[slot]), slot_phase, &control->abort_flag, p.error_word);
-                    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-                    if (!ok) break;
-                    fence_after();
-                    const uint32_t taddr = lane_base + slot * kBN;
-                    const bool real = ks * kKB + b < p.blocks;
-                    const float scale_a = da[b * kBM + row_in_tile];
+                const float *scale_a = stage_da(stage) + row_in_tile;
+                const float *scale_w = stage_dw(stage) + part * kCols;
+                const bool more = ks + 1 < p.k_stages || !last_tile;
 #pragma unroll
-                    for (int c = 0; c < kCols; c += 32) {
-                        uint32_t r[32];
-                        tmem_ld32(taddr + c, r);
-                        tmem_wait_ld(r);
-                        tmem_seed32(taddr + c);
-                        if (real) accumulate32(acc + c, r, scale_a, dw + b * kBN + part * kCols + c);
+                for (uint32_t b = 0; b < kKB; ++b) {
+                    const uint32_t taddr = lane_base + b * kBN;
+                    const float da = scale_a[b * kBM];
+#pragma unroll
+                    for (int c = 0; c < kChunks; c += 2) {
+                        const float *w = scale_w + b * kBN + 16 * c;
+                        // even chunks arrive in ra, odd ones in rb
+                        tmem_wait_ld16(ra);
+                        tmem_ld16(taddr + 16 * (c + 1), rb);
+                        accumulate16(acc + 16 * c, ra, da, w);
+                        tmem_wait_ld16(rb);
+                        if (c + 2 == kChunks) {
+                            fence_before();
+                            mbar_arrive(smem_u32(&control->slot_empty[b]));  // this thread has read the slot
+                        }
+                        if (c + 2 < kChunks) {
+                            tmem_ld16(taddr + 16 * (c + 2), ra);
+                        } else if (b + 1 < kKB) {
+                            ok = slot_ready(b + 1, slot_phase);
+                            if (ok) tmem_ld16(taddr + kBN, ra);
+                        } else if (more) {
+                            ok = slot_ready(0, slot_phase ^ 1u);
+                            if (ok) tmem_ld16(lane_base, ra);
+                        }
+                        accumulate16(acc + 16 * (c + 1), rb, da, w + 16);
                     }
-                    tmem_wait_st();
-                    fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(smem_u32(&control->slot_empty[slot]));
-                    if (++slot == kSlots) {
-                        slot = 0;
-                        slot_phase ^= 1u;
-                    }
+                    if (!ok) break;
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(&control->empty[stage]));  // done with this stage's scales
+                if (!ok) break;
+                mbar_arrive(smem_u32(&control->empty[stage]));  // done with this stage's scales
+                slot_phase ^= 1u;
                 if (++stage == kStages) {
                     stage = 0;
                     phase ^= 1u;
@@ -377,6 +383,7 @@ __global__ void __launch_bounds__(kThreads)
                 }
             }
         }
+        if (!ok) tmem_wait_ld16(ra);  // a load issued before the abort lands before tensor memory is freed
     }
 
     fence_before();

@@ -71,6 +71,36 @@ __device__ __forceinline__ bool wait_bounded_ns(uint32_t bar, uint32_t parity, v
     }
 }
 
+// try_wait that may suspend the thread for up to suspend_ns (it resumes as soon as the phase
+// completes): a waiting warp then takes no issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity, uint32_t suspend_ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity), "r"(suspend_ns)
+        : "memory");
+    return done != 0;
+}
+
+// wait_bounded_ns built on the suspending try_wait (each attempt sleeps up to 20 us at most).
+__device__ __forceinline__ bool wait_bounded_suspend(uint32_t bar, uint32_t parity, volatile int *abort_flag,
+                                                     unsigned int *error_word) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = globaltimer();
+    for (;;) {
+        if (mbar_try_wait_suspend(bar, parity, 20000u)) return true;
+        if (*abort_flag != 0) return false;
+        if (globaltimer() - start > kKernelWaitLimitNs) {
+            *abort_flag = 1;
+            atomicExch(error_word, static_cast<unsigned int>(kKernelWaitTimeout));
+            return false;
+        }
+    }
+}
+
 // The product kernels' waits: bounded by kKernelWaitLimitNs.
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, volatile int *abort_flag,
                                              unsigned int *error_word) {

@@ -161,3 +161,56 @@ def test_repack_keeps_extreme_blocks(native) -> None:  # type: ignore[no-untyped
             np.testing.assert_array_equal(out.cpu().numpy()[0], expected)
     finally:
         native.lib.qpucuda_q4_0_linear_destroy(handle)
+
+
+def non_finite_operands(rows: int, blocks: int, outputs: int, seed: int) -> tuple[np.ndarray, np.ndarray]:
+    """Random Q8_0/Q4_0 operands with fp16 scales of +inf, -inf, NaN and 65504 planted in both."""
+    rng = np.random.default_rng(seed)
+    a_scales = rng.uniform(0.001, 0.2, (rows, blocks)).astype(np.float16)
+    a_values = rng.integers(-128, 128, (rows, blocks, 32), dtype=np.int16)
+    w_scales = rng.uniform(-0.2, 0.2, (outputs, blocks)).astype(np.float16)
+    w_codes = rng.integers(0, 16, (outputs, blocks, 32), dtype=np.uint8)
+    special = (np.inf, -np.inf, np.nan, 65504.0)
+    for i, value in enumerate(special):
+        a_scales[i % rows, (3 * i + 1) % blocks] = value
+        w_scales[(5 * i + 2) % outputs, (2 * i) % blocks] = value
+    a_scales[rows - 1, blocks - 1] = np.inf
+    a_values[rows - 1, blocks - 1] = 0  # +inf times a zero dot
+    activation = oracle.pack_q8_0_blocks(a_scales.reshape(-1), a_values.reshape(-1, 32)).reshape(rows, blocks, 34)
+    weights = oracle.pack_q4_0_blocks(w_scales.reshape(-1), w_codes.reshape(-1, 32)).reshape(outputs, blocks, 18)
+    return activation, weights
+
+
+@pytest.mark.parametrize("rows", (1, 4, 5, 16, 130))
+def test_non_finite_scales(native, rows: int) -> None:  # type: ignore[no-untyped-def]
+    """Infinite and NaN block scales in either operand: the tiled MX path (rows > 4) equals the
+    reference program's arithmetic bit for bit, infinities and NaN positions included; the decode
+    matvec (rows 1-4) has the same non-finite positions and agrees elsewhere within its tolerance."""
+    import torch
+
+    outputs, blocks = 48, 12
+    activation, weights = non_finite_operands(rows, blocks, outputs, seed=9100 + rows)
+    with np.errstate(all="ignore"):
+        expected = oracle.q4_0_q8_0_linear_mx(activation, weights) if rows > 4 else oracle.q4_0_q8_0_linear(activation, weights)
+    assert np.isnan(expected).any() and (rows == 1 or np.isinf(expected).any())
+    handle = prepare(native, weights, rows)
+    try:
+        act = torch.from_numpy(activation).cuda()
+        out = torch.full((rows, outputs), 7.0, dtype=torch.float32, device="cuda")
+        native.context.set_stream(torch.cuda.current_stream().cuda_stream)
+        native.context.check(
+            native.lib.qpucuda_q4_0_linear_execute_device(handle, act.data_ptr(), rows, out.data_ptr(), outputs, 0, outputs, 0),
+            "execute_device",
+        )
+        native.sync()
+        got = out.cpu().numpy()
+    finally:
+        native.lib.qpucuda_q4_0_linear_destroy(handle)
+    if rows > 4:
+        np.testing.assert_array_equal(got, expected)
+    else:
+        np.testing.assert_array_equal(np.isnan(got), np.isnan(expected))
+        np.testing.assert_array_equal(np.isposinf(got), np.isposinf(expected))
+        np.testing.assert_array_equal(np.isneginf(got), np.isneginf(expected))
+        finite = np.isfinite(expected)
+        np.testing.assert_allclose(got[finite], expected[finite], rtol=2e-6, atol=2e-5)

@@ -85,5 +85,6 @@ def test_q4_0_kernel_source_hash_is_the_sha256_of_the_kernel_source() -> None:
     import hashlib
 
     csrc = REPO / "qpu-xla-triton_b200" / "csrc"
-    digest = hashlib.sha256((csrc / "q4_0_gemv.cu").read_bytes()).hexdigest()
+    sources = ("q4_0_gemv.cu", "q4_0_mx_sm100.cu")  # the kernels a prepared Q4_0 linear runs
+    digest = hashlib.sha256(b"".join((csrc / name).read_bytes() for name in sources)).hexdigest()
     assert _native.load().qpucuda_q4_0_kernel_source_hash().decode() == digest

@@ -181,8 +181,10 @@ qpucuda_status qpucuda_q4_0_linear_prepare(qpucuda_context *context, const qpucu
     const size_t output_bytes = static_cast<size_t>(desc->rows) * desc->resident_column_count * sizeof(float);
     const size_t mx_bytes = desc->rows > kMaxRows ? q4_0_mx_scratch_bytes(desc->rows, linear->blocks) : 0;
     // Rows > 4 on sm_100: the tcgen05 MX kernel reads the codes expanded to int8 and the scales as
-    // fp32, block-major (made once here from the repacked weights).
-    const bool mx_tcgen05 = mx_bytes != 0 && context->cc_major == 10 && context->cc_minor == 0;
+    // fp32, block-major (made once here from the repacked weights), when a call of the plan's rows
+    // over its resident columns would give it a wave of tiles.
+    const bool mx_tcgen05 = mx_bytes != 0 && context->cc_major == 10 && context->cc_minor == 0 &&
+                            q4_0_mx_sm100_fills_wave(desc->rows, desc->resident_column_count, context->sm_count);
     const size_t mx_blocks_pad = q4_0_mx_blocks_pad(linear->blocks);
     const size_t mx_value_bytes = mx_tcgen05 ? static_cast<size_t>(desc->resident_column_count) * mx_blocks_pad * 32 : 0;
     const size_t mx_scale_bytes = mx_tcgen05 ? static_cast<size_t>(desc->resident_column_count) * mx_blocks_pad * 4 : 0;

@@ -855,7 +855,8 @@ cudaError_t launch_mx(const Q40Weights &weights, const ActivationView &view, uin
     const uint32_t rows_pad = mx_rows_pad(view.rows);
     const uint32_t blocks_pad = mx_blocks_pad(weights.blocks);
     const size_t items_bytes = static_cast<size_t>(rows_pad) * blocks_pad;
-    const bool tcgen05 = weights.mx_values != nullptr && weights.mx_scales_t != nullptr;
+    const bool tcgen05 = weights.mx_values != nullptr && weights.mx_scales_t != nullptr &&
+                         q4_0_mx_sm100_fills_wave(view.rows, count, sm_count);
     MxSplitParams split{view, rows_pad, blocks_pad, reinterpret_cast<int8_t *>(scratch),
                         reinterpret_cast<int2 *>(scratch + items_bytes * 32),
                         tcgen05 ? reinterpret_cast<float *>(scratch + items_bytes * 40) : nullptr};

@@ -215,6 +215,10 @@ cudaError_t launch_q4_0_mx_sm100(const int8_t *q, const float *da_t, uint32_t ro
                                  uint32_t blocks_pad, float *destination, size_t destination_stride, uint32_t col0,
                                  uint32_t out_col0, uint32_t count, unsigned int *error_word, int sm_count,
                                  cudaStream_t stream);
+// Whether a call of `rows` rows over `count` columns gives the tcgen05 MX kernel at least one tile
+// per SM. Below that (few rows over a narrow window) each tile's block-serial K loop is the whole
+// runtime, and the mma.sync kernel's smaller tiles spread the work over more SMs.
+bool q4_0_mx_sm100_fills_wave(uint32_t rows, uint32_t count, int sm_count);
 inline uint32_t q4_0_scale_stride(uint32_t blocks) { return (blocks + 7u) & ~7u; }
 // activation: native Q8_0 rows [rows][blocks][34] (interleave 0) or CPU_REPACK
 // block_q8_0x4 groups (interleave 4/8). Writes destination[r * stride + out_col0 + j]

@@ -297,6 +297,11 @@ def test_decode_full_size_columns_sample(native, shape) -> None:  # type: ignore
         (100, 5632, 2048, 512, 1024),  # ragged rows, a column window
         (300, 8192, 384, 128, 256),  # several row tiles, a partial column tile
         (1000, 4096, 528, 16, 512),  # 8 row tiles of 128 (ragged last), 4 column tiles from column 16
+        # calls that give the tcgen05 kernel a tile per SM (fewer go to the mma.sync kernel)
+        (16, 1024, 19200, 0, 19200),  # 16-row tiles (two CTAs per SM)
+        (30, 1024, 19456, 256, 19200),  # 32-row tiles, ragged rows, a column window
+        (64, 2048, 19200, 0, 19200),  # 64-row tiles
+        (300, 1056, 9600, 0, 9600),  # 128-row tiles, ragged rows, 33 blocks: a partial last K stage
     ],
 )
 def test_mx_rows_match_the_reference_program(native, rows: int, k: int, n: int, start: int, count: int) -> None:  # type: ignore[no-untyped-def]

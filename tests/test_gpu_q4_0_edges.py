@@ -181,14 +181,15 @@ def non_finite_operands(rows: int, blocks: int, outputs: int, seed: int) -> tupl
     return activation, weights
 
 
-@pytest.mark.parametrize("rows", (1, 4, 5, 16, 130))
-def test_non_finite_scales(native, rows: int) -> None:  # type: ignore[no-untyped-def]
+@pytest.mark.parametrize("rows,outputs", [(1, 48), (4, 48), (5, 48), (16, 48), (130, 48), (16, 19200), (130, 9600)])
+def test_non_finite_scales(native, rows: int, outputs: int) -> None:  # type: ignore[no-untyped-def]
     """Infinite and NaN block scales in either operand: the tiled MX path (rows > 4) equals the
     reference program's arithmetic bit for bit, infinities and NaN positions included; the decode
-    matvec (rows 1-4) has the same non-finite positions and agrees elsewhere within its tolerance."""
+    matvec (rows 1-4) has the same non-finite positions and agrees elsewhere within its tolerance.
+    The wide cases give the tcgen05 MX kernel a tile per SM; the narrow ones run the mma.sync kernel."""
     import torch
 
-    outputs, blocks = 48, 12
+    blocks = 12
     activation, weights = non_finite_operands(rows, blocks, outputs, seed=9100 + rows)
     with np.errstate(all="ignore"):
         expected = oracle.q4_0_q8_0_linear_mx(activation, weights) if rows > 4 else oracle.q4_0_q8_0_linear(activation, weights)

@@ -1,16 +1,19 @@
-// Small-M W8A8 kernels (HBM-bound on the weight, no tensor cores).
+// Small-M W8A8 kernels (HBM-bound on the weight).
 //
 //  * w8a8_gemv: acc[m, n] = sum_k a[m, k] * w[n, k] for m <= 8 rows, exact int32.
 //    Replaces vc7.w8a8_gemv (src/qpu_xla/kernels/gemv_int8.py:20-153), which the
 //    reference selects for batch == 1 (src/qpu_xla/models/tinyllama/quantization.py:184).
-//    One warp, or SPLIT warps of a CTA over disjoint K ranges, per output column n;
-//    each lane streams 16-byte chunks of the weight row (a warp reads 512
-//    contiguous bytes per step), multiplies them with four dp4a per activation
-//    row, the warp reduces with shuffles and split warps add through shared
-//    memory. Integer addition is associative, so the int32 result is exact in any
-//    order, and the fused epilogue is the same ((float)acc * s_a) * s_w (+ bias)
-//    as the GEMM. The grid is persistent, sized from the occupancy API with every
-//    column slot running the same number of rounds.
+//    - One row (w8a8_gemv_kernel): one warp, or SPLIT warps of a CTA over disjoint K
+//      ranges, per output column n; each lane streams 16-byte chunks of the weight row (a
+//      warp reads 512 contiguous bytes per step) into dp4a, the warp reduces with shuffles
+//      and split warps add through shared memory.
+//    - Two to eight rows (w8a8_gemv_mma_kernel): mma.sync m16n8k32 over 16-column groups,
+//      so the weight bytes are read once however many rows there are (dp4a would issue four
+//      instructions per row per 16 bytes and re-read the activation chunks per row).
+//    Integer addition is associative, so the int32 result is exact in any order, and the
+//    fused epilogue is the same ((float)acc * s_a) * s_w (+ bias) as the GEMM. The grids
+//    are persistent, sized from the occupancy API with every CTA running the same number
+//    of rounds.
 //  * w8a8_dequantize: the standalone vc7.w8a8_dequantize epilogue
 //    (src/qpu_xla/kernels/w8a8_epilogue.py:20-96), elementwise.
 #include <atomic>
@@ -162,6 +165,90 @@ __global__ void __launch_bounds__(kGemvThreads) w8a8_gemv_kernel(const GemvParam
     }
 }
 
+// ---- tensor-core GEMV (M <= 8) ------------------------------------------------------------
+// D[16 weight columns][8 rows] += W[16][32] x A[32][8] with mma.sync m16n8k32 (s8 x s8 -> s32),
+// the weights as the A operand and the activation rows as B (rows >= m are zero). The K order
+// inside an MMA may be any permutation applied to both operands (the dot is a sum), so every lane
+// reads whole 16-byte chunks: over a 64-byte K segment, lane (g, t) loads bytes 16t..16t+15 of
+// weight columns g and g + 8 and of activation row g; words x, y feed one MMA (as its k = 4t..
+// and 16 + 4t.. fragments) and words z, w a second. Each weight byte is loaded once, with no
+// per-row re-reads, so the kernel streams the weights instead of issuing 4 dp4a per row and
+// 16 bytes. The 8 warps of a CTA take disjoint K slices of the same 16 columns and add their
+// int32 partial sums through shared memory (exact in any order); the epilogue is the same
+// ((float)acc * s_a) * s_w (+ bias) as the GEMM.
+constexpr int kMmaSegments = 4;  // 64-byte K segments loaded per lane before its MMAs
+
+__device__ __forceinline__ void mma_s8_acc(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1,
+                                           int (&d)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(kGemvThreads) w8a8_gemv_mma_kernel(const GemvParams p) {
+    __shared__ int partial[kGemvWarps][128];
+    const uint32_t warp = threadIdx.x >> 5;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint32_t g = lane >> 2;  // weight columns g and g + 8; activation row g
+    const uint32_t t = lane & 3;   // 16-byte chunk t of each 64-byte segment
+    const uint32_t segments = (p.k + 63) / 64;
+    const uint32_t per_warp = (segments + kGemvWarps - 1) / kGemvWarps;
+    const uint32_t s_begin = min(segments, warp * per_warp);
+    const uint32_t s_end = min(segments, s_begin + per_warp);
+    const uint32_t groups = (p.n + 15) / 16;
+    const bool row_live = g < p.m;
+    const int8_t *a_row = p.a + static_cast<size_t>(row_live ? g : 0) * p.a_stride;
+
+    for (uint32_t group = blockIdx.x; group < groups; group += gridDim.x) {
+        const uint32_t n0 = group * 16;
+        const bool live0 = n0 + g < p.n, live1 = n0 + g + 8 < p.n;
+        const int8_t *w0 = p.w + static_cast<size_t>(live0 ? n0 + g : 0) * p.w_stride;
+        const int8_t *w1 = p.w + static_cast<size_t>(live1 ? n0 + g + 8 : 0) * p.w_stride;
+        int d[4] = {0, 0, 0, 0};
+        for (uint32_t s = s_begin; s < s_end; s += kMmaSegments) {
+            uint4 wa[kMmaSegments], wb[kMmaSegments], av[kMmaSegments];
+#pragma unroll
+            for (int u = 0; u < kMmaSegments; ++u) {
+                const uint32_t byte = (s + u) * 64 + t * 16;
+                const bool in = s + u < s_end && byte < p.k;
+                wa[u] = in && live0 ? load_weight_chunk(w0 + byte) : make_uint4(0, 0, 0, 0);
+                wb[u] = in && live1 ? load_weight_chunk(w1 + byte) : make_uint4(0, 0, 0, 0);
+                av[u] = in && row_live ? __ldg(reinterpret_cast<const uint4 *>(a_row + byte)) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < kMmaSegments; ++u) {
+                mma_s8_acc(wa[u].x, wb[u].x, wa[u].y, wb[u].y, av[u].x, av[u].y, d);
+                mma_s8_acc(wa[u].z, wb[u].z, wa[u].w, wb[u].w, av[u].z, av[u].w, d);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) partial[warp][lane * 4 + i] = d[i];
+        __syncthreads();
+        if (threadIdx.x < 128) {
+            // output x: lane x / 4 of every warp holds it in register x % 4
+            const uint32_t x = threadIdx.x;
+            const uint32_t col = n0 + ((x >> 2) >> 2) + 8 * ((x & 3) >> 1);
+            const uint32_t row = 2 * ((x >> 2) & 3) + (x & 1);
+            int value = 0;
+#pragma unroll
+            for (int w = 0; w < kGemvWarps; ++w) value += partial[w][x];
+            if (row < p.m && col < p.n) {
+                const size_t index = static_cast<size_t>(row) * p.out_stride + col;
+                if (p.mode == static_cast<int>(EpilogueMode::kStoreS32)) {
+                    static_cast<int32_t *>(p.out)[index] = value;
+                } else {
+                    float v = dequant_value(value, p.row_scales[row], p.col_scales[col]);
+                    if (p.mode == static_cast<int>(EpilogueMode::kDequantizeBias)) v = __fadd_rn(v, p.bias[col]);
+                    static_cast<float *>(p.out)[index] = v;
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
 __global__ void __launch_bounds__(256) w8a8_dequantize_kernel(const int32_t *__restrict__ acc, size_t acc_stride,
                                                               uint32_t m, uint32_t n, int mode,
                                                               const float *__restrict__ row_scales,
@@ -245,6 +332,32 @@ cudaError_t launch_rows(const GemvParams &p, int sm_count, cudaStream_t stream) 
     return cudaGetLastError();
 }
 
+int mma_resident_ctas() {
+    static std::atomic<int> cached[64] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return 1;
+    const int known = cached[device].load(std::memory_order_relaxed);
+    if (known > 0) return known;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, w8a8_gemv_mma_kernel, kGemvThreads, 0) != cudaSuccess ||
+        per_sm < 1) {
+        (void)cudaGetLastError();
+        return 1;
+    }
+    cached[device].store(per_sm, std::memory_order_relaxed);
+    return per_sm;
+}
+
+// Persistent grid with every CTA running the same number of 16-column groups.
+cudaError_t launch_mma(const GemvParams &p, int sm_count, cudaStream_t stream) {
+    const uint64_t groups = (p.n + 15) / 16;
+    const uint64_t capacity = static_cast<uint64_t>(sm_count) * static_cast<uint64_t>(mma_resident_ctas());
+    const uint64_t rounds = (groups + capacity - 1) / capacity;
+    const uint32_t grid = static_cast<uint32_t>((groups + rounds - 1) / rounds);
+    w8a8_gemv_mma_kernel<<<grid, kGemvThreads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
 template <int ROWS>
 cudaError_t preload_rows() {
     cudaFuncAttributes attributes;
@@ -262,10 +375,10 @@ cudaError_t preload_rows() {
 }  // namespace
 
 cudaError_t preload_w8a8_gemv() {
-    cudaError_t error = preload_rows<1>();
-    if (error == cudaSuccess) error = preload_rows<2>();
-    if (error == cudaSuccess) error = preload_rows<4>();
-    if (error == cudaSuccess) error = preload_rows<8>();
+    cudaFuncAttributes attributes;
+    cudaError_t error = cudaFuncGetAttributes(&attributes, w8a8_gemv_mma_kernel);
+    (void)mma_resident_ctas();
+    if (error == cudaSuccess) error = preload_rows<1>();
     return error;
 }
 
@@ -291,13 +404,13 @@ cudaError_t launch_w8a8_gemv(const int8_t *a, size_t a_stride, const int8_t *w, 
     p.bias = epilogue.bias;
     p.out = epilogue.out;
     p.out_stride = epilogue.out_stride;
-    switch (m) {
-        case 1: return launch_rows<1>(p, sm_count, stream);
-        case 2: return launch_rows<2>(p, sm_count, stream);
-        case 3:
-        case 4: return launch_rows<4>(p, sm_count, stream);
-        default: return launch_rows<8>(p, sm_count, stream);
-    }
+    // One row streams the weights best with dp4a and the cross-column prefetch; two or more rows
+    // go to the tensor-core kernel, whose time does not grow with the rows. Measured on B200
+    // (prepared plan, row quantizer included, L2 flushed): 70B gate 8192 -> 28672 at M = 1 50.2 us
+    // (dp4a) against 52.4 (MMA); at M = 4 68.6 against 54.2, at M = 8 103.5 against 54.3; 70B down
+    // 28672 -> 8192 at M = 8 140.3 against 52.2.
+    if (m == 1) return launch_rows<1>(p, sm_count, stream);
+    return launch_mma(p, sm_count, stream);
 }
 
 cudaError_t launch_w8a8_dequantize(const int32_t *acc, size_t acc_stride, uint32_t m, uint32_t n,

@@ -162,12 +162,12 @@ def test_standalone_dequantize_matches_epilogue(native) -> None:  # type: ignore
     np.testing.assert_array_equal(out, oracle.w8a8_dequantize(acc, row_scales, col_scales, bias))
 
 
-@pytest.mark.parametrize("k,n", [(16, 16), (512, 512), (1536, 512), (28672, 8192), (28672, 1024), (28672, 256), (4112, 16)])
-@pytest.mark.parametrize("m", [1, 3, 8])
+@pytest.mark.parametrize("k,n", [(16, 16), (512, 512), (1536, 512), (28672, 8192), (28672, 1024), (28672, 256), (4112, 16), (1040, 1000)])
+@pytest.mark.parametrize("m", [1, 3, 5, 8])
 def test_gemv_is_exact(native, m: int, k: int, n: int) -> None:  # type: ignore[no-untyped-def]
     """tests/test_qpu_xla_gemv_int8.py:13-33 shapes, plus M = 3, 8, the 70B down projection and
-    narrower long-K matrices (its 8-GPU column shard and below), which spread each column over
-    2, 4 or 8 warps; K = 4112 leaves the last warp's K range ragged."""
+    narrower long-K matrices (its 8-GPU column shard and below); K = 4112 and 1040 leave the last
+    K slice ragged, N = 1000 a partial 16-column group."""
     from gpu_helpers import padded_int8, to_cuda
 
     rng = np.random.default_rng(190 + k + m)

@@ -65,6 +65,9 @@ SEED = 4
 L2_FLUSH_BYTES = 256 << 20
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 OBJECTS = ("square", "tinyllama_w8a8", "tinyllama_q4_0", "llama7b_ffn", "q4_0_mx")
+FP32_LANES = 148 * 128  # B200: SMs x fp32 lanes per SM
+SM_MAX_MHZ = 1965.0
+NVLINK_PEER_GBS = 770.0  # measured peer copy per direction per GPU on this pool's B200s
 Q4_0_COPIES = 16  # distinct TinyLlama weight copies streamed per bracket (16 x 6.5 MB)
 
 
@@ -491,6 +494,9 @@ def run_ours(args: argparse.Namespace) -> None:
             "note": "kernel = quantize + GEMM on the rank's column shard alone; exchange = the step's extra time "
             "over that (the fused epilogue overlaps the peer stores with the GEMM, so this is the exposed part)",
         }
+    # Roofline of the fused GEMM + all-gather: the step cannot beat the slower of the rank's GEMM
+    # work at the int8 peak and the fp32 outputs every rank must receive over NVLink (peer-copy
+    # bandwidth measured on this pool, per direction per GPU); filled in below once the peak is known.
     rank_gemm_ops = sum(2.0 * TOKENS * p["gather"].count * p["k"] for p in projections)
     gemm_seconds = sum(gemm_ms) * 1e-3
     achieved_tops = rank_gemm_ops / gemm_seconds / 1e12 if gemm_seconds > 0 else 0.0
@@ -511,6 +517,19 @@ def run_ours(args: argparse.Namespace) -> None:
     library_tops = max_over_ranks(rank_gemm_ops / (sum(library_ms) * 1e-3) / 1e12)
     bf16_doubled = 2.0 * peaks["bf16_tflops"]
     int8_peak = max(bf16_doubled, library_tops)
+    if multi_gpu is not None:
+        compute_ms = rank_gemm_ops / (int8_peak * 1e12) * 1e3
+        link_ms = multi_gpu["received_bytes_per_rank_step"] / (NVLINK_PEER_GBS * 1e9) * 1e3
+        target_ms = max(compute_ms, link_ms)
+        multi_gpu["roofline"] = {
+            "bound": "nvlink" if link_ms >= compute_ms else "tensor",
+            "target_ms_per_step": round(target_ms, 4),
+            "compute_ms_at_peak": round(compute_ms, 4),
+            "receive_ms_at_link": round(link_ms, 4),
+            "link_gbs": NVLINK_PEER_GBS,
+            "link_source": "peer copy per direction per GPU measured on this pool (nominal NVLink 5: 900 GB/s)",
+            "frac": round(target_ms / step_ms, 4),
+        }
     int8_note = (f"the larger of cuBLASLt int8 (torch._int_mm) measured live on the 70B FFN shapes ({library_tops:.1f} TOPS) "
                  f"and 2 x {peak_kind} cuBLAS bf16 burst ({bf16_doubled:.1f} TOPS)")
     hbm_note = f"{peak_kind} STREAM-style copy"
@@ -930,12 +949,20 @@ def object_q4_0_mx(bench: Bench, int8_peak: float, hbm_peak: float, int8_note: s
         finally:
             plan.close()
         ops = 2.0 * rows * n * k
+        # The fp32 side: 4 roundings per (row, column, block) on 148 SMs x 128 fp32 lanes at the
+        # maximum SM clock, expressed in the metric's int ops (2 x 32 per (row, column, block)).
+        fp32_bound_tops = FP32_LANES * SM_MAX_MHZ * 1e6 / 4.0 * 64.0 / 1e12
         result["shapes"][f"{name} {k}->{n}"] = {
             "tops": round(ops / (ms * 1e-3) / 1e12, 1),
             "ms_per_call": round(ms, 4),
             "roofline": roofline(kernel="activation split + q4_0_mx_sm100_kernel (tcgen05 kind::i8, one MMA per block)",
                                  seconds=ms * 1e-3, ops=ops, nbytes=0.0, int8_peak=int8_peak, hbm_peak=hbm_peak,
                                  peak_note=int8_note, traffic=None),
+            "fp32_scaling_bound": {
+                "tops": round(fp32_bound_tops, 1),
+                "frac": round(ops / (ms * 1e-3) / 1e12 / fp32_bound_tops, 4),
+                "source": "nominal: 148 SMs x 128 fp32 lanes x the maximum SM clock, 4 fp32 roundings per (row, column, block)",
+            },
         }
         del act, out
     result["value"] = next(iter(result["shapes"].values()))["tops"]

@@ -77,6 +77,12 @@ __global__ void __launch_bounds__(THREADS) quantize_rows_int8_vec(const float *_
                                                                   float *__restrict__ scales) {
     __shared__ float scratch[32];
     const uint32_t vectors = cols / 4;
+    // Launched as a programmatic dependent of the previous kernel on the stream: wait for it
+    // (its writes may be this kernel's source, or it may still read this kernel's destination)
+    // before touching memory, then let the next kernel (the GEMV that reads these rows) launch
+    // and start streaming its weights while the rows are quantized.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     for (uint32_t row = blockIdx.x; row < rows; row += gridDim.x) {
         const float4 *source = reinterpret_cast<const float4 *>(x + static_cast<size_t>(row) * x_stride);
         float4 cache[VEC];
@@ -209,9 +215,17 @@ template <int THREADS, int VEC>
 cudaError_t launch_vec(const float *x, size_t x_stride, uint32_t rows, uint32_t cols, uint32_t padded_cols, int8_t *q,
                        size_t q_stride, float *scales, cudaStream_t stream) {
     const uint32_t grid = rows < 65535u * 4u ? rows : 65535u * 4u;
-    quantize_rows_int8_vec<THREADS, VEC><<<grid, THREADS, 0, stream>>>(x, x_stride, rows, cols, padded_cols, q,
-                                                                        q_stride, scales);
-    return cudaGetLastError();
+    cudaLaunchAttribute attribute{};
+    attribute.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute.val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(grid);
+    config.blockDim = dim3(THREADS);
+    config.stream = stream;
+    config.attrs = &attribute;
+    config.numAttrs = 1;
+    return cudaLaunchKernelEx(&config, quantize_rows_int8_vec<THREADS, VEC>, x, x_stride, rows, cols, padded_cols, q,
+                              q_stride, scales);
 }
 
 // Layout path: one thread per row; consecutive threads take consecutive rows, so for NCHW

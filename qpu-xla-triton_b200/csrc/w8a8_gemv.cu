@@ -80,7 +80,6 @@ __global__ void __launch_bounds__(kGemvThreads) w8a8_gemv_kernel(const GemvParam
     // Whether a lane's K range starts with a whole four-load trip (the same for every column).
     const bool first_wide = c_first + 96 < c_end;
     const bool writer = lane < static_cast<uint32_t>(ROWS) && lane < p.m;
-    const float row_scale = writer && p.mode != static_cast<int>(EpilogueMode::kStoreS32) ? p.row_scales[lane] : 0.0f;
     uint4 wv[4];
     auto load_trip = [&](uint32_t column, uint32_t c) {
         const int8_t *row = p.w + static_cast<size_t>(column) * p.w_stride;
@@ -89,6 +88,12 @@ __global__ void __launch_bounds__(kGemvThreads) w8a8_gemv_kernel(const GemvParam
     };
     uint32_t n = blockIdx.x * kSlots + slot;
     if (kPrefetch && n < p.n && first_wide) load_trip(n, c_first);
+    // Programmatic dependent launch: the weights are immutable, so the first trip above is issued
+    // while the previous kernel (the row quantizer) may still run; the activation rows and their
+    // scales are its output and are read only after the wait.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const float row_scale = writer && p.mode != static_cast<int>(EpilogueMode::kStoreS32) ? p.row_scales[lane] : 0.0f;
     for (; n < p.n; n += stride) {
         const int8_t *w_row = p.w + static_cast<size_t>(n) * p.w_stride;
         // The epilogue's per-column operands, loaded now so they arrive with the weights.
@@ -187,7 +192,7 @@ __device__ __forceinline__ void mma_s8_acc(uint32_t a0, uint32_t a1, uint32_t a2
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__global__ void __launch_bounds__(kGemvThreads) w8a8_gemv_mma_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(kGemvThreads, 4) w8a8_gemv_mma_kernel(const GemvParams p) {
     __shared__ int partial[kGemvWarps][128];
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
@@ -200,6 +205,29 @@ __global__ void __launch_bounds__(kGemvThreads) w8a8_gemv_mma_kernel(const GemvP
     const uint32_t groups = (p.n + 15) / 16;
     const bool row_live = g < p.m;
     const int8_t *a_row = p.a + static_cast<size_t>(row_live ? g : 0) * p.a_stride;
+    uint4 wa[kMmaSegments], wb[kMmaSegments];
+    auto load_weights = [&](const int8_t *w0, const int8_t *w1, bool live0, bool live1, uint32_t s) {
+#pragma unroll
+        for (int u = 0; u < kMmaSegments; ++u) {
+            const uint32_t byte = (s + u) * 64 + t * 16;
+            const bool in = s + u < s_end && byte < p.k;
+            wa[u] = in && live0 ? load_weight_chunk(w0 + byte) : make_uint4(0, 0, 0, 0);
+            wb[u] = in && live1 ? load_weight_chunk(w1 + byte) : make_uint4(0, 0, 0, 0);
+        }
+    };
+    // Programmatic dependent launch: the first group's first weight loads are issued while the
+    // previous kernel (the row quantizer) may still run; the activation rows and scales are read
+    // only after the wait.
+    bool primed = false;
+    if (blockIdx.x < groups && s_begin < s_end) {
+        const uint32_t n0 = blockIdx.x * 16;
+        load_weights(p.w + static_cast<size_t>(n0 + g < p.n ? n0 + g : 0) * p.w_stride,
+                     p.w + static_cast<size_t>(n0 + g + 8 < p.n ? n0 + g + 8 : 0) * p.w_stride, n0 + g < p.n,
+                     n0 + g + 8 < p.n, s_begin);
+        primed = true;
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     for (uint32_t group = blockIdx.x; group < groups; group += gridDim.x) {
         const uint32_t n0 = group * 16;
@@ -208,13 +236,13 @@ __global__ void __launch_bounds__(kGemvThreads) w8a8_gemv_mma_kernel(const GemvP
         const int8_t *w1 = p.w + static_cast<size_t>(live1 ? n0 + g + 8 : 0) * p.w_stride;
         int d[4] = {0, 0, 0, 0};
         for (uint32_t s = s_begin; s < s_end; s += kMmaSegments) {
-            uint4 wa[kMmaSegments], wb[kMmaSegments], av[kMmaSegments];
+            uint4 av[kMmaSegments];
+            if (!primed) load_weights(w0, w1, live0, live1, s);
+            primed = false;
 #pragma unroll
             for (int u = 0; u < kMmaSegments; ++u) {
                 const uint32_t byte = (s + u) * 64 + t * 16;
                 const bool in = s + u < s_end && byte < p.k;
-                wa[u] = in && live0 ? load_weight_chunk(w0 + byte) : make_uint4(0, 0, 0, 0);
-                wb[u] = in && live1 ? load_weight_chunk(w1 + byte) : make_uint4(0, 0, 0, 0);
                 av[u] = in && row_live ? __ldg(reinterpret_cast<const uint4 *>(a_row + byte)) : make_uint4(0, 0, 0, 0);
             }
 #pragma unroll
@@ -264,6 +292,21 @@ __global__ void __launch_bounds__(256) w8a8_dequantize_kernel(const int32_t *__r
         if (mode == static_cast<int>(EpilogueMode::kDequantizeBias)) v = __fadd_rn(v, bias[col]);
         out[row * out_stride + col] = v;
     }
+}
+
+// A launch that may begin while the previous kernel on the stream finishes (programmatic stream
+// serialization); the kernel's griddepcontrol.wait orders its reads of that kernel's output.
+cudaError_t launch_dependent(void (*kernel)(GemvParams), uint32_t grid, const GemvParams &p, cudaStream_t stream) {
+    cudaLaunchAttribute attribute{};
+    attribute.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute.val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(grid);
+    config.blockDim = dim3(kGemvThreads);
+    config.stream = stream;
+    config.attrs = &attribute;
+    config.numAttrs = 1;
+    return cudaLaunchKernelEx(&config, kernel, p);
 }
 
 // CTAs of one instantiation resident per SM, from the occupancy API, cached per device.
@@ -324,12 +367,11 @@ cudaError_t launch_rows(const GemvParams &p, int sm_count, cudaStream_t stream) 
     }
     const uint32_t grid = shapes[choice].grid;
     switch (choice) {
-        case 0: w8a8_gemv_kernel<ROWS, 1><<<grid, kGemvThreads, 0, stream>>>(p); break;
-        case 1: w8a8_gemv_kernel<ROWS, 2><<<grid, kGemvThreads, 0, stream>>>(p); break;
-        case 2: w8a8_gemv_kernel<ROWS, 4><<<grid, kGemvThreads, 0, stream>>>(p); break;
-        default: w8a8_gemv_kernel<ROWS, 8><<<grid, kGemvThreads, 0, stream>>>(p); break;
+        case 0: return launch_dependent(w8a8_gemv_kernel<ROWS, 1>, grid, p, stream);
+        case 1: return launch_dependent(w8a8_gemv_kernel<ROWS, 2>, grid, p, stream);
+        case 2: return launch_dependent(w8a8_gemv_kernel<ROWS, 4>, grid, p, stream);
+        default: return launch_dependent(w8a8_gemv_kernel<ROWS, 8>, grid, p, stream);
     }
-    return cudaGetLastError();
 }
 
 int mma_resident_ctas() {
@@ -354,8 +396,7 @@ cudaError_t launch_mma(const GemvParams &p, int sm_count, cudaStream_t stream) {
     const uint64_t capacity = static_cast<uint64_t>(sm_count) * static_cast<uint64_t>(mma_resident_ctas());
     const uint64_t rounds = (groups + capacity - 1) / capacity;
     const uint32_t grid = static_cast<uint32_t>((groups + rounds - 1) / rounds);
-    w8a8_gemv_mma_kernel<<<grid, kGemvThreads, 0, stream>>>(p);
-    return cudaGetLastError();
+    return launch_dependent(w8a8_gemv_mma_kernel, grid, p, stream);
 }
 
 template <int ROWS>

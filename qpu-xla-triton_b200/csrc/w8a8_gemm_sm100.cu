@@ -410,6 +410,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any remote arrive or copy
     tc_fence_after();
     const uint32_t tmem_base = control->tmem_base;
+    // Programmatic dependent launch: the set-up above (barriers, tensor memory) overlaps the end of
+    // the previous kernel on the stream (the row quantizer, whose output this kernel reads); every
+    // global read and write below comes after the wait. The next kernel may launch at once: it
+    // waits for this grid in turn before touching memory.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -792,11 +798,19 @@ int resident_pairs(int sm_count) {
 template <bool FANOUT, bool PAIR>
 cudaError_t launch_kernel(uint32_t tiles, int sm_count, const CUtensorMap *map_a, const CUtensorMap *map_w,
                           const CUtensorMap *map_out, const GemmParams &params, cudaStream_t stream) {
+    cudaLaunchAttribute attributes[2] = {};
+    attributes[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attributes[0].val.programmaticStreamSerializationAllowed = 1;
     if constexpr (!PAIR) {
         const uint32_t grid = tiles < static_cast<uint32_t>(sm_count) ? tiles : static_cast<uint32_t>(sm_count);
-        w8a8_gemm_sm100_kernel<FANOUT, false>
-            <<<grid, NUM_THREADS, smem_bytes<false>(), stream>>>(*map_a, *map_w, *map_out, params);
-        return cudaGetLastError();
+        cudaLaunchConfig_t config = {};
+        config.gridDim = dim3(grid, 1, 1);
+        config.blockDim = dim3(NUM_THREADS, 1, 1);
+        config.dynamicSmemBytes = smem_bytes<false>();
+        config.stream = stream;
+        config.attrs = attributes;
+        config.numAttrs = 1;
+        return cudaLaunchKernelEx(&config, w8a8_gemm_sm100_kernel<FANOUT, false>, *map_a, *map_w, *map_out, params);
     } else {
         const uint32_t pairs = static_cast<uint32_t>(resident_pairs(sm_count));
         const uint32_t clusters = tiles < pairs ? tiles : pairs;
@@ -805,13 +819,12 @@ cudaError_t launch_kernel(uint32_t tiles, int sm_count, const CUtensorMap *map_a
         config.blockDim = dim3(NUM_THREADS, 1, 1);
         config.dynamicSmemBytes = smem_bytes<true>();
         config.stream = stream;
-        cudaLaunchAttribute attribute;
-        attribute.id = cudaLaunchAttributeClusterDimension;
-        attribute.val.clusterDim.x = 2;
-        attribute.val.clusterDim.y = 1;
-        attribute.val.clusterDim.z = 1;
-        config.attrs = &attribute;
-        config.numAttrs = 1;
+        attributes[1].id = cudaLaunchAttributeClusterDimension;
+        attributes[1].val.clusterDim.x = 2;
+        attributes[1].val.clusterDim.y = 1;
+        attributes[1].val.clusterDim.z = 1;
+        config.attrs = attributes;
+        config.numAttrs = 2;
         return cudaLaunchKernelEx(&config, w8a8_gemm_sm100_kernel<FANOUT, true>, *map_a, *map_w, *map_out, params);
     }
 }

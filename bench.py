@@ -401,6 +401,7 @@ def run_ours(args: argparse.Namespace) -> None:
         })
         del weight, quantized, q4_blocks
     exchange = "none"
+    copy_streams: list[Any] = []
     if world > 1 and args.exchange == "nccl":
         exchange = "NCCL all-gather after the GEMM (selected with --exchange nccl)"
         barrier_flag = None
@@ -408,14 +409,20 @@ def run_ours(args: argparse.Namespace) -> None:
         from qpu_xla.sharded import PeerOutput
 
         exchange = "fused GEMM epilogue stores into every rank's output (CUDA IPC over NVLink) + one NCCL all-reduce per step"
+        if args.exchange == "copy":
+            exchange = ("GEMM into the local output, then copy-engine pushes of each projection's column block to every "
+                        "peer (one stream per peer, overlapping the next projection) + one NCCL all-reduce per step")
+            copy_streams = [torch.cuda.Stream(cuda) for _ in range(world - 1)]
         try:
             for p in projections:
                 p["peer"] = PeerOutput(device, TOKENS, p["n"])
+                p["written"] = torch.cuda.Event()
         except Exception as error:  # noqa: BLE001 - the mapping refusal is reported, not hidden
             for p in projections:
                 if "peer" in p:
                     p.pop("peer").close()
             exchange = f"NCCL all-gather after the GEMM (peer mapping refused: {str(error)[:120]})"
+            copy_streams.clear()
         barrier_flag = torch.zeros(1, dtype=torch.float32, device=cuda)
     torch.cuda.empty_cache()
 
@@ -425,7 +432,14 @@ def run_ours(args: argparse.Namespace) -> None:
             g = p["gather"]
             if "peer" in p:
                 destination, peers = p["peer"].slice_pointers(g.start)
-                p["plan"].forward_fanout(p["source"], destination, peers, p["n"])
+                if copy_streams:
+                    p["plan"].forward_fanout(p["source"], destination, [], p["n"])
+                    p["written"].record(stream)
+                    for side in copy_streams:
+                        side.wait_event(p["written"])
+                    p["peer"].push_columns(g.start, g.count, copy_streams)
+                else:
+                    p["plan"].forward_fanout(p["source"], destination, peers, p["n"])
                 fused = True
                 continue
             p["step"].quantize()
@@ -433,6 +447,8 @@ def run_ours(args: argparse.Namespace) -> None:
             if world > 1:
                 g.gather(p["local"], out=p["full"])
         if fused:
+            for side in copy_streams:
+                stream.wait_stream(side)
             dist.all_reduce(barrier_flag)  # every rank's peer stores of this step are done
 
     def barrier() -> None:
@@ -957,7 +973,8 @@ def object_q4_0_mx(bench: Bench, int8_peak: float, hbm_peak: float, int8_note: s
             "ms_per_call": round(ms, 4),
             "roofline": roofline(kernel="activation split + q4_0_mx_sm100_kernel (tcgen05 kind::i8, one MMA per block)",
                                  seconds=ms * 1e-3, ops=ops, nbytes=0.0, int8_peak=int8_peak, hbm_peak=hbm_peak,
-                                 peak_note=int8_note, traffic=None),
+                                 peak_note=int8_note,
+                                 traffic=profile_traffic("q4_0_mx_sm100_70b_gate_m4096") if name == "gate_proj" else None),
             "fp32_scaling_bound": {
                 "tops": round(fp32_bound_tops, 1),
                 "frac": round(ops / (ms * 1e-3) / 1e12 / fp32_bound_tops, 4),
@@ -1251,9 +1268,9 @@ def main() -> None:
                         help=f"comma-separated subset of {','.join(OBJECTS)} to time at N = 1 (default all; empty string: none)")
     parser.add_argument(
         "--exchange",
-        choices=("fused", "nccl"),
+        choices=("fused", "copy", "nccl"),
         default="fused",
-        help="N > 1: fused GEMM + all-gather over NVLink (default) or NCCL all-gather after the GEMM",
+        help="N > 1: fused GEMM + all-gather over NVLink (default), copy-engine pushes after each GEMM, or NCCL all-gather after the GEMM",
     )
     args = parser.parse_args()
     if args.warmup < 3:

@@ -66,6 +66,20 @@ qpucuda_status qpucuda_w8a8_linear_execute_device_fanout(qpucuda_w8a8_linear *li
                                                          float *const *peer_destinations, uint32_t peer_count,
                                                          size_t destination_stride);
 
+/* Copies a block of `rows` rows of `width_bytes` bytes from `source` (rows
+ * `source_pitch` bytes apart) to `destination` (rows `destination_pitch` bytes
+ * apart) with the copy engines, asynchronously on `stream` (a cudaStream_t of the
+ * context's device; NULL for the context stream). With `destination` a mapped
+ * peer buffer (qpucuda_peer_buffer_open) this pushes a column block of this
+ * rank's output to another rank over NVLink without occupying the SMs: the
+ * exchange of the N-split done by DMA instead of by the GEMM epilogue's stores.
+ * No counterpart in the reference (its output split joins in host memory).
+ * QPUCUDA_INVALID_ARGUMENT for NULL pointers, a zero size or pitches below the
+ * width. */
+qpucuda_status qpucuda_peer_copy_rows(qpucuda_context *context, void *destination, size_t destination_pitch,
+                                      const void *source, size_t source_pitch, size_t width_bytes, size_t rows,
+                                      void *stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

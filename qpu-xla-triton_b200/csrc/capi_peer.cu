@@ -78,4 +78,20 @@ qpucuda_status qpucuda_peer_buffer_destroy(qpucuda_context *context, void *devic
     return QPUCUDA_OK;
 }
 
+qpucuda_status qpucuda_peer_copy_rows(qpucuda_context *context, void *destination, size_t destination_pitch,
+                                      const void *source, size_t source_pitch, size_t width_bytes, size_t rows,
+                                      void *stream) {
+    if (context == nullptr) return QPUCUDA_INVALID_ARGUMENT;
+    if (destination == nullptr || source == nullptr || width_bytes == 0 || rows == 0 || destination_pitch < width_bytes ||
+        source_pitch < width_bytes) {
+        return fail(context, QPUCUDA_INVALID_ARGUMENT, "peer copy: invalid arguments");
+    }
+    DeviceGuard guard(context->device);
+    cudaStream_t target = stream != nullptr ? static_cast<cudaStream_t>(stream) : context->stream;
+    const cudaError_t error = cudaMemcpy2DAsync(destination, destination_pitch, source, source_pitch, width_bytes, rows,
+                                                cudaMemcpyDeviceToDevice, target);
+    if (error != cudaSuccess) return cuda_fail(context, error, "peer copy", QPUCUDA_IO_FAILED);
+    return QPUCUDA_OK;
+}
+
 }  // extern "C"

@@ -239,6 +239,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "qpucuda_peer_buffer_close": (_S, [_P, _P]),
     "qpucuda_peer_buffer_destroy": (_S, [_P, _P]),
     "qpucuda_w8a8_linear_execute_device_fanout": (_S, [_P, _P, c_size_t, c_uint32, _P, POINTER(c_void_p), c_uint32, c_size_t]),
+    "qpucuda_peer_copy_rows": (_S, [_P, _P, c_size_t, _P, c_size_t, c_size_t, c_size_t, _P]),
     # qpucuda_q4_0.h
     "qpucuda_q4_0_linear_prepare": (_S, [_P, POINTER(Q40LinearDesc), POINTER(c_void_p)]),
     "qpucuda_q4_0_linear_destroy": (None, [_P]),

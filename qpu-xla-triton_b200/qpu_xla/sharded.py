@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+from collections.abc import Sequence
 from typing import Any, Self
 
 import numpy as np
@@ -128,6 +129,24 @@ class PeerOutput:
         offset = 4 * column_start
         return self._own + offset, [self._bases[r] + offset for r in range(self.world_size) if r != self.rank]
 
+    def push_columns(self: Self, column_start: int, column_count: int, streams: Sequence[Any], rows: int | None = None) -> None:
+        """Copy columns ``[column_start, column_start + column_count)`` of the first ``rows`` rows
+        (default all) of this rank's buffer into the same place of every other rank's buffer with the copy engines
+        (``qpucuda_peer_copy_rows``), peer i on ``streams[i % len(streams)]`` (torch CUDA streams
+        of this device, already ordered after the kernel that wrote the columns). The SMs stay free
+        for the next kernel while NVLink carries the block."""
+        library, context = self._native.library, self._native.handle
+        pitch = 4 * self.total
+        source = self._own + 4 * column_start
+        peers = [r for r in range(self.world_size) if r != self.rank]
+        for i, peer in enumerate(peers):
+            stream = streams[i % len(streams)]
+            self._native.check(
+                library.qpucuda_peer_copy_rows(context, self._bases[peer] + 4 * column_start, pitch, source, pitch,
+                                               4 * column_count, self.rows if rows is None else rows, stream.cuda_stream),
+                "qpucuda_peer_copy_rows",
+            )
+
     def _release(self: Self) -> None:
         library, context = self._native.library, self._native.handle
         for mapped in self._opened:
@@ -211,6 +230,32 @@ class ShardedW8A8Linear:
         if self.local is not None:
             destination, peers = output.slice_pointers(self.gather.start)
             self.local.forward_fanout(source, destination, peers, output.total)
+        if getattr(self, "_barrier", None) is None:
+            self._barrier = torch.zeros(1, dtype=torch.float32, device=source.device)
+        dist.all_reduce(self._barrier, group=self.gather.group)
+        return output.tensor[: source.shape[0]]
+
+    def forward_copied(self: Self, source: Any, output: PeerOutput, streams: Sequence[Any]) -> Any:
+        """``forward_fused`` with the exchange done by the copy engines: the GEMM writes this rank's
+        columns into its own ``output`` buffer only, then ``output.push_columns`` copies them to every
+        other rank on ``streams`` (ordered after the GEMM); the current stream waits for those copies
+        before the one-element NCCL all-reduce. Returns ``output.tensor``."""
+        import torch
+        import torch.distributed as dist
+
+        if output.total != self.out_features or source.shape[0] > output.rows:
+            raise ValueError("peer output must be [rows >= batch, out_features]")
+        current = torch.cuda.current_stream(source.device)
+        if self.local is not None and self.gather.count > 0:
+            destination, _ = output.slice_pointers(self.gather.start)
+            self.local.forward_fanout(source, destination, [], output.total)
+            written = torch.cuda.Event()
+            written.record(current)
+            for side in streams:
+                side.wait_event(written)
+            output.push_columns(self.gather.start, self.gather.count, streams, rows=source.shape[0])
+            for side in streams:
+                current.wait_stream(side)
         if getattr(self, "_barrier", None) is None:
             self._barrier = torch.zeros(1, dtype=torch.float32, device=source.device)
         dist.all_reduce(self._barrier, group=self.gather.group)

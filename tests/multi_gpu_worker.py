@@ -2,8 +2,9 @@
 
 Each rank builds the same seeded weights and activations, computes the full linear on its
 own GPU with one plan (the 1-GPU result), then the N-split: the fused GEMM + all-gather
-(``forward_fused`` into a ``PeerOutput``, twice into the same buffers) and the NCCL
-all-gather path (``forward``). Both must equal the 1-GPU result bit for bit on every rank;
+(``forward_fused`` into a ``PeerOutput``, twice into the same buffers), the same with the
+copy engines doing the exchange (``forward_copied``, twice) and the NCCL all-gather path
+(``forward``). All three must equal the 1-GPU result bit for bit on every rank;
 a mismatch raises, the rank exits non-zero and the launcher stops the others.
 """
 
@@ -69,6 +70,14 @@ def main() -> None:
                     bad = int((got != expected).sum())
                     raise AssertionError(f"rank {rank}: fused all-gather differs in {bad} outputs (case {rows}x{k}x{n}, pass {attempt})")
                 dist.barrier()  # every rank has read the buffers before they are written again
+            streams = [torch.cuda.Stream(cuda) for _ in range(max(1, dist.get_world_size() - 1))]
+            for attempt in range(2):
+                got = sharded.forward_copied(source, output, streams)
+                torch.cuda.synchronize()
+                if not torch.equal(got, expected):
+                    bad = int((got != expected).sum())
+                    raise AssertionError(f"rank {rank}: copy-engine all-gather differs in {bad} outputs (case {rows}x{k}x{n}, pass {attempt})")
+                dist.barrier()
             gathered = sharded.forward(source)
             torch.cuda.synchronize()
             if not torch.equal(gathered, expected):

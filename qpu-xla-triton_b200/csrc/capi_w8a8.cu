@@ -34,6 +34,10 @@ struct qpucuda_w8a8_linear {
     float *d_bias = nullptr;           // [columns] or null
     int8_t *d_quantized = nullptr;     // scratch [max_batch][k_pad]
     float *d_row_scales = nullptr;     // scratch [max_batch]
+    // Split-K workspace for batches of 9..128 rows over few output tiles: int32 partial tiles
+    // [splitk_max][kGemmBlockM][columns], or null when the columns fill the SMs without it.
+    int32_t *d_splitk = nullptr;
+    uint32_t splitk_max = 1;
     CUtensorMap map_weight;
     CUtensorMap map_quantized;
     bool maps_ready = false;
@@ -63,6 +67,7 @@ void free_linear(qpucuda_w8a8_linear *linear) {
     cudaFree(linear->d_bias);
     cudaFree(linear->d_quantized);
     cudaFree(linear->d_row_scales);
+    cudaFree(linear->d_splitk);
     cudaFree(linear->d_source);
     cudaFree(linear->d_destination);
     cudaFreeHost(linear->h_destination);
@@ -199,7 +204,17 @@ qpucuda_status enqueue_to(qpucuda_w8a8_linear *linear, const float *source, size
     } else {
         epilogue.peer_count = peer_count;
         for (uint32_t p = 0; p < peer_count; ++p) epilogue.peer_out[p] = peers[p];
-        if (quantized == linear->d_quantized && linear->maps_ready) {
+        uint32_t used_splits = 0;
+        if (peer_count == 0 && rows <= kGemmBlockM && linear->d_splitk != nullptr && quantized == linear->d_quantized &&
+            linear->maps_ready) {
+            // few output tiles: K slices into the workspace, then one reduce + epilogue launch
+            error = launch_w8a8_gemm_sm100_splitk(&linear->map_quantized, &linear->map_weight, rows, linear->columns,
+                                                  linear->k_pad, linear->d_splitk, linear->splitk_max, context->d_error,
+                                                  context->sm_count, stream, &used_splits);
+            if (error == cudaSuccess)
+                error = launch_w8a8_splitk_reduce(linear->d_splitk, used_splits, rows, linear->columns, epilogue,
+                                                  context->sm_count, stream);
+        } else if (quantized == linear->d_quantized && linear->maps_ready) {
             error = launch_w8a8_gemm_sm100(&linear->map_quantized, &linear->map_weight, rows, linear->columns,
                                            linear->k_pad, epilogue, context->d_error, context->sm_count, stream);
         } else {
@@ -275,6 +290,19 @@ qpucuda_status qpucuda_w8a8_linear_prepare(qpucuda_context *context, const qpucu
     if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_quantized), scratch_bytes);
     if (error == cudaSuccess)
         error = cudaMalloc(reinterpret_cast<void **>(&linear->d_row_scales), desc->max_batch * sizeof(float));
+    // Split-K pays when a batch of at most one row block leaves most SMs without an output tile
+    // (and the K stages are enough to share out): at most 8 slices, tiles x slices <= SMs.
+    const uint32_t row_block_tiles = (count + kGemmBlockN - 1) / kGemmBlockN;
+    const uint32_t k_stages = (linear->k_pad + kGemmBlockK - 1) / kGemmBlockK;
+    uint32_t splitk = context->sm_count > 0 ? static_cast<uint32_t>(context->sm_count) / row_block_tiles : 1u;
+    splitk = splitk < 8u ? splitk : 8u;
+    splitk = splitk < k_stages / 2u ? splitk : k_stages / 2u;
+    const size_t splitk_bytes = static_cast<size_t>(splitk) * kGemmBlockM * count * sizeof(int32_t);
+    if (error == cudaSuccess && splitk >= 2 && desc->max_batch > kGemvMaxRows && count % 4 == 0 &&
+        context->cc_major == 10 && context->cc_minor == 0) {
+        error = cudaMalloc(reinterpret_cast<void **>(&linear->d_splitk), splitk_bytes);
+        linear->splitk_max = splitk;
+    }
     if (error != cudaSuccess) {
         free_linear(linear);
         return cuda_fail(context, error, "allocate W8A8 plan", QPUCUDA_ALLOCATION_FAILED);
@@ -308,7 +336,7 @@ qpucuda_status qpucuda_w8a8_linear_prepare(qpucuda_context *context, const qpucu
                                     linear->k_pad, kGemmBlockK, kGemmBlockM);
     }
     linear->resident_bytes = weight_bytes + count * sizeof(float) * (linear->has_bias ? 2 : 1) + scratch_bytes +
-                             desc->max_batch * sizeof(float);
+                             desc->max_batch * sizeof(float) + (linear->d_splitk != nullptr ? splitk_bytes : 0);
     *result = linear;
     return QPUCUDA_OK;
 }

@@ -124,6 +124,12 @@ struct GemmParams {
     // Local row-major output written by TMA stores through map_out (32 x 32 boxes).
     uint32_t tma_store;
     unsigned int *error_word;
+    // Split-K (single-CTA tiles, int32 output only): work unit u is tile u % tiles over K stages
+    // [s * kb_per_split, (s + 1) * kb_per_split) with s = u / tiles; its rows go to output rows
+    // s * split_rows + m (split_rows a multiple of the tile rows). splits = 1: no split.
+    uint32_t splits;
+    uint32_t kb_per_split;
+    uint32_t split_rows;
 };
 
 using namespace sm100;
@@ -369,6 +375,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t warp = threadIdx.x >> 5;
     const uint32_t lane = threadIdx.x & 31;
     const uint32_t num_tiles = params.m_blocks * params.n_blocks;
+    const uint32_t num_units = num_tiles * params.splits;  // (tile, K slice) pairs
+    auto unit_range = [&](uint32_t unit, uint32_t &tile, uint32_t &kb_begin, uint32_t &kb_end) {
+        tile = unit % num_tiles;
+        kb_begin = (unit / num_tiles) * params.kb_per_split;
+        kb_end = min(params.num_kb, kb_begin + params.kb_per_split);
+    };
     const uint32_t rank = PAIR ? cluster_rank() : 0u;  // this CTA's half of the pair
     const bool leader = rank == 0;
     const uint32_t first_tile = PAIR ? blockIdx.x / 2 : blockIdx.x;
@@ -427,12 +439,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             // rather than arrays indexed by the runtime stage, which would live in local memory.
             uint32_t issued_mask = 0, issued_phases = 0;
             bool ok = true;
-            for (uint32_t tile = first_tile; ok && tile < num_tiles; tile += tile_step) {
+            for (uint32_t unit = first_tile; ok && unit < num_units; unit += tile_step) {
+                uint32_t tile, kb_begin, kb_end;
+                unit_range(unit, tile, kb_begin, kb_end);
                 uint32_t m_block, n_block;
                 tile_coords(tile, params.m_blocks, params.n_blocks, m_block, n_block);
                 const int m0 = static_cast<int>(m_block * kTileRows + rank * BM);
                 const int n0 = static_cast<int>(n_block * BN);
-                for (uint32_t kb = 0; kb < params.num_kb; ++kb) {
+                for (uint32_t kb = kb_begin; kb < kb_end; ++kb) {
                     if (!wait_bounded(smem_u32(&control->empty[stage]), phase ^ 1u, control, params.error_word)) {
                         ok = false;
                         break;
@@ -488,14 +502,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0 && (!PAIR || leader)) {
             uint32_t stage = 0, phase = 0, local_tile = 0;
             bool ok = true, any_mma = false;
-            for (uint32_t tile = first_tile; ok && tile < num_tiles; tile += tile_step, ++local_tile) {
+            for (uint32_t unit = first_tile; ok && unit < num_units; unit += tile_step, ++local_tile) {
+                uint32_t tile, kb_begin, kb_end;
+                unit_range(unit, tile, kb_begin, kb_end);
                 const uint32_t acc = local_tile & 1u;
                 const uint32_t acc_phase = (local_tile >> 1) & 1u;
                 ok = wait_bounded(smem_u32(&control->tmem_empty[acc]), acc_phase ^ 1u, control, params.error_word);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * BN;
-                for (uint32_t kb = 0; kb < params.num_kb; ++kb) {
+                for (uint32_t kb = kb_begin; kb < kb_end; ++kb) {
                     ok = wait_bounded(smem_u32(&control->full[stage]), phase, control, params.error_word);
                     if (!ok) break;
                     tc_fence_after();
@@ -510,9 +526,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         const uint64_t b = smem_desc_sw128(smem_u32(stage_b + stage * B_STAGE_BYTES + box * Pipe<PAIR>::B_BOX_BYTES)) +
                                            static_cast<uint64_t>((kk % kPerBox) * (UMMA_K >> 4));
                         if constexpr (PAIR) {
-                            umma_i8_pair(d_tmem, a, b, (kb | kk) != 0 ? 1u : 0u);
+                            umma_i8_pair(d_tmem, a, b, (kb != kb_begin || kk != 0) ? 1u : 0u);
                         } else {
-                            umma_i8(d_tmem, a, b, (kb | kk) != 0 ? 1u : 0u);
+                            umma_i8(d_tmem, a, b, (kb != kb_begin || kk != 0) ? 1u : 0u);
                         }
                     }
                     // frees this stage in both CTAs of a pair
@@ -581,7 +597,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t empty_bar0 = PAIR ? map_to_rank(smem_u32(&control->tmem_empty[0]), 0) : smem_u32(&control->tmem_empty[0]);
         const uint32_t empty_bar1 = PAIR ? map_to_rank(smem_u32(&control->tmem_empty[1]), 0) : smem_u32(&control->tmem_empty[1]);
         uint32_t local_tile = 0;
-        for (uint32_t tile = first_tile; tile < num_tiles; tile += tile_step, ++local_tile) {
+        for (uint32_t unit = first_tile; unit < num_units; unit += tile_step, ++local_tile) {
+            uint32_t tile, kb_begin, kb_end;
+            unit_range(unit, tile, kb_begin, kb_end);
+            const uint32_t split_row0 = (unit / num_tiles) * params.split_rows;  // 0 without a split
             const uint32_t acc = local_tile & 1u;
             const uint32_t acc_phase = (local_tile >> 1) & 1u;
             uint32_t m_block, n_block;
@@ -624,7 +643,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     fence_proxy_async_shared();
                     __syncwarp();
                     if (lane == 0) {
-                        tma_store_2d(&map_out, smem_u32(buffer), static_cast<int>(n0), static_cast<int>(row0));
+                        tma_store_2d(&map_out, smem_u32(buffer), static_cast<int>(n0), static_cast<int>(split_row0 + row0));
                         bulk_commit();
                     }
                     ++stores_issued;
@@ -894,6 +913,9 @@ cudaError_t launch_w8a8_gemm_sm100_mode(const CUtensorMap *map_a, const CUtensor
     params.batch_stride = epilogue.batch_stride;
     params.col_stride = epilogue.col_stride;
     params.error_word = error_word;
+    params.splits = 1;
+    params.kb_per_split = params.num_kb;
+    params.split_rows = 0;
     const uint32_t tiles = params.m_blocks * params.n_blocks;
     const bool fanout = params.peer_count != 0;
     // A local row-major output leaves through TMA stores (full 128-byte lines; per-lane 16-byte
@@ -909,6 +931,43 @@ cudaError_t launch_w8a8_gemm_sm100_mode(const CUtensorMap *map_a, const CUtensor
     }
     return fanout ? launch_kernel<true, false>(tiles, sm_count, map_a, map_w, &map_out, params, stream)
                   : launch_kernel<false, false>(tiles, sm_count, map_a, map_w, &map_out, params, stream);
+}
+
+cudaError_t launch_w8a8_gemm_sm100_splitk(const CUtensorMap *map_a, const CUtensorMap *map_w, uint32_t m, uint32_t n,
+                                          uint32_t k, int32_t *workspace, uint32_t splits, unsigned int *error_word,
+                                          int sm_count, cudaStream_t stream, uint32_t *used_splits) {
+    if (m == 0 || n == 0 || k == 0 || m > static_cast<uint32_t>(BM) || splits < 2 || n % 4 != 0 ||
+        (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) {
+        return cudaErrorInvalidValue;
+    }
+    const cudaError_t configure_error = configure_all_variants();
+    if (configure_error != cudaSuccess) return configure_error;
+    GemmParams params{};
+    params.m = m;
+    params.n = n;
+    params.k = k;
+    params.num_kb = (k + BK - 1) / BK;
+    params.m_blocks = 1;
+    params.n_blocks = (n + BN - 1) / BN;
+    params.mode = static_cast<int>(EpilogueMode::kStoreS32);
+    params.out = workspace;
+    params.out_stride = n;
+    params.peer_count = 0;
+    params.rows_per_batch = 0xFFFFFFFFu;
+    params.batch_stride = 0;
+    params.col_stride = 1;
+    params.error_word = error_word;
+    // every slice gets at least one K stage
+    params.kb_per_split = (params.num_kb + splits - 1) / splits;
+    params.splits = (params.num_kb + params.kb_per_split - 1) / params.kb_per_split;
+    params.split_rows = BM;
+    CUtensorMap map_out;
+    std::memset(&map_out, 0, sizeof(map_out));
+    params.tma_store = encode_tensor_map_2d_b32(&map_out, workspace, n, static_cast<uint64_t>(params.splits) * BM,
+                                                static_cast<uint64_t>(n) * 4u, 32u, 32u);
+    if (!params.tma_store || params.splits < 2) return cudaErrorInvalidValue;
+    *used_splits = params.splits;
+    return launch_kernel<false, false>(params.n_blocks * params.splits, sm_count, map_a, map_w, &map_out, params, stream);
 }
 
 cudaError_t run_w8a8_gemm(const int8_t *a, size_t a_stride, const int8_t *w, size_t w_stride, uint32_t m, uint32_t n,

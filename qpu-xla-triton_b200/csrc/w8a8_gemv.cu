@@ -309,6 +309,52 @@ cudaError_t launch_dependent(void (*kernel)(GemvParams), uint32_t grid, const Ge
     return cudaLaunchKernelEx(&config, kernel, p);
 }
 
+// Split-K reduction: out[r][c] = epilogue(sum over slices s of ws[s * kGemmBlockM + r][c]), four
+// columns per thread with 16-byte loads. Integer sums are exact in any order, so the result equals
+// the unsplit GEMM's bit for bit. Launched as a programmatic dependent of the split GEMM.
+__global__ void __launch_bounds__(256) w8a8_splitk_reduce_kernel(const int32_t *__restrict__ ws, uint32_t splits,
+                                                                 uint32_t m, uint32_t n, int mode,
+                                                                 const float *__restrict__ row_scales,
+                                                                 const float *__restrict__ col_scales,
+                                                                 const float *__restrict__ bias, float *__restrict__ out,
+                                                                 size_t out_stride) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const uint32_t quads = n / 4;
+    const size_t slice = static_cast<size_t>(kGemmBlockM) * n;
+    const bool vector_out = (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && (out_stride & 3u) == 0;
+    for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < static_cast<size_t>(m) * quads;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const uint32_t row = static_cast<uint32_t>(i / quads);
+        const uint32_t col = static_cast<uint32_t>(i % quads) * 4;
+        const int32_t *src = ws + static_cast<size_t>(row) * n + col;
+        int4 acc = __ldg(reinterpret_cast<const int4 *>(src));
+        for (uint32_t s = 1; s < splits; ++s) {
+            const int4 part = __ldg(reinterpret_cast<const int4 *>(src + s * slice));
+            acc.x += part.x;
+            acc.y += part.y;
+            acc.z += part.z;
+            acc.w += part.w;
+        }
+        const int values[4] = {acc.x, acc.y, acc.z, acc.w};
+        float result[4];
+        const float row_scale = row_scales[row];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float v = dequant_value(values[j], row_scale, col_scales[col + j]);
+            if (mode == static_cast<int>(EpilogueMode::kDequantizeBias)) v = __fadd_rn(v, bias[col + j]);
+            result[j] = v;
+        }
+        float *dst = out + static_cast<size_t>(row) * out_stride + col;
+        if (vector_out) {
+            *reinterpret_cast<float4 *>(dst) = make_float4(result[0], result[1], result[2], result[3]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) dst[j] = result[j];
+        }
+    }
+}
+
 // CTAs of one instantiation resident per SM, from the occupancy API, cached per device.
 template <int ROWS, int SPLIT>
 int resident_ctas() {
@@ -452,6 +498,28 @@ cudaError_t launch_w8a8_gemv(const int8_t *a, size_t a_stride, const int8_t *w, 
     // 28672 -> 8192 at M = 8 140.3 against 52.2.
     if (m == 1) return launch_rows<1>(p, sm_count, stream);
     return launch_mma(p, sm_count, stream);
+}
+
+cudaError_t launch_w8a8_splitk_reduce(const int32_t *workspace, uint32_t splits, uint32_t m, uint32_t n,
+                                      const GemmEpilogue &epilogue, int sm_count, cudaStream_t stream) {
+    if (m == 0 || n == 0) return cudaSuccess;
+    if (n % 4 != 0 || m > kGemmBlockM || epilogue.mode == EpilogueMode::kStoreS32) return cudaErrorInvalidValue;
+    const uint64_t items = static_cast<uint64_t>(m) * (n / 4);
+    uint64_t grid = (items + 255) / 256;
+    const uint64_t cap = static_cast<uint64_t>(sm_count) * 8u;
+    if (grid > cap) grid = cap;
+    cudaLaunchAttribute attribute{};
+    attribute.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute.val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3(static_cast<uint32_t>(grid));
+    config.blockDim = dim3(256);
+    config.stream = stream;
+    config.attrs = &attribute;
+    config.numAttrs = 1;
+    return cudaLaunchKernelEx(&config, w8a8_splitk_reduce_kernel, workspace, splits, m, n, static_cast<int>(epilogue.mode),
+                              epilogue.row_scales, epilogue.col_scales, epilogue.bias, static_cast<float *>(epilogue.out),
+                              epilogue.out_stride);
 }
 
 cudaError_t launch_w8a8_dequantize(const int32_t *acc, size_t acc_stride, uint32_t m, uint32_t n,

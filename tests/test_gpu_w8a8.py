@@ -234,6 +234,32 @@ def test_reference_odd_shapes_and_decode_gemv(native) -> None:  # type: ignore[n
         np.testing.assert_array_equal(out, expected)
 
 
+def test_split_k_batches_match_the_reference(native) -> None:  # type: ignore[no-untyped-def]
+    """Batches of 9..128 rows over a few output tiles run the GEMM in K slices into the plan's
+    int32 workspace and add them in a second launch. One plan, calls of 128, 17 and 100 rows in a
+    row (later calls must not see an earlier call's partial tiles), K = 4112 (33 stages: uneven
+    slices), N = 1000 with bias: bit for bit against the oracle."""
+    import torch
+
+    rng = np.random.default_rng(5150)
+    k, n = 4112, 1000
+    values, scales = oracle.quantize_per_output_channel_int8(rng.standard_normal((n, k), dtype=np.float32) * 0.05)
+    bias = rng.standard_normal(n, dtype=np.float32) * 0.1
+    handle = native.w8a8_prepare(values, scales, bias, max_batch=128)
+    try:
+        native.context.set_stream(torch.cuda.current_stream().cuda_stream)
+        for rows in (128, 17, 100):
+            source = rng.standard_normal((rows, k), dtype=np.float32)
+            src = torch.from_numpy(source).cuda()
+            out = torch.full((rows, n), float("nan"), dtype=torch.float32, device="cuda")
+            status = native.lib.qpucuda_w8a8_linear_execute_device(handle, src.data_ptr(), src.stride(0), rows, out.data_ptr(), out.stride(0))
+            native.context.check(status, "execute_device")
+            native.sync()
+            np.testing.assert_array_equal(out.cpu().numpy(), oracle.w8a8_linear(source, values, scales, bias))
+    finally:
+        native.lib.qpucuda_w8a8_linear_destroy(handle)
+
+
 def test_resident_output_window_is_a_disjoint_column_split(native) -> None:  # type: ignore[no-untyped-def]
     """The reference's output split (execute_hybrid, quantization.py:350-514) as two resident windows."""
     case = workloads.linear_inputs(40, 96, 600, seed=21, weight_std=0.05, bias=True)

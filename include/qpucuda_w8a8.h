@@ -95,6 +95,25 @@ qpucuda_status qpucuda_w8a8_linear_execute(qpucuda_w8a8_linear *linear, const qp
 qpucuda_status qpucuda_w8a8_linear_execute_direct(qpucuda_w8a8_linear *linear,
                                                   const qpucuda_w8a8_execution *execution);
 
+/* Asynchronous form of qpucuda_w8a8_linear_execute_direct: the copies and
+ * kernels are queued and the call returns at once with a submission handle.
+ * Batches above 1024 rows leave their device-to-host copies on the plan's own
+ * copy stream, so the host-to-device copies and kernels of a submission on
+ * another plan of the same context overlap them (e.g. the projections of one
+ * layer). The source and the page-locked destination must stay valid and
+ * untouched until qpucuda_w8a8_submission_wait returns; the plan accepts no
+ * other call until then (QPUCUDA_INTERNAL_ERROR). The wait is bounded by the
+ * context timeout and has the same failure rule as the direct entry point
+ * (TIMEOUT poisons the context; the destination may hold part of the results).
+ * No counterpart in the reference, whose W8A8 operator has no C form. */
+typedef struct qpucuda_w8a8_submission qpucuda_w8a8_submission;
+qpucuda_status qpucuda_w8a8_linear_submit_direct(qpucuda_w8a8_linear *linear, const qpucuda_w8a8_execution *execution,
+                                                 qpucuda_w8a8_submission **submission);
+/* Waits (bounded) for a submission; calling it again returns the same status. */
+qpucuda_status qpucuda_w8a8_submission_wait(qpucuda_w8a8_submission *submission);
+/* Frees a submission, waiting for it first if it was not waited for. */
+void qpucuda_w8a8_submission_destroy(qpucuda_w8a8_submission *submission);
+
 /* Device pointers, asynchronous on the context stream:
  * quantize source rows into the plan scratch, GEMM (tcgen05 kind::i8 for
  * rows > 8, int8 dot-product GEMV otherwise), fused dequant (+ bias) into

@@ -34,10 +34,11 @@ struct qpucuda_w8a8_linear {
     float *d_bias = nullptr;           // [columns] or null
     int8_t *d_quantized = nullptr;     // scratch [max_batch][k_pad]
     float *d_row_scales = nullptr;     // scratch [max_batch]
-    // Split-K workspace for batches of 9..128 rows over few output tiles: int32 partial tiles
-    // [splitk_max][kGemmBlockM][columns], or null when the columns fill the SMs without it.
+    // Split-K workspace for batches of 9..splitk_rows rows whose output tiles leave most SMs idle:
+    // int32 partial rows [splitk_max][splitk_rows][columns], or null when no batch needs it.
     int32_t *d_splitk = nullptr;
     uint32_t splitk_max = 1;
+    uint32_t splitk_rows = 0;  // a multiple of kGemmBlockM
     CUtensorMap map_weight;
     CUtensorMap map_quantized;
     bool maps_ready = false;
@@ -49,6 +50,9 @@ struct qpucuda_w8a8_linear {
     cudaStream_t copy_in = nullptr;
     cudaStream_t copy_out = nullptr;
     std::vector<cudaEvent_t> events;
+    // Asynchronous submissions: a page-locked copy of the kernel error word per plan, read after
+    // the submission's completion event.
+    unsigned int *h_submit_error = nullptr;
     size_t resident_bytes = 0;
     bool busy = false;
     std::mutex mutex;
@@ -68,6 +72,7 @@ void free_linear(qpucuda_w8a8_linear *linear) {
     cudaFree(linear->d_quantized);
     cudaFree(linear->d_row_scales);
     cudaFree(linear->d_splitk);
+    if (linear->h_submit_error != nullptr) cudaFreeHost(linear->h_submit_error);
     cudaFree(linear->d_source);
     cudaFree(linear->d_destination);
     cudaFreeHost(linear->h_destination);
@@ -90,7 +95,7 @@ bool ensure_pipeline(qpucuda_w8a8_linear *linear, uint32_t slices) {
             return false;
         }
     }
-    const size_t needed = 2u * slices + 2u;
+    const size_t needed = 2u * slices + 3u;
     try {
         linear->events.reserve(needed);
     } catch (...) {
@@ -117,7 +122,7 @@ qpucuda_status enqueue(qpucuda_w8a8_linear *linear, const float *source, size_t 
 // GEMM (events 1 + 2s copied in, 2 + 2s computed); the last copy-out is joined back into the
 // context stream, whose bounded wait then covers every copy and kernel of the call.
 qpucuda_status enqueue_sliced(qpucuda_w8a8_linear *linear, const float *source, uint32_t rows, uint32_t slices,
-                              float *host_out) {
+                              float *host_out, bool join = true) {
     qpucuda_context *context = linear->context;
     cudaEvent_t *events = linear->events.data();
     cudaError_t error = cudaEventRecord(events[0], context->stream);  // earlier work on the stream comes first
@@ -148,6 +153,7 @@ qpucuda_status enqueue_sliced(qpucuda_w8a8_linear *linear, const float *source, 
                                     cudaMemcpyDeviceToHost, linear->copy_out);
         if (error != cudaSuccess) return cuda_fail(context, error, "copy W8A8 destination slice");
     }
+    if (!join) return QPUCUDA_OK;  // an asynchronous submission waits on the copy stream itself
     cudaEvent_t done = events[1 + 2 * slices];
     error = cudaEventRecord(done, linear->copy_out);
     if (error == cudaSuccess) error = cudaStreamWaitEvent(context->stream, done, 0);
@@ -205,11 +211,15 @@ qpucuda_status enqueue_to(qpucuda_w8a8_linear *linear, const float *source, size
         epilogue.peer_count = peer_count;
         for (uint32_t p = 0; p < peer_count; ++p) epilogue.peer_out[p] = peers[p];
         uint32_t used_splits = 0;
-        if (peer_count == 0 && rows <= kGemmBlockM && linear->d_splitk != nullptr && quantized == linear->d_quantized &&
-            linear->maps_ready) {
+        // slices for this batch: as many as the SMs left by its tiles allow, up to the workspace's
+        const uint32_t tiles = ((rows + kGemmBlockM - 1) / kGemmBlockM) * ((linear->columns + kGemmBlockN - 1) / kGemmBlockN);
+        uint32_t splits = static_cast<uint32_t>(context->sm_count) / tiles;
+        splits = splits < linear->splitk_max ? splits : linear->splitk_max;
+        if (peer_count == 0 && rows <= linear->splitk_rows && splits >= 2 && linear->d_splitk != nullptr &&
+            quantized == linear->d_quantized && linear->maps_ready) {
             // few output tiles: K slices into the workspace, then one reduce + epilogue launch
             error = launch_w8a8_gemm_sm100_splitk(&linear->map_quantized, &linear->map_weight, rows, linear->columns,
-                                                  linear->k_pad, linear->d_splitk, linear->splitk_max, context->d_error,
+                                                  linear->k_pad, linear->d_splitk, splits, context->d_error,
                                                   context->sm_count, stream, &used_splits);
             if (error == cudaSuccess)
                 error = launch_w8a8_splitk_reduce(linear->d_splitk, used_splits, rows, linear->columns, epilogue,
@@ -290,18 +300,28 @@ qpucuda_status qpucuda_w8a8_linear_prepare(qpucuda_context *context, const qpucu
     if (error == cudaSuccess) error = cudaMalloc(reinterpret_cast<void **>(&linear->d_quantized), scratch_bytes);
     if (error == cudaSuccess)
         error = cudaMalloc(reinterpret_cast<void **>(&linear->d_row_scales), desc->max_batch * sizeof(float));
-    // Split-K pays when a batch of at most one row block leaves most SMs without an output tile
-    // (and the K stages are enough to share out): at most 8 slices, tiles x slices <= SMs.
+    // Split-K pays when a batch's output tiles (single-CTA, 128 x 256) fill at most half of the SMs
+    // and the K stages are enough to share out: at most 8 slices, tiles x slices <= SMs. The
+    // workspace covers the batches up to splitk_rows rows that qualify, within 64 MiB.
     const uint32_t row_block_tiles = (count + kGemmBlockN - 1) / kGemmBlockN;
     const uint32_t k_stages = (linear->k_pad + kGemmBlockK - 1) / kGemmBlockK;
-    uint32_t splitk = context->sm_count > 0 ? static_cast<uint32_t>(context->sm_count) / row_block_tiles : 1u;
+    const uint32_t sms = context->sm_count > 0 ? static_cast<uint32_t>(context->sm_count) : 1u;
+    uint32_t splitk = sms / row_block_tiles;
     splitk = splitk < 8u ? splitk : 8u;
     splitk = splitk < k_stages / 2u ? splitk : k_stages / 2u;
-    const size_t splitk_bytes = static_cast<size_t>(splitk) * kGemmBlockM * count * sizeof(int32_t);
-    if (error == cudaSuccess && splitk >= 2 && desc->max_batch > kGemvMaxRows && count % 4 == 0 &&
-        context->cc_major == 10 && context->cc_minor == 0) {
+    const uint32_t batch_rows = (desc->max_batch + kGemmBlockM - 1) / kGemmBlockM * kGemmBlockM;
+    uint32_t splitk_rows = sms / (2u * row_block_tiles) * kGemmBlockM;
+    splitk_rows = splitk_rows < batch_rows ? splitk_rows : batch_rows;
+    while (splitk_rows > kGemmBlockM &&
+           static_cast<size_t>(splitk) * splitk_rows * count * sizeof(int32_t) > (size_t{64} << 20)) {
+        splitk_rows -= kGemmBlockM;
+    }
+    const size_t splitk_bytes = static_cast<size_t>(splitk) * splitk_rows * count * sizeof(int32_t);
+    if (error == cudaSuccess && splitk >= 2 && splitk_rows >= kGemmBlockM && desc->max_batch > kGemvMaxRows &&
+        count % 4 == 0 && context->cc_major == 10 && context->cc_minor == 0) {
         error = cudaMalloc(reinterpret_cast<void **>(&linear->d_splitk), splitk_bytes);
         linear->splitk_max = splitk;
+        linear->splitk_rows = splitk_rows;
     }
     if (error != cudaSuccess) {
         free_linear(linear);
@@ -582,6 +602,173 @@ qpucuda_status execute_host(qpucuda_w8a8_linear *linear, const qpucuda_w8a8_exec
 }  // namespace
 
 extern "C" {
+
+struct qpucuda_w8a8_submission {
+    qpucuda_w8a8_linear *linear = nullptr;
+    cudaEvent_t done = nullptr;  // the plan's completion event of this submission
+    uint32_t slices = 1;
+    bool waited = false;
+    qpucuda_status status = QPUCUDA_OK;
+};
+
+qpucuda_status qpucuda_w8a8_linear_submit_direct(qpucuda_w8a8_linear *linear, const qpucuda_w8a8_execution *execution,
+                                                 qpucuda_w8a8_submission **submission) {
+    if (linear == nullptr || execution == nullptr || submission == nullptr) return QPUCUDA_INVALID_ARGUMENT;
+    *submission = nullptr;
+    qpucuda_context *context = linear->context;
+    const uint32_t rows = execution->rows;
+    size_t source_bytes = 0, destination_bytes = 0;
+    if (execution->source == nullptr || execution->destination == nullptr || rows == 0 || rows > linear->max_batch ||
+        !multiply_size(static_cast<size_t>(rows) * linear->k, sizeof(float), &source_bytes) ||
+        !multiply_size(static_cast<size_t>(rows) * linear->columns, sizeof(float), &destination_bytes) ||
+        execution->source_size < source_bytes || execution->destination_size < destination_bytes) {
+        return fail(context, QPUCUDA_INVALID_ARGUMENT, "prepared W8A8 linear source exceeds the plan shape");
+    }
+    if (rows > kGemvMaxRows && !(context->cc_major == 10 && context->cc_minor == 0)) {
+        return fail(context, QPUCUDA_CAPABILITY_MISSING, "the tcgen05 int8 GEMM needs an sm_100 device");
+    }
+    if (!page_locked(execution->destination) ||
+        !page_locked(reinterpret_cast<const char *>(execution->destination) + destination_bytes - 1)) {
+        return fail(context, QPUCUDA_INVALID_ARGUMENT,
+                    "a W8A8 submission needs a page-locked destination (cudaMallocHost or cudaHostRegister)");
+    }
+    qpucuda_w8a8_submission *handle = new (std::nothrow) qpucuda_w8a8_submission();
+    if (handle == nullptr) return QPUCUDA_ALLOCATION_FAILED;
+    {
+        std::lock_guard<std::mutex> guard(linear->mutex);
+        if (linear->busy) {
+            delete handle;
+            return fail(context, QPUCUDA_INTERNAL_ERROR, "prepared W8A8 linear plan already has an in-flight invocation");
+        }
+        linear->busy = true;
+    }
+    std::lock_guard<std::mutex> lock(context->mutex);
+    DeviceGuard device_guard(context->device);
+    auto release = [linear, handle](qpucuda_status status) {
+        std::lock_guard<std::mutex> guard(linear->mutex);
+        linear->busy = false;
+        delete handle;
+        return status;
+    };
+    qpucuda_status status = begin_submit(context);
+    if (status != QPUCUDA_OK) return release(status);
+    const size_t max_source = static_cast<size_t>(linear->max_batch) * linear->k * sizeof(float);
+    const size_t max_destination = static_cast<size_t>(linear->max_batch) * linear->columns * sizeof(float);
+    if (linear->d_source == nullptr) {
+        if ((context->failure_mask & QPUCUDA_FAIL_ALLOCATION) != 0 ||
+            cudaMalloc(reinterpret_cast<void **>(&linear->d_source), max_source) != cudaSuccess ||
+            cudaMalloc(reinterpret_cast<void **>(&linear->d_destination), max_destination) != cudaSuccess) {
+            (void)cudaGetLastError();
+            cudaFree(linear->d_source);
+            cudaFree(linear->d_destination);
+            linear->d_source = linear->d_destination = nullptr;
+            return release(fail(context, QPUCUDA_ALLOCATION_FAILED, "allocate W8A8 device staging"));
+        }
+    }
+    if (linear->h_submit_error == nullptr &&
+        cudaMallocHost(reinterpret_cast<void **>(&linear->h_submit_error), sizeof(unsigned int)) != cudaSuccess) {
+        (void)cudaGetLastError();
+        linear->h_submit_error = nullptr;
+        return release(fail(context, QPUCUDA_ALLOCATION_FAILED, "allocate W8A8 submission error word"));
+    }
+    const uint32_t slices = rows > kSliceRows ? (rows + kSliceRows - 1) / kSliceRows : 1;
+    if (!ensure_pipeline(linear, slices)) {
+        return release(fail(context, QPUCUDA_ALLOCATION_FAILED, "create W8A8 copy streams"));
+    }
+    float *host_out = execution->destination;
+    cudaError_t error = cudaSuccess;
+    if (slices == 1) {
+        error = cudaMemcpyAsync(linear->d_source, execution->source, source_bytes, cudaMemcpyHostToDevice, context->stream);
+        if (error != cudaSuccess) return release(cuda_fail(context, error, "copy W8A8 source"));
+        status = enqueue(linear, linear->d_source, linear->k, nullptr, 0, nullptr, rows, linear->d_destination,
+                         linear->columns);
+        if (status != QPUCUDA_OK) return release(status);
+        error = cudaMemcpyAsync(host_out, linear->d_destination, destination_bytes, cudaMemcpyDeviceToHost,
+                                context->stream);
+        if (error == cudaSuccess)
+            error = cudaMemcpyAsync(linear->h_submit_error, context->d_error, sizeof(unsigned int),
+                                    cudaMemcpyDeviceToHost, context->stream);
+        handle->done = linear->events[2 * slices + 2];
+        if (error == cudaSuccess) error = cudaEventRecord(handle->done, context->stream);
+        if (error != cudaSuccess) return release(cuda_fail(context, error, "copy W8A8 destination"));
+    } else {
+        // The device-to-host copies stay on the plan's copy stream: the next submission's
+        // host-to-device copies and kernels do not wait for them.
+        status = enqueue_sliced(linear, static_cast<const float *>(execution->source), rows, slices, host_out, false);
+        if (status == QPUCUDA_OK) {
+            cudaEvent_t computed = linear->events[1 + 2 * slices];
+            handle->done = linear->events[2 * slices + 2];
+            error = cudaMemcpyAsync(linear->h_submit_error, context->d_error, sizeof(unsigned int),
+                                    cudaMemcpyDeviceToHost, context->stream);
+            if (error == cudaSuccess) error = cudaEventRecord(computed, context->stream);
+            if (error == cudaSuccess) error = cudaStreamWaitEvent(linear->copy_out, computed, 0);
+            if (error == cudaSuccess) error = cudaEventRecord(handle->done, linear->copy_out);
+            if (error != cudaSuccess) status = cuda_fail(context, error, "record W8A8 submission");
+        }
+        if (status != QPUCUDA_OK) {
+            (void)wait_stream(context);  // drain whatever was issued before the failure (bounded)
+            drain_copies(linear);
+            return release(status);
+        }
+    }
+    handle->linear = linear;
+    handle->slices = slices;
+    *submission = handle;
+    return QPUCUDA_OK;
+}
+
+qpucuda_status qpucuda_w8a8_submission_wait(qpucuda_w8a8_submission *submission) {
+    if (submission == nullptr) return QPUCUDA_INVALID_ARGUMENT;
+    if (submission->waited) return submission->status;
+    qpucuda_w8a8_linear *linear = submission->linear;
+    qpucuda_context *context = linear->context;
+    DeviceGuard device_guard(context->device);
+    qpucuda_status status = QPUCUDA_OK;
+    const uint64_t start = monotonic_ns();
+    uint64_t polls = 0;
+    for (;;) {
+        const cudaError_t error = cudaEventQuery(submission->done);
+        if (error == cudaSuccess) break;
+        if (error != cudaErrorNotReady) {
+            std::lock_guard<std::mutex> lock(context->mutex);
+            context->poisoned = true;
+            status = cuda_fail(context, error, "wait for a W8A8 submission", QPUCUDA_IO_FAILED);
+            break;
+        }
+        if (monotonic_ns() - start > context->timeout_ns) {
+            std::lock_guard<std::mutex> lock(context->mutex);
+            context->poisoned = true;
+            status = fail(context, QPUCUDA_TIMEOUT, "W8A8 submission did not complete within %llu ns",
+                          static_cast<unsigned long long>(context->timeout_ns));
+            break;
+        }
+        if (++polls > 2000) std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    if (status == QPUCUDA_OK && (context->failure_mask & QPUCUDA_FAIL_WAIT) != 0) {
+        std::lock_guard<std::mutex> lock(context->mutex);
+        context->poisoned = true;
+        status = fail(context, QPUCUDA_TIMEOUT, "injected wait timeout");
+    }
+    if (status == QPUCUDA_OK && *linear->h_submit_error != kKernelOk) {
+        std::lock_guard<std::mutex> lock(context->mutex);
+        context->poisoned = true;
+        status = fail(context, QPUCUDA_TIMEOUT, "a kernel barrier wait exceeded its bound (code %u)", *linear->h_submit_error);
+    }
+    if (status != QPUCUDA_OK && submission->slices > 1) drain_copies(linear);
+    {
+        std::lock_guard<std::mutex> guard(linear->mutex);
+        linear->busy = false;
+    }
+    submission->waited = true;
+    submission->status = status;
+    return status;
+}
+
+void qpucuda_w8a8_submission_destroy(qpucuda_w8a8_submission *submission) {
+    if (submission == nullptr) return;
+    if (!submission->waited) (void)qpucuda_w8a8_submission_wait(submission);
+    delete submission;
+}
 
 qpucuda_status qpucuda_w8a8_linear_execute(qpucuda_w8a8_linear *linear, const qpucuda_w8a8_execution *execution) {
     return execute_host(linear, execution, false);

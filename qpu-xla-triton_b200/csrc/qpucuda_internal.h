@@ -175,11 +175,11 @@ cudaError_t launch_w8a8_gemm_sm100(const CUtensorMap *map_a, const CUtensorMap *
 cudaError_t launch_w8a8_gemm_sm100_mode(const CUtensorMap *map_a, const CUtensorMap *map_w, uint32_t m, uint32_t n,
                                         uint32_t k, const GemmEpilogue &epilogue, unsigned int *error_word,
                                         int sm_count, bool pair, cudaStream_t stream);
-// Split-K for few output tiles (m <= kGemmBlockM): the K stages are divided into `splits` slices
+// Split-K for few output tiles (single-CTA tiles): the K stages are divided into `splits` slices
 // (fewer if K is short; *used_splits says how many), and slice s writes its exact int32 partial
-// tile to workspace rows [s * kGemmBlockM, s * kGemmBlockM + m) ([used_splits * kGemmBlockM][n]
-// int32, n a multiple of 4). launch_w8a8_splitk_reduce then adds the slices and applies the
-// epilogue.
+// rows to workspace rows [s * R, s * R + m), R = m rounded up to kGemmBlockM
+// ([used_splits * R][n] int32, n a multiple of 4). launch_w8a8_splitk_reduce then adds the slices
+// and applies the epilogue.
 cudaError_t launch_w8a8_gemm_sm100_splitk(const CUtensorMap *map_a, const CUtensorMap *map_w, uint32_t m, uint32_t n,
                                           uint32_t k, int32_t *workspace, uint32_t splits, unsigned int *error_word,
                                           int sm_count, cudaStream_t stream, uint32_t *used_splits);

@@ -936,8 +936,7 @@ cudaError_t launch_w8a8_gemm_sm100_mode(const CUtensorMap *map_a, const CUtensor
 cudaError_t launch_w8a8_gemm_sm100_splitk(const CUtensorMap *map_a, const CUtensorMap *map_w, uint32_t m, uint32_t n,
                                           uint32_t k, int32_t *workspace, uint32_t splits, unsigned int *error_word,
                                           int sm_count, cudaStream_t stream, uint32_t *used_splits) {
-    if (m == 0 || n == 0 || k == 0 || m > static_cast<uint32_t>(BM) || splits < 2 || n % 4 != 0 ||
-        (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) {
+    if (m == 0 || n == 0 || k == 0 || splits < 2 || n % 4 != 0 || (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) {
         return cudaErrorInvalidValue;
     }
     const cudaError_t configure_error = configure_all_variants();
@@ -947,7 +946,7 @@ cudaError_t launch_w8a8_gemm_sm100_splitk(const CUtensorMap *map_a, const CUtens
     params.n = n;
     params.k = k;
     params.num_kb = (k + BK - 1) / BK;
-    params.m_blocks = 1;
+    params.m_blocks = (m + BM - 1) / BM;
     params.n_blocks = (n + BN - 1) / BN;
     params.mode = static_cast<int>(EpilogueMode::kStoreS32);
     params.out = workspace;
@@ -960,14 +959,16 @@ cudaError_t launch_w8a8_gemm_sm100_splitk(const CUtensorMap *map_a, const CUtens
     // every slice gets at least one K stage
     params.kb_per_split = (params.num_kb + splits - 1) / splits;
     params.splits = (params.num_kb + params.kb_per_split - 1) / params.kb_per_split;
-    params.split_rows = BM;
+    params.split_rows = params.m_blocks * BM;
     CUtensorMap map_out;
     std::memset(&map_out, 0, sizeof(map_out));
-    params.tma_store = encode_tensor_map_2d_b32(&map_out, workspace, n, static_cast<uint64_t>(params.splits) * BM,
+    params.tma_store = encode_tensor_map_2d_b32(&map_out, workspace, n,
+                                                static_cast<uint64_t>(params.splits) * params.split_rows,
                                                 static_cast<uint64_t>(n) * 4u, 32u, 32u);
     if (!params.tma_store || params.splits < 2) return cudaErrorInvalidValue;
     *used_splits = params.splits;
-    return launch_kernel<false, false>(params.n_blocks * params.splits, sm_count, map_a, map_w, &map_out, params, stream);
+    return launch_kernel<false, false>(params.m_blocks * params.n_blocks * params.splits, sm_count, map_a, map_w, &map_out,
+                                       params, stream);
 }
 
 cudaError_t run_w8a8_gemm(const int8_t *a, size_t a_stride, const int8_t *w, size_t w_stride, uint32_t m, uint32_t n,

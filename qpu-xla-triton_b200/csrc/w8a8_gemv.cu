@@ -309,7 +309,8 @@ cudaError_t launch_dependent(void (*kernel)(GemvParams), uint32_t grid, const Ge
     return cudaLaunchKernelEx(&config, kernel, p);
 }
 
-// Split-K reduction: out[r][c] = epilogue(sum over slices s of ws[s * kGemmBlockM + r][c]), four
+// Split-K reduction: out[r][c] = epilogue(sum over slices s of ws[s * R + r][c]), R = m rounded up
+// to kGemmBlockM, four
 // columns per thread with 16-byte loads. Integer sums are exact in any order, so the result equals
 // the unsplit GEMM's bit for bit. Launched as a programmatic dependent of the split GEMM.
 __global__ void __launch_bounds__(256) w8a8_splitk_reduce_kernel(const int32_t *__restrict__ ws, uint32_t splits,
@@ -321,7 +322,7 @@ __global__ void __launch_bounds__(256) w8a8_splitk_reduce_kernel(const int32_t *
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint32_t quads = n / 4;
-    const size_t slice = static_cast<size_t>(kGemmBlockM) * n;
+    const size_t slice = static_cast<size_t>((m + kGemmBlockM - 1) / kGemmBlockM * kGemmBlockM) * n;
     const bool vector_out = (reinterpret_cast<uintptr_t>(out) & 15u) == 0 && (out_stride & 3u) == 0;
     for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < static_cast<size_t>(m) * quads;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -503,7 +504,7 @@ cudaError_t launch_w8a8_gemv(const int8_t *a, size_t a_stride, const int8_t *w, 
 cudaError_t launch_w8a8_splitk_reduce(const int32_t *workspace, uint32_t splits, uint32_t m, uint32_t n,
                                       const GemmEpilogue &epilogue, int sm_count, cudaStream_t stream) {
     if (m == 0 || n == 0) return cudaSuccess;
-    if (n % 4 != 0 || m > kGemmBlockM || epilogue.mode == EpilogueMode::kStoreS32) return cudaErrorInvalidValue;
+    if (n % 4 != 0 || epilogue.mode == EpilogueMode::kStoreS32) return cudaErrorInvalidValue;
     const uint64_t items = static_cast<uint64_t>(m) * (n / 4);
     uint64_t grid = (items + 255) / 256;
     const uint64_t cap = static_cast<uint64_t>(sm_count) * 8u;

@@ -225,6 +225,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "qpucuda_w8a8_linear_resident_bytes": (c_size_t, [_P]),
     "qpucuda_w8a8_linear_execute": (_S, [_P, POINTER(W8A8Execution)]),
     "qpucuda_w8a8_linear_execute_direct": (_S, [_P, POINTER(W8A8Execution)]),
+    "qpucuda_w8a8_linear_submit_direct": (_S, [_P, POINTER(W8A8Execution), POINTER(c_void_p)]),
+    "qpucuda_w8a8_submission_wait": (_S, [_P]),
+    "qpucuda_w8a8_submission_destroy": (None, [_P]),
     "qpucuda_w8a8_linear_execute_device": (_S, [_P, _P, c_size_t, c_uint32, _P, c_size_t]),
     "qpucuda_w8a8_linear_execute_prepared_device": (_S, [_P, _P, c_size_t, _P, c_uint32, _P, c_size_t]),
     "qpucuda_w8a8_linear_execute_device_layout": (_S, [_P, _P, POINTER(MatrixLayout), c_uint32, _P, POINTER(MatrixLayout)]),

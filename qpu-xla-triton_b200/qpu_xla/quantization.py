@@ -452,6 +452,38 @@ class PreparedW8A8Linear:
         self._native.check(status, name)
         return destination
 
+    def submit_direct(self: Self, source: npt.NDArray[np.float32], destination: npt.NDArray[np.float32]) -> W8A8Submission:
+        """``qpucuda_w8a8_linear_submit_direct``: queue the host-buffer execution of ``execute_host(direct=True)``
+        and return at once; ``W8A8Submission.wait`` returns the page-locked ``destination`` once it holds the
+        results. Submissions on different plans overlap their host copies (for batches above 1024 rows)."""
+        source = np.ascontiguousarray(source, dtype=np.float32)
+        batch = source.shape[0]
+        execution = _native.W8A8Execution(source.ctypes.data, source.nbytes, destination.ctypes.data, destination.nbytes, batch)
+        handle = ctypes.c_void_p()
+        with self._backend.launch_lock:  # type: ignore[attr-defined]
+            self._native.use_library_stream()
+            status = self._native.library.qpucuda_w8a8_linear_submit_direct(self._handle, ctypes.byref(execution), ctypes.byref(handle))
+        self._native.check(status, "qpucuda_w8a8_linear_submit_direct")
+        return W8A8Submission(self._native, int(handle.value), (source, destination))  # type: ignore[arg-type]
+
+
+class W8A8Submission:
+    """A queued host-buffer execution (``qpucuda_w8a8_linear_submit_direct``); ``wait`` blocks
+    (bounded by the context timeout) until the results are in the destination."""
+
+    def __init__(self: Self, native: Any, handle: int, keep: tuple[Any, ...]) -> None:
+        self._native = native
+        self._handle = handle
+        self._keep = keep  # the source and destination stay alive until the wait
+        self._status: int | None = None
+
+    def wait(self: Self) -> Any:
+        if self._status is None:
+            self._status = int(self._native.library.qpucuda_w8a8_submission_wait(self._handle))
+            self._native.library.qpucuda_w8a8_submission_destroy(self._handle)
+        self._native.check(self._status, "qpucuda_w8a8_submission_wait")
+        return self._keep[1]
+
 
 def _torch_view(address: int, shape: tuple[int, ...], dtype: Any, device: Any) -> Any:
     """Zero-copy torch tensor over device memory owned by libqpucuda."""
@@ -562,6 +594,7 @@ class CalibratedW8A8Linear:
 
 __all__ = [
     "CalibratedW8A8Linear",
+    "W8A8Submission",
     "PreparedW8A8Linear",
     "QuantizedMatrixInt8",
     "quantize_per_output_channel_int8",

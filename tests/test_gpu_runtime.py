@@ -124,6 +124,38 @@ def test_direct_host_execute_writes_a_page_locked_destination_in_place(cuda_devi
         assert np.isnan(pageable).all()
 
 
+def test_submissions_on_three_plans_overlap_and_match(cuda_device: Device) -> None:
+    """qpucuda_w8a8_linear_submit_direct on three plans of one context, queued back to back before any
+    wait (sliced and single-slice batches, the GEMV rows, one plan with bias): every destination
+    equals the oracle bit for bit after its wait; a second submission on a plan still in flight is
+    refused; waiting twice returns the same result."""
+    import torch
+
+    from qpu_xla.quantization import PreparedW8A8Linear as Plan
+
+    rng = np.random.default_rng(91)
+    shapes = ((2300, 256, 512, False), (1500, 384, 1024, True), (5, 512, 256, False))
+    plans, jobs = [], []
+    try:
+        for rows, k, n, with_bias in shapes:
+            values, scales = oracle.quantize_per_output_channel_int8(rng.standard_normal((n, k)).astype(np.float32))
+            bias = rng.standard_normal(n).astype(np.float32) if with_bias else None
+            plan = Plan(cuda_device, QuantizedMatrixInt8(values, scales), max_batch=rows, bias=bias)
+            plans.append(plan)
+            source = torch.from_numpy(rng.standard_normal((rows, k)).astype(np.float32)).pin_memory()
+            pinned = torch.full((rows, n), float("nan"), dtype=torch.float32).pin_memory()
+            jobs.append((plan.submit_direct(source.numpy(), pinned.numpy()), source, pinned, values, scales, bias))
+        with pytest.raises(RuntimeError):
+            plans[0].submit_direct(jobs[0][1].numpy(), jobs[0][2].numpy())
+        for submission, source, pinned, values, scales, bias in jobs:
+            result = submission.wait()
+            np.testing.assert_array_equal(result, oracle.w8a8_linear(source.numpy(), values, scales, bias))
+            assert submission.wait() is result
+    finally:
+        for plan in plans:
+            plan.close()
+
+
 def test_two_contexts_driven_from_two_threads_at_once() -> None:
     """Two contexts on one device, each called from its own host thread at the same time (the C
     calls release the GIL): every kernel's one-time set-up is per device and thread-safe, and each

@@ -234,21 +234,26 @@ def test_reference_odd_shapes_and_decode_gemv(native) -> None:  # type: ignore[n
         np.testing.assert_array_equal(out, expected)
 
 
-def test_split_k_batches_match_the_reference(native) -> None:  # type: ignore[no-untyped-def]
-    """Batches of 9..128 rows over a few output tiles run the GEMM in K slices into the plan's
-    int32 workspace and add them in a second launch. One plan, calls of 128, 17 and 100 rows in a
-    row (later calls must not see an earlier call's partial tiles), K = 4112 (33 stages: uneven
-    slices), N = 1000 with bias: bit for bit against the oracle."""
+@pytest.mark.parametrize(
+    "k,n,max_batch,batches",
+    [
+        (4112, 1000, 128, (128, 17, 100)),  # one row block; 33 K stages: uneven slices
+        (2064, 256, 512, (300, 512, 130, 9)),  # one column tile, several row blocks per slice
+    ],
+)
+def test_split_k_batches_match_the_reference(native, k: int, n: int, max_batch: int, batches: tuple[int, ...]) -> None:  # type: ignore[no-untyped-def]
+    """Batches whose output tiles leave most SMs idle run the GEMM in K slices into the plan's
+    int32 workspace and add them in a second launch. One plan, several batch sizes in a row (later
+    calls must not see an earlier call's partial rows), with bias: bit for bit against the oracle."""
     import torch
 
-    rng = np.random.default_rng(5150)
-    k, n = 4112, 1000
+    rng = np.random.default_rng(5150 + n)
     values, scales = oracle.quantize_per_output_channel_int8(rng.standard_normal((n, k), dtype=np.float32) * 0.05)
     bias = rng.standard_normal(n, dtype=np.float32) * 0.1
-    handle = native.w8a8_prepare(values, scales, bias, max_batch=128)
+    handle = native.w8a8_prepare(values, scales, bias, max_batch=max_batch)
     try:
         native.context.set_stream(torch.cuda.current_stream().cuda_stream)
-        for rows in (128, 17, 100):
+        for rows in batches:
             source = rng.standard_normal((rows, k), dtype=np.float32)
             src = torch.from_numpy(source).cuda()
             out = torch.full((rows, n), float("nan"), dtype=torch.float32, device="cuda")

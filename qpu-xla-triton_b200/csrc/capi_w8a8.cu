@@ -310,10 +310,7 @@ qpucuda_status qpucuda_w8a8_linear_prepare(qpucuda_context *context, const qpucu
     splitk = splitk < 8u ? splitk : 8u;
     splitk = splitk < k_stages / 2u ? splitk : k_stages / 2u;
     const uint32_t batch_rows = (desc->max_batch + kGemmBlockM - 1) / kGemmBlockM * kGemmBlockM;
-    // Larger batches gain nothing: at 2048 rows a 256-column projection took as long split (8 slices,
-    // 16.8 MB of partial rows and a reduce launch) as unsplit, so the split stops at 256 rows.
     uint32_t splitk_rows = sms / (2u * row_block_tiles) * kGemmBlockM;
-    splitk_rows = splitk_rows < 2u * kGemmBlockM ? splitk_rows : 2u * kGemmBlockM;
     splitk_rows = splitk_rows < batch_rows ? splitk_rows : batch_rows;
     while (splitk_rows > kGemmBlockM &&
            static_cast<size_t>(splitk) * splitk_rows * count * sizeof(int32_t) > (size_t{64} << 20)) {

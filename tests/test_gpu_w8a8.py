@@ -42,6 +42,7 @@ def sha256(array: np.ndarray) -> str:
         (2, 40000, 40000), (5, 33, 48),
         # many rows: register-cached kernel up to ~14.5K columns, bulk-staged kernel above
         (297, 1024, 1040), (300, 16384, 16384), (600, 28672, 28688), (4096, 8192, 8192), (296, 14592, 14592),
+        (2048, 2048, 2048), (100, 1500, 1504), (64, 996, 1008),
     ],
 )
 def test_row_quantizer_is_bit_exact(native, rows: int, cols: int, padded: int) -> None:  # type: ignore[no-untyped-def]
@@ -238,7 +239,7 @@ def test_reference_odd_shapes_and_decode_gemv(native) -> None:  # type: ignore[n
     "k,n,max_batch,batches",
     [
         (4112, 1000, 128, (128, 17, 100)),  # one row block; 33 K stages: uneven slices
-        (2064, 256, 256, (200, 256, 130, 9)),  # one column tile, two row blocks per slice
+        (2064, 256, 512, (300, 512, 130, 9)),  # one column tile, several row blocks per slice
     ],
 )
 def test_split_k_batches_match_the_reference(native, k: int, n: int, max_batch: int, batches: tuple[int, ...]) -> None:  # type: ignore[no-untyped-def]

@@ -437,12 +437,13 @@ int mma_resident_ctas() {
     return per_sm;
 }
 
-// Persistent grid with every CTA running the same number of 16-column groups.
+// Persistent grid filling every resident slot, so each SM carries the same share of the 16-column
+// groups (a grid trimmed to equal rounds per CTA put a fourth CTA on a few SMs: 70B gate at M = 8
+// 52.3 against 48.2 us with the quantizer).
 cudaError_t launch_mma(const GemvParams &p, int sm_count, cudaStream_t stream) {
     const uint64_t groups = (p.n + 15) / 16;
     const uint64_t capacity = static_cast<uint64_t>(sm_count) * static_cast<uint64_t>(mma_resident_ctas());
-    const uint64_t rounds = (groups + capacity - 1) / capacity;
-    const uint32_t grid = static_cast<uint32_t>((groups + rounds - 1) / rounds);
+    const uint32_t grid = static_cast<uint32_t>(groups < capacity ? groups : capacity);
     return launch_dependent(w8a8_gemv_mma_kernel, grid, p, stream);
 }
 

@@ -833,6 +833,61 @@ def object_tinyllama_w8a8(bench: Bench, int8_peak: float, hbm_peak: float, int8_
         for plan in plans:
             plan.close()
     result["value"] = result["tokens"]["2048"]["tops"]
+    result["merged"] = tinyllama_merged(bench, int8_peak, hbm_peak, int8_note, hbm_note)
+    return result
+
+
+def tinyllama_merged(bench: Bench, int8_peak: float, hbm_peak: float, int8_note: str, hbm_note: str) -> dict[str, Any]:
+    """The same seven projections as four plans: q/k/v and gate/up read one input each in a layer,
+    so each trio or pair runs as one MergedW8A8Linear (one row quantization, one GEMM or GEMV over
+    the stacked output channels); o and down stay single. Same weights and outputs column for column."""
+    import torch
+
+    from qpu_xla import workloads
+    from qpu_xla.quantization import MergedW8A8Linear, quantize_per_output_channel_int8
+
+    shapes7 = workloads.TINYLLAMA_LAYER
+    groups = ((0, 1, 2), (3,), (4, 5), (6,))
+    weights = [quantize_per_output_channel_int8(workloads.tinyllama_case(s, workloads.TINYLLAMA_TOKENS[-1]).weight, device=bench.device)
+               for s in shapes7]
+    plans = [MergedW8A8Linear(bench.device, [weights[i] for i in g], max_batch=max(workloads.TINYLLAMA_TOKENS)) for g in groups]
+    result: dict[str, Any] = {
+        "groups": ["q+k+v", "o", "gate+up", "down"],
+        "note": "q/k/v share the layer input and gate/up the FFN input, so each group is one row quantization and one "
+                "GEMM/GEMV over the stacked output channels (8 launches per layer instead of 14); outputs equal the "
+                "seven separate plans bit for bit",
+        "tokens": {},
+    }
+    try:
+        for tokens in workloads.TINYLLAMA_TOKENS:
+            sources = [torch.from_numpy(workloads.tinyllama_case(shapes7[g[0]], tokens).source).to(bench.cuda) for g in groups]
+            outs = [torch.empty((tokens, plan.output_count), dtype=torch.float32, device=bench.cuda) for plan in plans]
+
+            def layer(sources: list[Any] = sources, outs: list[Any] = outs) -> None:
+                for plan, src, out in zip(plans, sources, outs):
+                    plan.plan.forward(src, out=out)
+
+            ms = statistics.median(bench.brackets(layer, 20, launches=2 * len(plans)))
+            ops = sum(2.0 * tokens * s.in_features * s.out_features for s in shapes7)
+            nbytes = 0.0
+            for g in groups:
+                k = shapes7[g[0]].in_features
+                n = sum(shapes7[i].out_features for i in g)
+                k16 = (k + 15) // 16 * 16
+                nbytes += n * k16 + tokens * k * 4.0 + tokens * k16 + 4.0 * (n + tokens + tokens * n)
+            path = "row quantizer + w8a8_gemv (merged sections)" if tokens <= 8 else "row quantizer + w8a8_gemm_sm100 (merged sections)"
+            result["tokens"][str(tokens)] = {
+                "tops": round(ops / (ms * 1e-3) / 1e12, 2),
+                "gbs": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                "us_per_layer": round(ms * 1e3, 2),
+                "roofline": roofline(kernel=path, seconds=ms * 1e-3, ops=ops, nbytes=nbytes, int8_peak=int8_peak, hbm_peak=hbm_peak,
+                                     peak_note=int8_note if ops / (int8_peak * 1e12) >= nbytes / (hbm_peak * 1e9) else hbm_note,
+                                     traffic=None),
+            }
+            del sources, outs
+    finally:
+        for plan in plans:
+            plan.close()
     return result
 
 

@@ -485,6 +485,76 @@ class W8A8Submission:
         return self._keep[1]
 
 
+def concatenate_output_channels(weights: Sequence[QuantizedMatrixInt8]) -> QuantizedMatrixInt8:
+    """Stack int8 weight matrices of the same input width along the output-channel axis (each row
+    keeps its own scale)."""
+    if not weights:
+        raise ValueError("concatenate_output_channels needs at least one weight")
+    features = weights[0].shape[1]
+    if any(w.shape[1] != features for w in weights):
+        raise ValueError("merged W8A8 linears must share the input width")
+    return QuantizedMatrixInt8(
+        np.ascontiguousarray(np.concatenate([w.values for w in weights], axis=0)),
+        np.ascontiguousarray(np.concatenate([w.scales for w in weights])),
+    )
+
+
+class MergedW8A8Linear:
+    """Linears that read the same input (a layer's q/k/v, an FFN's gate/up) run as one plan.
+
+    No counterpart in the reference, which quantizes the input once per linear
+    (models/tinyllama/accelerated.py:228-266 calls each projection's plan). Here the int8 weights
+    are stacked along the output channels, so one row quantization and one GEMM (or GEMV) launch
+    produce every section. Each section equals its own :class:`PreparedW8A8Linear` bit for bit:
+    activation rows are quantized without reference to the weights, the int32 dot of a column is
+    exact in any order, and every output channel has its own scale (and bias). Either every section
+    has a bias or none has one (a zero bias would turn a -0.0 output into +0.0).
+    """
+
+    def __init__(
+        self: Self,
+        device: Device,
+        weights: Sequence[QuantizedMatrixInt8],
+        *,
+        max_batch: int,
+        biases: Sequence[npt.NDArray[np.float32]] | None = None,
+    ) -> None:
+        merged = concatenate_output_channels(weights)
+        self.sections = tuple(int(w.shape[0]) for w in weights)
+        bias = None
+        if biases is not None:
+            if len(biases) != len(weights) or any(b is None for b in biases):
+                raise ValueError("merged W8A8 linears need a bias for every section or for none")
+            parts = [np.ascontiguousarray(b, dtype=np.float32) for b in biases]
+            if any(p.shape != (n,) for p, n in zip(parts, self.sections)):
+                raise ValueError("bias must have one fp32 value per output feature")
+            bias = np.ascontiguousarray(np.concatenate(parts))
+        self.bounds = tuple((int(a), int(b)) for a, b in zip(np.cumsum((0, *self.sections[:-1])), np.cumsum(self.sections)))
+        self.plan = PreparedW8A8Linear(device, merged, max_batch=max_batch, bias=bias)
+
+    @property
+    def output_count(self: Self) -> int:
+        return self.plan.output_count
+
+    def split(self: Self, out: Any) -> list[Any]:
+        """Column views of a merged ``[batch, output_count]`` output, one per section."""
+        return [out[:, a:b] for a, b in self.bounds]
+
+    def forward(self: Self, source: Any, out: Any = None) -> list[Any]:
+        """Torch path on the current stream: fp32 ``[batch, K]`` -> one ``[batch, n_i]`` view per
+        section of the merged output (``out``, ``[batch, output_count]``, when given)."""
+        return self.split(self.plan.forward(source, out=out))
+
+    def close(self: Self) -> None:
+        self.plan.close()
+
+    def __enter__(self: Self) -> Self:
+        return self
+
+    def __exit__(self: Self, exc_type: object, exc_value: object, traceback: object) -> None:
+        self.close()
+
+
 def _torch_view(address: int, shape: tuple[int, ...], dtype: Any, device: Any) -> Any:
     """Zero-copy torch tensor over device memory owned by libqpucuda."""
     import torch
@@ -594,8 +664,10 @@ class CalibratedW8A8Linear:
 
 __all__ = [
     "CalibratedW8A8Linear",
+    "MergedW8A8Linear",
     "W8A8Submission",
     "PreparedW8A8Linear",
     "QuantizedMatrixInt8",
+    "concatenate_output_channels",
     "quantize_per_output_channel_int8",
 ]

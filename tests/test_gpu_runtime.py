@@ -342,3 +342,39 @@ def test_sharded_linear_on_one_rank_equals_the_unsharded_plan(cuda_device: Devic
     finally:
         if owned:
             dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("with_bias", (False, True), ids=("no-bias", "bias"))
+def test_merged_linear_sections_equal_their_own_linears(cuda_device: Device, with_bias: bool) -> None:
+    """q/k/v-shaped weights (wide, narrow, narrow) merged into one plan: at GEMV, split-K,
+    single-tile and CTA-pair batch sizes each section of the merged output equals the oracle of
+    its own linear bit for bit, and the merged output equals three separate plans."""
+    import torch
+
+    from qpu_xla.quantization import MergedW8A8Linear
+
+    rng = np.random.default_rng(57)
+    k, sections = 1040, (512, 64, 64)
+    weights, biases = [], []
+    for n in sections:
+        values, scales = oracle.quantize_per_output_channel_int8((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+        weights.append(QuantizedMatrixInt8(values, scales))
+        biases.append(rng.standard_normal(n).astype(np.float32))
+    merged = MergedW8A8Linear(cuda_device, weights, max_batch=600, biases=biases if with_bias else None)
+    separate = [PreparedW8A8Linear(cuda_device, w, max_batch=600, bias=b if with_bias else None) for w, b in zip(weights, biases)]
+    try:
+        assert merged.output_count == sum(sections)
+        for rows in (1, 6, 64, 600):
+            source_np = rng.standard_normal((rows, k)).astype(np.float32)
+            source = torch.from_numpy(source_np).cuda()
+            parts = merged.forward(source)
+            alone = [plan.forward(source) for plan in separate]
+            torch.cuda.synchronize()
+            for part, single, w, b in zip(parts, alone, weights, biases):
+                expected = oracle.w8a8_linear(source_np, w.values, w.scales, b if with_bias else None)
+                np.testing.assert_array_equal(part.cpu().numpy(), expected)
+                assert torch.equal(part, single)
+    finally:
+        merged.close()
+        for plan in separate:
+            plan.close()

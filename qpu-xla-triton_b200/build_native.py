@@ -67,7 +67,7 @@ def common_flags() -> list[str]:
 
 def _stamp() -> str:
     digest = hashlib.sha256()
-    for path in sorted([*sources(), *CSRC.glob("*.h"), *INCLUDE.glob("*.h"), Path(__file__)]):
+    for path in sorted([*sources(), *CSRC.glob("*.h"), *CSRC.glob("*.cuh"), *INCLUDE.glob("*.h"), Path(__file__)]):
         digest.update(path.name.encode())
         digest.update(path.read_bytes())
     return digest.hexdigest()

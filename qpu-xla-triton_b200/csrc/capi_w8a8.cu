@@ -182,26 +182,40 @@ qpucuda_status enqueue_to(qpucuda_w8a8_linear *linear, const float *source, size
                           float *destination, size_t destination_stride, float *const *peers, uint32_t peer_count) {
     qpucuda_context *context = linear->context;
     cudaStream_t stream = context->stream;
-    if (source != nullptr) {
-        const cudaError_t error = launch_quantize_rows_int8(source, source_stride, rows, linear->k, linear->k_pad,
-                                                            linear->d_quantized, linear->k_pad, linear->d_row_scales,
-                                                            context->d_error, stream);
-        if (error != cudaSuccess) return cuda_fail(context, error, "quantize activations");
-        quantized = linear->d_quantized;
-        quantized_stride = linear->k_pad;
-        row_scales = linear->d_row_scales;
-    }
     GemmEpilogue epilogue;
     epilogue.mode = linear->has_bias ? EpilogueMode::kDequantizeBias : EpilogueMode::kDequantize;
-    epilogue.row_scales = row_scales;
     epilogue.col_scales = linear->d_weight_scales;
     epilogue.bias = linear->d_bias;
     epilogue.out = destination;
     epilogue.out_stride = destination_stride;
-    cudaError_t error;
+    // A single fp32 row: the GEMV quantizes it itself (one launch instead of two) when the row is
+    // short enough; it still leaves the int8 row and scale in the plan scratch.
+    cudaError_t fused = cudaErrorNotSupported;
+    if (source != nullptr && rows == 1) {
+        epilogue.row_scales = linear->d_row_scales;
+        fused = launch_w8a8_gemv_quantize(source, linear->k, linear->d_quantized, linear->d_row_scales,
+                                          linear->d_weight, linear->k_pad, linear->columns, linear->k_pad, epilogue,
+                                          context->sm_count, stream);
+        if (fused != cudaSuccess && fused != cudaErrorNotSupported) return cuda_fail(context, fused, "W8A8 GEMV launch");
+    }
+    if (source != nullptr && fused != cudaSuccess) {
+        const cudaError_t error = launch_quantize_rows_int8(source, source_stride, rows, linear->k, linear->k_pad,
+                                                            linear->d_quantized, linear->k_pad, linear->d_row_scales,
+                                                            context->d_error, stream);
+        if (error != cudaSuccess) return cuda_fail(context, error, "quantize activations");
+    }
+    if (source != nullptr) {
+        quantized = linear->d_quantized;
+        quantized_stride = linear->k_pad;
+        row_scales = linear->d_row_scales;
+    }
+    epilogue.row_scales = row_scales;
+    cudaError_t error = cudaSuccess;
     if (rows <= kGemvMaxRows) {
-        error = launch_w8a8_gemv(quantized, quantized_stride, linear->d_weight, linear->k_pad, rows, linear->columns,
-                                 linear->k_pad, epilogue, context->sm_count, stream);
+        if (fused != cudaSuccess) {
+            error = launch_w8a8_gemv(quantized, quantized_stride, linear->d_weight, linear->k_pad, rows,
+                                     linear->columns, linear->k_pad, epilogue, context->sm_count, stream);
+        }
         for (uint32_t p = 0; error == cudaSuccess && p < peer_count; ++p) {
             error = cudaMemcpy2DAsync(peers[p], destination_stride * sizeof(float), destination,
                                       destination_stride * sizeof(float), static_cast<size_t>(linear->columns) * sizeof(float),

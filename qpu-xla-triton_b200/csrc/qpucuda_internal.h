@@ -197,6 +197,13 @@ constexpr uint32_t kGemmWeightBoxRows = 128;  // W rows per TMA box (a 256-row t
 cudaError_t launch_w8a8_gemv(const int8_t *a, size_t a_stride, const int8_t *w, size_t w_stride, uint32_t m,
                              uint32_t n, uint32_t k, const GemmEpilogue &epilogue, int sm_count,
                              cudaStream_t stream);
+// One row, quantized by the GEMV itself: x[0 .. cols) fp32 -> int8 (every CTA into shared memory;
+// CTA 0 also into q_out[0 .. k), zero padded, and *scale_out), then the dequantizing GEMV. Returns
+// cudaErrorNotSupported (nothing launched) unless cols % 4 == 0, x is 16-byte and q_out 4-byte
+// aligned and k <= 8192; the caller then runs the row quantizer and launch_w8a8_gemv.
+cudaError_t launch_w8a8_gemv_quantize(const float *x, uint32_t cols, int8_t *q_out, float *scale_out, const int8_t *w,
+                                      size_t w_stride, uint32_t n, uint32_t k, const GemmEpilogue &epilogue,
+                                      int sm_count, cudaStream_t stream);
 cudaError_t launch_w8a8_dequantize(const int32_t *acc, size_t acc_stride, uint32_t m, uint32_t n,
                                    const GemmEpilogue &epilogue, cudaStream_t stream);
 

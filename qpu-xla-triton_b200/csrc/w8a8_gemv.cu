@@ -10,6 +10,11 @@
 //    - Two to eight rows (w8a8_gemv_mma_kernel): mma.sync m16n8k32 over 16-column groups,
 //      so the weight bytes are read once however many rows there are (dp4a would issue four
 //      instructions per row per 16 bytes and re-read the activation chunks per row).
+//    - One row with its quantization fused (w8a8_gemv_kernel<1, SPLIT, true>): every CTA
+//      quantizes the fp32 row into shared memory itself (the row quantizer's arithmetic,
+//      row_quantize.cuh) after streaming in its first weights, so no separate quantizer launch
+//      sits between the previous kernel and the GEMV; CTA 0 also writes the int8 row and scale to
+//      the plan scratch. Used for rows up to kFusedQuantMaxK columns (an L1-resident re-read).
 //    Integer addition is associative, so the int32 result is exact in any order, and the
 //    fused epilogue is the same ((float)acc * s_a) * s_w (+ bias) as the GEMM. The grids
 //    are persistent, sized from the occupancy API with every CTA running the same number
@@ -19,6 +24,7 @@
 #include <atomic>
 
 #include "qpucuda_internal.h"
+#include "row_quantize.cuh"
 
 namespace qpucuda {
 namespace {
@@ -35,6 +41,12 @@ struct GemvParams {
     const float *bias;
     void *out;
     size_t out_stride;
+    // One-row kernel that quantizes its own activation (QUANT): the fp32 row x[0 .. x_cols) and
+    // where CTA 0 leaves the int8 row (k bytes, zero padded) and its scale.
+    const float *x;
+    uint32_t x_cols;
+    int8_t *q_out;
+    float *scale_out;
 };
 
 __device__ __forceinline__ uint4 load_weight_chunk(const int8_t *p) {
@@ -56,9 +68,11 @@ constexpr int kGemvWarps = kGemvThreads / 32;
 // warp steps); their int32 partial sums meet in shared memory. Integer addition is
 // associative, so any split gives the same exact accumulator. The grid is persistent and
 // balanced (every column slot runs the same number of rounds), so no partial wave trails.
-template <int ROWS, int SPLIT>
+template <int ROWS, int SPLIT, bool QUANT = false>
 __global__ void __launch_bounds__(kGemvThreads) w8a8_gemv_kernel(const GemvParams p) {
+    static_assert(!QUANT || ROWS == 1, "the fused quantizer serves one row");
     __shared__ int partial[kGemvWarps][ROWS];
+    extern __shared__ __align__(16) uint8_t quantized_row[];  // QUANT: the int8 row, p.k bytes
     constexpr uint32_t kSlots = kGemvWarps / SPLIT;
     // One or two rows are bound by the weight stream: each column's first trip is loaded during
     // the previous column's reduction. More rows are issue-bound and keep those registers for
@@ -93,7 +107,44 @@ __global__ void __launch_bounds__(kGemvThreads) w8a8_gemv_kernel(const GemvParam
     // scales are its output and are read only after the wait.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const float row_scale = writer && p.mode != static_cast<int>(EpilogueMode::kStoreS32) ? p.row_scales[lane] : 0.0f;
+    float quant_scale = 0.0f;
+    if constexpr (QUANT) {
+        // The row quantizer's two passes over the fp32 row (the second one hits L1): max|x|
+        // over the CTA, then the int8 row into shared memory (and, from CTA 0, the plan scratch).
+        __shared__ float reduce_scratch[32];
+        const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
+        const uint32_t vectors = p.x_cols / 4;
+        float amax = 0.0f;
+        for (uint32_t i = threadIdx.x; i < vectors; i += kGemvThreads) amax = abs_max4(amax, __ldg(x4 + i));
+        amax = block_max<kGemvThreads>(amax, reduce_scratch);
+        quant_scale = row_scale_of(amax);
+        const float inverse = __frcp_rn(quant_scale);
+        uint32_t *row_words = reinterpret_cast<uint32_t *>(quantized_row);
+        uint32_t *scratch_words = reinterpret_cast<uint32_t *>(p.q_out);
+        const bool keeper = blockIdx.x == 0;
+        for (uint32_t i = threadIdx.x; i < vectors; i += kGemvThreads) {
+            const uint32_t packed = quantize4(__ldg(x4 + i), quant_scale, inverse);
+            row_words[i] = packed;
+            if (keeper) scratch_words[i] = packed;
+        }
+        for (uint32_t i = vectors + threadIdx.x; i < p.k / 4; i += kGemvThreads) {
+            row_words[i] = 0u;
+            if (keeper) scratch_words[i] = 0u;
+        }
+        if (keeper && threadIdx.x == 0) *p.scale_out = quant_scale;
+        __syncthreads();
+    }
+    // 16 activation bytes (chunk `index` of row r): from the CTA's own quantized row, or global.
+    auto activation = [&](int r, uint32_t index) -> uint4 {
+        if constexpr (QUANT) {
+            return reinterpret_cast<const uint4 *>(quantized_row)[index];
+        } else {
+            return __ldg(reinterpret_cast<const uint4 *>(p.a + static_cast<size_t>(r) * p.a_stride) + index);
+        }
+    };
+    const float row_scale = writer && p.mode != static_cast<int>(EpilogueMode::kStoreS32)
+                                ? (QUANT ? quant_scale : p.row_scales[lane])
+                                : 0.0f;
     for (; n < p.n; n += stride) {
         const int8_t *w_row = p.w + static_cast<size_t>(n) * p.w_stride;
         // The epilogue's per-column operands, loaded now so they arrive with the weights.
@@ -115,8 +166,7 @@ __global__ void __launch_bounds__(kGemvThreads) w8a8_gemv_kernel(const GemvParam
 #pragma unroll
                 for (int r = 0; r < ROWS; ++r) {
                     if (static_cast<uint32_t>(r) >= p.m) break;  // uniform across the warp
-                    const uint4 av =
-                        __ldg(reinterpret_cast<const uint4 *>(p.a + static_cast<size_t>(r) * p.a_stride) + c + 32 * u);
+                    const uint4 av = activation(r, c + 32 * u);
                     acc[r] = __dp4a(static_cast<int>(wv[u].x), static_cast<int>(av.x), acc[r]);
                     acc[r] = __dp4a(static_cast<int>(wv[u].y), static_cast<int>(av.y), acc[r]);
                     acc[r] = __dp4a(static_cast<int>(wv[u].z), static_cast<int>(av.z), acc[r]);
@@ -131,7 +181,7 @@ __global__ void __launch_bounds__(kGemvThreads) w8a8_gemv_kernel(const GemvParam
 #pragma unroll
             for (int r = 0; r < ROWS; ++r) {
                 if (static_cast<uint32_t>(r) >= p.m) break;  // uniform across the warp
-                const uint4 av = __ldg(reinterpret_cast<const uint4 *>(p.a + static_cast<size_t>(r) * p.a_stride) + c);
+                const uint4 av = activation(r, c);
                 acc[r] = __dp4a(static_cast<int>(wt.x), static_cast<int>(av.x), acc[r]);
                 acc[r] = __dp4a(static_cast<int>(wt.y), static_cast<int>(av.y), acc[r]);
                 acc[r] = __dp4a(static_cast<int>(wt.z), static_cast<int>(av.z), acc[r]);
@@ -296,13 +346,15 @@ __global__ void __launch_bounds__(256) w8a8_dequantize_kernel(const int32_t *__r
 
 // A launch that may begin while the previous kernel on the stream finishes (programmatic stream
 // serialization); the kernel's griddepcontrol.wait orders its reads of that kernel's output.
-cudaError_t launch_dependent(void (*kernel)(GemvParams), uint32_t grid, const GemvParams &p, cudaStream_t stream) {
+cudaError_t launch_dependent(void (*kernel)(GemvParams), uint32_t grid, const GemvParams &p, cudaStream_t stream,
+                             size_t smem = 0) {
     cudaLaunchAttribute attribute{};
     attribute.id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attribute.val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t config{};
     config.gridDim = dim3(grid);
     config.blockDim = dim3(kGemvThreads);
+    config.dynamicSmemBytes = smem;
     config.stream = stream;
     config.attrs = &attribute;
     config.numAttrs = 1;
@@ -356,8 +408,13 @@ __global__ void __launch_bounds__(256) w8a8_splitk_reduce_kernel(const int32_t *
     }
 }
 
-// CTAs of one instantiation resident per SM, from the occupancy API, cached per device.
-template <int ROWS, int SPLIT>
+// Longest row the one-row GEMV quantizes itself (32 KB of fp32, re-read from L1); its int8 copy
+// is the kernel's dynamic shared memory.
+constexpr uint32_t kFusedQuantMaxK = 8192;
+
+// CTAs of one instantiation resident per SM, from the occupancy API, cached per device (the
+// fused-quantizer variants with the largest shared-memory row they take).
+template <int ROWS, int SPLIT, bool QUANT = false>
 int resident_ctas() {
     static std::atomic<int> cached[64] = {};
     int device = 0;
@@ -365,8 +422,8 @@ int resident_ctas() {
     const int known = cached[device].load(std::memory_order_relaxed);
     if (known > 0) return known;
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, w8a8_gemv_kernel<ROWS, SPLIT>, kGemvThreads, 0) !=
-            cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, w8a8_gemv_kernel<ROWS, SPLIT, QUANT>, kGemvThreads,
+                                                      QUANT ? kFusedQuantMaxK : 0) != cudaSuccess ||
         per_sm < 1) {
         (void)cudaGetLastError();
         return 1;
@@ -382,10 +439,11 @@ struct GemvShape {
     double occupied = 0.0;
 };
 
-template <int ROWS, int SPLIT>
+template <int ROWS, int SPLIT, bool QUANT = false>
 GemvShape gemv_shape(uint32_t n, int sm_count) {
     constexpr uint64_t kSlots = kGemvWarps / SPLIT;
-    const uint64_t capacity = static_cast<uint64_t>(sm_count) * static_cast<uint64_t>(resident_ctas<ROWS, SPLIT>());
+    const uint64_t capacity =
+        static_cast<uint64_t>(sm_count) * static_cast<uint64_t>(resident_ctas<ROWS, SPLIT, QUANT>());
     const uint64_t rounds = (n + capacity * kSlots - 1) / (capacity * kSlots);
     GemvShape shape;
     shape.grid = static_cast<uint32_t>((n + kSlots * rounds - 1) / (kSlots * rounds));
@@ -398,11 +456,11 @@ GemvShape gemv_shape(uint32_t n, int sm_count) {
 // least four 32-chunk steps of K; else the split that occupies the most. Wide matrices take
 // one warp per column; narrow ones (a column shard, or the down projection's few long
 // columns) spread each column over 2, 4 or 8 warps.
-template <int ROWS>
+template <int ROWS, bool QUANT = false>
 cudaError_t launch_rows(const GemvParams &p, int sm_count, cudaStream_t stream) {
     const uint32_t steps = (p.k / 16 + 31) / 32;
-    const GemvShape shapes[4] = {gemv_shape<ROWS, 1>(p.n, sm_count), gemv_shape<ROWS, 2>(p.n, sm_count),
-                                 gemv_shape<ROWS, 4>(p.n, sm_count), gemv_shape<ROWS, 8>(p.n, sm_count)};
+    const GemvShape shapes[4] = {gemv_shape<ROWS, 1, QUANT>(p.n, sm_count), gemv_shape<ROWS, 2, QUANT>(p.n, sm_count),
+                                 gemv_shape<ROWS, 4, QUANT>(p.n, sm_count), gemv_shape<ROWS, 8, QUANT>(p.n, sm_count)};
     int choice = 0;
     for (int i = 0; i < 4; ++i) {
         if (i > 0 && steps < 4u * (1u << i)) break;
@@ -413,11 +471,12 @@ cudaError_t launch_rows(const GemvParams &p, int sm_count, cudaStream_t stream) 
         if (shapes[i].occupied > shapes[choice].occupied) choice = i;
     }
     const uint32_t grid = shapes[choice].grid;
+    const size_t smem = QUANT ? p.k : 0;
     switch (choice) {
-        case 0: return launch_dependent(w8a8_gemv_kernel<ROWS, 1>, grid, p, stream);
-        case 1: return launch_dependent(w8a8_gemv_kernel<ROWS, 2>, grid, p, stream);
-        case 2: return launch_dependent(w8a8_gemv_kernel<ROWS, 4>, grid, p, stream);
-        default: return launch_dependent(w8a8_gemv_kernel<ROWS, 8>, grid, p, stream);
+        case 0: return launch_dependent(w8a8_gemv_kernel<ROWS, 1, QUANT>, grid, p, stream, smem);
+        case 1: return launch_dependent(w8a8_gemv_kernel<ROWS, 2, QUANT>, grid, p, stream, smem);
+        case 2: return launch_dependent(w8a8_gemv_kernel<ROWS, 4, QUANT>, grid, p, stream, smem);
+        default: return launch_dependent(w8a8_gemv_kernel<ROWS, 8, QUANT>, grid, p, stream, smem);
     }
 }
 
@@ -447,17 +506,17 @@ cudaError_t launch_mma(const GemvParams &p, int sm_count, cudaStream_t stream) {
     return launch_dependent(w8a8_gemv_mma_kernel, grid, p, stream);
 }
 
-template <int ROWS>
+template <int ROWS, bool QUANT = false>
 cudaError_t preload_rows() {
     cudaFuncAttributes attributes;
-    cudaError_t error = cudaFuncGetAttributes(&attributes, w8a8_gemv_kernel<ROWS, 1>);
-    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, w8a8_gemv_kernel<ROWS, 2>);
-    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, w8a8_gemv_kernel<ROWS, 4>);
-    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, w8a8_gemv_kernel<ROWS, 8>);
-    (void)resident_ctas<ROWS, 1>();
-    (void)resident_ctas<ROWS, 2>();
-    (void)resident_ctas<ROWS, 4>();
-    (void)resident_ctas<ROWS, 8>();
+    cudaError_t error = cudaFuncGetAttributes(&attributes, w8a8_gemv_kernel<ROWS, 1, QUANT>);
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, w8a8_gemv_kernel<ROWS, 2, QUANT>);
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, w8a8_gemv_kernel<ROWS, 4, QUANT>);
+    if (error == cudaSuccess) error = cudaFuncGetAttributes(&attributes, w8a8_gemv_kernel<ROWS, 8, QUANT>);
+    (void)resident_ctas<ROWS, 1, QUANT>();
+    (void)resident_ctas<ROWS, 2, QUANT>();
+    (void)resident_ctas<ROWS, 4, QUANT>();
+    (void)resident_ctas<ROWS, 8, QUANT>();
     return error;
 }
 
@@ -468,6 +527,7 @@ cudaError_t preload_w8a8_gemv() {
     cudaError_t error = cudaFuncGetAttributes(&attributes, w8a8_gemv_mma_kernel);
     (void)mma_resident_ctas();
     if (error == cudaSuccess) error = preload_rows<1>();
+    if (error == cudaSuccess) error = preload_rows<1, true>();
     return error;
 }
 
@@ -500,6 +560,37 @@ cudaError_t launch_w8a8_gemv(const int8_t *a, size_t a_stride, const int8_t *w, 
     // 28672 -> 8192 at M = 8 140.3 against 52.2.
     if (m == 1) return launch_rows<1>(p, sm_count, stream);
     return launch_mma(p, sm_count, stream);
+}
+
+cudaError_t launch_w8a8_gemv_quantize(const float *x, uint32_t cols, int8_t *q_out, float *scale_out, const int8_t *w,
+                                      size_t w_stride, uint32_t n, uint32_t k, const GemmEpilogue &epilogue,
+                                      int sm_count, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    if (x == nullptr || q_out == nullptr || scale_out == nullptr || cols == 0 || cols % 4 != 0 || k < cols ||
+        k % 16 != 0 || k > kFusedQuantMaxK || w_stride % 16 != 0 || (reinterpret_cast<uintptr_t>(x) & 15u) != 0 ||
+        (reinterpret_cast<uintptr_t>(q_out) & 3u) != 0 || (reinterpret_cast<uintptr_t>(w) & 15u) != 0 ||
+        epilogue.mode == EpilogueMode::kStoreS32) {
+        return cudaErrorNotSupported;
+    }
+    GemvParams p{};
+    p.a = q_out;
+    p.a_stride = k;
+    p.w = w;
+    p.w_stride = w_stride;
+    p.m = 1;
+    p.n = n;
+    p.k = k;
+    p.mode = static_cast<int>(epilogue.mode);
+    p.row_scales = scale_out;
+    p.col_scales = epilogue.col_scales;
+    p.bias = epilogue.bias;
+    p.out = epilogue.out;
+    p.out_stride = epilogue.out_stride;
+    p.x = x;
+    p.x_cols = cols;
+    p.q_out = q_out;
+    p.scale_out = scale_out;
+    return launch_rows<1, true>(p, sm_count, stream);
 }
 
 cudaError_t launch_w8a8_splitk_reduce(const int32_t *workspace, uint32_t splits, uint32_t m, uint32_t n,

@@ -378,3 +378,37 @@ def test_merged_linear_sections_equal_their_own_linears(cuda_device: Device, wit
         merged.close()
         for plan in separate:
             plan.close()
+
+
+@pytest.mark.parametrize("k", (16, 1036, 2048, 8192, 8196, 1038), ids=lambda k: f"k{k}")
+def test_single_row_plan_call_quantizes_inside_the_gemv(cuda_device: Device, k: int) -> None:
+    """One fp32 row through the plan: up to 8192 columns (a multiple of 4) the GEMV quantizes the
+    row itself, otherwise the row quantizer runs first. Either way the output equals the oracle
+    bit for bit, and the plan scratch holds the oracle's int8 row, zero padded over stale bytes,
+    and its scale (execute_prepared reads them back). Rows of normal values, with a huge value,
+    and all zeros (the 1/127 scale floor)."""
+    import torch
+
+    rng = np.random.default_rng(k)
+    n = 700
+    values, scales = oracle.quantize_per_output_channel_int8((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    bias = rng.standard_normal(n).astype(np.float32)
+    with PreparedW8A8Linear(cuda_device, QuantizedMatrixInt8(values, scales), max_batch=4, bias=bias) as plan:
+        quantized, row_scales = plan.scratch()
+        for case in range(3):
+            row = rng.standard_normal((1, k)).astype(np.float32)
+            if case == 1:
+                row[0, k // 3] = np.float32(3.0e38)
+                row[0, 0] = np.float32(0.0)
+            if case == 2:
+                row[:] = np.float32(0.0)
+            quantized.fill_(0x5A)
+            row_scales.fill_(-1.0)
+            out = plan.forward(torch.from_numpy(row).cuda())
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(out.cpu().numpy(), oracle.w8a8_linear(row, values, scales, bias))
+            q_expected, s_expected = oracle.quantize_rows_int8(row)
+            q_row = quantized[0].cpu().numpy()
+            np.testing.assert_array_equal(q_row[:k], q_expected[0])
+            assert not q_row[k:].any()
+            assert row_scales[0].item() == float(s_expected[0])

@@ -402,6 +402,8 @@ def run_ours(args: argparse.Namespace) -> None:
         del weight, quantized, q4_blocks
     exchange = "none"
     copy_streams: list[Any] = []
+    if args.exchange == "auto":
+        args.exchange = "copy" if world == 2 else "fused"
     if world > 1 and args.exchange == "nccl":
         exchange = "NCCL all-gather after the GEMM (selected with --exchange nccl)"
         barrier_flag = None
@@ -1327,9 +1329,11 @@ def main() -> None:
                         help=f"comma-separated subset of {','.join(OBJECTS)} to time at N = 1 (default all; empty string: none)")
     parser.add_argument(
         "--exchange",
-        choices=("fused", "copy", "nccl"),
-        default="fused",
-        help="N > 1: fused GEMM + all-gather over NVLink (default), copy-engine pushes after each GEMM, or NCCL all-gather after the GEMM",
+        choices=("auto", "fused", "copy", "nccl"),
+        default="auto",
+        help="N > 1: fused GEMM + all-gather over NVLink, copy-engine pushes after each GEMM, or NCCL all-gather after "
+        "the GEMM; auto (default) takes the copy engines at 2 GPUs and the fused exchange from 3 on (measured on B200, "
+        "70B FFN: 4507 against 4201 TOPS at 2 GPUs, 2423 against 3614 at 4, 1578 against 3266 at 8)",
     )
     args = parser.parse_args()
     if args.warmup < 3:

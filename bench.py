@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Headline benchmark: W8A8 GEMM TOPS (and Q4_0 GEMV GB/s) at 1/2/4/8 B200s.
 
-Headline workload (the configuration the metric is quoted on
+Headline workload (benchmark configuration configs[4], the one the metric is quoted on
 "at 1/2/4/8 GPUs"): the Llama-2-70B FFN at prefill, M = 4096 tokens, W8A8 dynamic
 linear for gate (8192->28672), up (8192->28672) and down (28672->8192). Weights are
 random-init ~N(0, 0.02), activations ~N(0, 1), drawn on the GPU from a fixed seed
@@ -11,10 +11,13 @@ ranks; N = 1 runs the identical inputs unsplit.
 One step = for each projection: quantize the fp32 rows (int8 row-quantizer kernel) into
 the plan's scratch, then the tcgen05 int8 GEMM with the fused dequant epilogue on the
 rank's column shard, and (N > 1) the exchange that leaves the full [M, N] fp32 output on
-every rank: the GEMM epilogue stores each tile into every rank's output buffer (mapped
-with CUDA IPC) over NVLink as it finishes, then one NCCL all-reduce of one element per
-step orders all ranks' stores (the fused GEMM + all-gather). If the peer mapping is
-refused, the step falls back to an NCCL all-gather after each GEMM and the line says so.
+every rank. From 3 GPUs on, the GEMM epilogue stores each tile into every rank's output
+buffer (mapped with CUDA IPC) over NVLink as it finishes (the fused GEMM + all-gather); at
+2 GPUs the GEMM writes the local buffer and the copy engines push each projection's column
+block to the peer while the next projection computes (``--exchange`` overrides the
+choice). One NCCL all-reduce of one element per step then orders all ranks' writes. If the
+peer mapping is refused, the step falls back to an NCCL all-gather after each GEMM and the
+line says so.
 At N = 1 CUDA events recorded between the quantizer and the GEMM launches inside the
 timed steps give the GEMM's own time, which the roofline uses.
 

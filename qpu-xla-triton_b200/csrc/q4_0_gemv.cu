@@ -555,6 +555,16 @@ cudaError_t launch_rows(const DirectParams &p, int sm_count, cudaStream_t stream
     // 34.8 -> 32.8 us (K = 8192) and 41.0 -> 34.8 us (K = 28672), four rows at K = 28672
     // 59.4 -> 51.2 us; four rows at K = 8192 and the single row gained nothing from it, and three
     // rows at K = 28672 lost (45.1 -> 49.2 us).
+    // A small matrix (a few MB, so one launch is mostly latency) whose reduction needs more than
+    // one four-block trip: six blocks per lane and column take each warp's whole group in one
+    // trip, loaded before the dependency wait. Measured on B200 (TinyLlama down 5632 -> 2048,
+    // 16 weight copies back to back, L2 flushed): 4.03 -> 3.13 us per launch at M = 1 and
+    // 6.08 -> 5.62 us at M = 4. Four columns per warp for the 64-block up projection measured
+    // the same at M = 1 and slower at M = 4 (5.04 against 4.80 us), so it is not used.
+    const uint64_t weight_bytes = static_cast<uint64_t>(p.count) * p.blocks * 18u;
+    if (weight_bytes <= (16u << 20) && p.blocks > 128 && p.blocks <= 192) {
+        return launch_direct<ROWS, 1, 2, 6, 2, F32>(p, sm_count, stream);
+    }
     if constexpr (ROWS == 1) {
         if (p.blocks >= 640) return launch_direct<ROWS, 4, 2, 7, 2, F32>(p, sm_count, stream);
         return launch_direct<ROWS, 1, 2, 4, 3, F32>(p, sm_count, stream);

@@ -565,10 +565,11 @@ cudaError_t launch_rows(const DirectParams &p, int sm_count, cudaStream_t stream
     if (weight_bytes <= (16u << 20) && p.blocks > 128 && p.blocks <= 192) {
         return launch_direct<ROWS, 1, 2, 6, 2, F32>(p, sm_count, stream);
     }
-    // Up to 32 MB and 512 blocks, one row: eight blocks per lane and column per trip (two trips
-    // instead of three for the 7B down projection's 344): 7B decode FFN at M = 1 25.6 -> 23.6 us.
-    // At M = 4 the same measured slower (39.9 against 38.0 us) and is not used.
-    if (ROWS == 1 && weight_bytes <= (32u << 20) && p.blocks > 192 && p.blocks <= 512) {
+    // One row over 193-512 blocks: eight blocks per lane and column per trip (two trips instead
+    // of three for the 7B down projection's 344, one instead of two for the 70B gate's 256):
+    // decode FFN at M = 1 25.6 -> 23.6 us on the 7B shapes, 74.8 -> 72.8 us on the 70B shapes.
+    // At M = 4 the same measured slower (7B: 39.9 against 38.0 us) and is not used.
+    if (ROWS == 1 && p.blocks > 192 && p.blocks <= 512) {
         return launch_direct<ROWS, 1, 2, 8, 2, F32>(p, sm_count, stream);
     }
     if constexpr (ROWS == 1) {

@@ -108,6 +108,15 @@ def profile_traffic(name: str, key: str | None = None) -> float | None:
     return None
 
 
+def resolve_exchange(choice: str, world: int) -> str:
+    """The N > 1 output exchange: ``auto`` takes the copy engines at 2 GPUs and the fused epilogue
+    stores from 3 GPUs on (measured on B200, 70B FFN: 4507 against 4201 TOPS at 2 GPUs, 2423
+    against 3614 at 4, 1578 against 3266 at 8); any other choice stands."""
+    if choice != "auto":
+        return choice
+    return "copy" if world == 2 else "fused"
+
+
 def roofline(*, kernel: str, seconds: float, ops: float, nbytes: float, int8_peak: float, hbm_peak: float,
              peak_note: str, traffic: float | None, traffic_launches: int = 1) -> dict[str, Any]:
     """Roofline of one timed launch sequence: the bound is whichever of ops / int8 peak and bytes
@@ -405,8 +414,7 @@ def run_ours(args: argparse.Namespace) -> None:
         del weight, quantized, q4_blocks
     exchange = "none"
     copy_streams: list[Any] = []
-    if args.exchange == "auto":
-        args.exchange = "copy" if world == 2 else "fused"
+    args.exchange = resolve_exchange(args.exchange, world)
     if world > 1 and args.exchange == "nccl":
         exchange = "NCCL all-gather after the GEMM (selected with --exchange nccl)"
         barrier_flag = None

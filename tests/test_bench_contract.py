@@ -41,3 +41,12 @@ def test_argument_rules() -> None:
         cwd=ROOT,
     )
     assert result.returncode != 0 and "--warmup must be >= 3" in (result.stderr + result.stdout)
+
+
+def test_exchange_follows_the_gpu_count() -> None:
+    assert bench.resolve_exchange("auto", 1) == "fused"
+    assert bench.resolve_exchange("auto", 2) == "copy"
+    assert bench.resolve_exchange("auto", 4) == "fused"
+    assert bench.resolve_exchange("auto", 8) == "fused"
+    assert bench.resolve_exchange("nccl", 2) == "nccl"
+    assert bench.resolve_exchange("fused", 2) == "fused"

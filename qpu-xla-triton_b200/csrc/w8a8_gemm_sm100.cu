@@ -130,22 +130,26 @@ struct GemmParams {
     uint32_t splits;
     uint32_t kb_per_split;
     uint32_t split_rows;
+    uint32_t group_rows;  // row blocks per tile group (see tile_coords)
 };
 
 using namespace sm100;
 
-// Tile order: groups of kTileGroupRows row blocks, and within a group the row block fastest. The
-// CTAs (pairs) resident at once then cover about 8 row blocks x 9 column blocks, so a group's A
-// rows stay in L2 while its columns stream past, where a row-fastest order over all row blocks
-// re-read the whole A from DRAM on every wave once A outgrew L2 (the 70B down projection's 117 MB
-// A was read 7 times).
+// Tile order: groups of group_rows row blocks, and within a group the row block fastest. The
+// CTAs (pairs) resident at once then cover a few column blocks of every row block of the group,
+// so the group's A rows stay in L2 while its columns stream past, and each W tile is read from
+// DRAM once per group. A row-fastest order over all row blocks re-read the whole A from DRAM on
+// every wave once A outgrew L2 (the 70B down projection's 117 MB A was read 7 times). The host
+// takes as many row blocks per group as keep the group's A within ~40 MB, at least 8: every row
+// block of the 70B gate and up (16 blocks of 2 MB, so W is read once), 8 for the down projection.
 constexpr uint32_t kTileGroupRows = 8;
+constexpr uint64_t kTileGroupBytes = 40ull << 20;
 __device__ __forceinline__ void tile_coords(uint32_t tile, uint32_t m_blocks, uint32_t n_blocks, uint32_t &m_block,
-                                            uint32_t &n_block) {
-    const uint32_t group_tiles = kTileGroupRows * n_blocks;
+                                            uint32_t &n_block, uint32_t group_rows) {
+    const uint32_t group_tiles = group_rows * n_blocks;
     const uint32_t group = tile / group_tiles;
-    const uint32_t first = group * kTileGroupRows;
-    const uint32_t rows = min(kTileGroupRows, m_blocks - first);
+    const uint32_t first = group * group_rows;
+    const uint32_t rows = min(group_rows, m_blocks - first);
     const uint32_t local = tile - group * group_tiles;
     m_block = first + local % rows;
     n_block = local / rows;
@@ -443,7 +447,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 uint32_t tile, kb_begin, kb_end;
                 unit_range(unit, tile, kb_begin, kb_end);
                 uint32_t m_block, n_block;
-                tile_coords(tile, params.m_blocks, params.n_blocks, m_block, n_block);
+                tile_coords(tile, params.m_blocks, params.n_blocks, m_block, n_block, params.group_rows);
                 const int m0 = static_cast<int>(m_block * kTileRows + rank * BM);
                 const int n0 = static_cast<int>(n_block * BN);
                 for (uint32_t kb = kb_begin; kb < kb_end; ++kb) {
@@ -604,7 +608,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const uint32_t acc = local_tile & 1u;
             const uint32_t acc_phase = (local_tile >> 1) & 1u;
             uint32_t m_block, n_block;
-            tile_coords(tile, params.m_blocks, params.n_blocks, m_block, n_block);
+            tile_coords(tile, params.m_blocks, params.n_blocks, m_block, n_block, params.group_rows);
             const uint32_t n_base = n_block * BN;
             bool ok = true;
             if (lane == 0) ok = wait_bounded(smem_u32(&control->tmem_full[acc]), acc_phase, control, params.error_word);
@@ -914,6 +918,13 @@ cudaError_t launch_w8a8_gemm_sm100_mode(const CUtensorMap *map_a, const CUtensor
     params.col_stride = epilogue.col_stride;
     params.error_word = error_word;
     params.splits = 1;
+    {
+        const uint64_t block_bytes = static_cast<uint64_t>(pair ? 2 * BM : BM) * k;
+        uint64_t group = block_bytes != 0 ? kTileGroupBytes / block_bytes : kTileGroupRows;
+        if (group < kTileGroupRows) group = kTileGroupRows;
+        if (group > params.m_blocks) group = params.m_blocks;
+        params.group_rows = group != 0 ? static_cast<uint32_t>(group) : 1u;
+    }
     params.kb_per_split = params.num_kb;
     params.split_rows = 0;
     const uint32_t tiles = params.m_blocks * params.n_blocks;
@@ -960,6 +971,7 @@ cudaError_t launch_w8a8_gemm_sm100_splitk(const CUtensorMap *map_a, const CUtens
     params.kb_per_split = (params.num_kb + splits - 1) / splits;
     params.splits = (params.num_kb + params.kb_per_split - 1) / params.kb_per_split;
     params.split_rows = params.m_blocks * BM;
+    params.group_rows = kTileGroupRows;
     CUtensorMap map_out;
     std::memset(&map_out, 0, sizeof(map_out));
     params.tma_store = encode_tensor_map_2d_b32(&map_out, workspace, n,

@@ -569,10 +569,8 @@ cudaError_t launch_rows(const DirectParams &p, int sm_count, cudaStream_t stream
     // of three for the 7B down projection's 344, one instead of two for the 70B gate's 256):
     // decode FFN at M = 1 25.6 -> 23.6 us on the 7B shapes, 74.8 -> 72.8 us on the 70B shapes.
     // At M = 4 the same measured slower (7B: 39.9 against 38.0 us) and is not used.
-    if (ROWS == 1 && p.blocks > 192 && p.blocks <= 512) {
-        return launch_direct<ROWS, 1, 2, 8, 2, F32>(p, sm_count, stream);
-    }
     if constexpr (ROWS == 1) {
+        if (p.blocks > 192 && p.blocks <= 512) return launch_direct<ROWS, 1, 2, 8, 2, F32>(p, sm_count, stream);
         if (p.blocks >= 640) return launch_direct<ROWS, 4, 2, 7, 2, F32>(p, sm_count, stream);
         return launch_direct<ROWS, 1, 2, 4, 3, F32>(p, sm_count, stream);
     } else if constexpr (ROWS == 2) {

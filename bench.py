@@ -712,6 +712,7 @@ def run_ours(args: argparse.Namespace) -> None:
             "gemm_timing": "CUDA events recorded between the row-quantizer and GEMM launches inside the timed steps (L2 flushed before each step)",
             "row_quantizer_ms_per_projection": [round(x, 4) for x in quant_ms],
             "row_quantizer_gbs": [round((4.0 + 1.0) * TOKENS * p["k"] / (ms * 1e-3) / 1e9, 1) for p, ms in zip(projections, quant_ms)],
+            "row_quantizer_traffic": [profile_traffic("quantize_rows_int8_70b_ffn", f"k{p['k']}") for p in projections],
         },
         "q4_0_gemv": {
             "metric": "Q4_0 x Q8_0 GEMV GB/s (whole job), one decode FFN step (gate, up, down) per bracket, at M = 1 and 4",

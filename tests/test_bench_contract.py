@@ -50,3 +50,9 @@ def test_exchange_follows_the_gpu_count() -> None:
     assert bench.resolve_exchange("auto", 8) == "fused"
     assert bench.resolve_exchange("nccl", 2) == "nccl"
     assert bench.resolve_exchange("fused", 2) == "fused"
+
+
+def test_row_quantizer_traffic_comes_from_the_committed_profile() -> None:
+    for k in (8192, 28672):
+        traffic = bench.profile_traffic("quantize_rows_int8_70b_ffn", f"k{k}")
+        assert traffic is not None and traffic > 4096 * k * 4 * 0.9  # at least the fp32 rows read
